@@ -1,0 +1,120 @@
+/*
+ * pto_fuser_gdn.h — C ABI of the B200 (sm_100a) chunked Gated DeltaNet kernels.
+ *
+ * This library replaces the Ascend kernel .so files that pto-fuser loads with
+ * ctypes (src/pto_fuser/fused.py:58-77, registry.py:96-104). It keeps their
+ * setup / exec / teardown discipline (fused.py:93-115): `*_setup` allocates the
+ * library-owned workspace once, `*_exec` only launches on the caller's stream
+ * (no host synchronisation, so calls can be captured into a CUDA graph), and
+ * `*_teardown` frees the workspace.
+ *
+ * Differences from the reference ABI, by design:
+ *   - shapes are runtime parameters (the reference rebuilds one .so per shape
+ *     through -D defines, fused.py:66-76);
+ *   - every exec returns a status code (the reference's exec functions return
+ *     void and report nothing);
+ *   - chunk batches are keyed on M = B*H*nc (the reference's native launchers
+ *     drop B, fused.py:256,264).
+ *
+ * All tensor arguments are device pointers; the caller owns inputs and outputs.
+ * Pointers must be 16-byte aligned and rows contiguous in the innermost dim.
+ */
+#ifndef PTO_FUSER_GDN_H
+#define PTO_FUSER_GDN_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PTOF_API __attribute__((visibility("default")))
+#else
+#define PTOF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes returned by every exec / check call ---------------------- */
+enum {
+  PTOF_OK = 0,
+  PTOF_EINVAL = 1,       /* bad shape / null pointer / bad dtype code           */
+  PTOF_EALIGN = 2,       /* pointer not 16-byte aligned                          */
+  PTOF_ECUDA = 3,        /* a CUDA runtime / driver call failed                  */
+  PTOF_EUNSUPPORTED = 4, /* valid request this build does not implement          */
+  PTOF_ETIMEOUT = 5      /* a device-side bounded wait gave up (see check_status) */
+};
+
+/* ---- element type codes ---------------------------------------------------- */
+enum { PTOF_F32 = 0, PTOF_F16 = 1, PTOF_BF16 = 2 };
+
+/* ---- memory layouts of q/k/v/o ([.., D] innermost) and of beta/g ------------ */
+enum {
+  PTOF_LAYOUT_BHTD = 0, /* q [B,H,T,D], beta/g [B,H,T]  (== reference [B,H,nc,C,D]) */
+  PTOF_LAYOUT_BTHD = 1  /* q [B,T,H,D], beta/g [B,T,H]  (reference "mega" layout)   */
+};
+
+/* ---- gate modes -------------------------------------------------------------- */
+enum {
+  PTOF_GATE_RAW = 0,    /* g is the per-token log decay; kernels do the chunk-local cumsum */
+  PTOF_GATE_CUMSUM = 1, /* g already holds the chunk-local inclusive cumsum (g_native)     */
+  PTOF_GATE_NONE = 2    /* ungated DeltaNet: g ignored (may be NULL)                        */
+};
+
+/* Shape / dtype description of one chunked GDN forward. */
+typedef struct ptof_gdn_params {
+  int32_t B, H, T;    /* batch, heads, tokens (T a multiple of C)          */
+  int32_t C;          /* chunk length; 64                                 */
+  int32_t Dk, Dv;     /* key / value head dims                            */
+  int32_t in_dtype;   /* q, k, v element type (PTOF_F32/F16/BF16)         */
+  int32_t beta_dtype; /* beta element type                                */
+  int32_t out_dtype;  /* o element type                                   */
+  int32_t gate_mode;  /* PTOF_GATE_*; g is always fp32                    */
+  int32_t layout;     /* PTOF_LAYOUT_*                                    */
+  float scale;        /* output scale (reference: D^-0.5)                 */
+} ptof_gdn_params;
+
+/* ---------------------------------------------------------------------------
+ * Full fused chunk forward:
+ *   cumsum -> A = tril(beta*KK^T*exp(dg), -1) -> T = (I+A)^-1 -> W, U ->
+ *   state scan -> o = scale*(exp(g)*(Q S) + tril(QK^T*exp(min(dg,0))) V_new)
+ * Replaces the whole lowered chain kkt_gated_native_v2 -> tri_inv_rec_unroll ->
+ * W/U einsums -> chunk_h_scan -> qkv_flash_native_v2 (fused.py:446-569,
+ * registry.py:96-140) and matches gdn_reference (examples/attention/_gdn_full.py:57-97)
+ * plus the final state and an optional initial state.
+ *   q,k: [.., Dk] in_dtype; v: [.., Dv] in_dtype; beta: in beta_dtype; g: fp32;
+ *   S0: [B,H,Dk,Dv] fp32 or NULL (zero state); o: [.., Dv] out_dtype;
+ *   S_final: [B,H,Dk,Dv] fp32 or NULL.
+ * fp32 inputs run the fp32 SIMT kernel (reference tolerance 1e-4); fp16/bf16
+ * inputs run the tcgen05 kernel (fp32 accumulate, tolerance 1e-2).
+ */
+PTOF_API void* ptof_gdn_fwd_setup(const ptof_gdn_params* p);
+PTOF_API int ptof_gdn_fwd_exec(void* ws, const void* q, const void* k, const void* v, const void* beta,
+                      const float* g, const float* S0, void* o, float* S_final, void* stream);
+PTOF_API void ptof_gdn_fwd_teardown(void* ws);
+
+/* Reads (and clears) the workspace's device status word after synchronising
+ * `stream`: PTOF_OK, or PTOF_ETIMEOUT when a bounded device wait gave up. */
+PTOF_API int ptof_check_status(void* ws, void* stream);
+
+/* Human-readable text of the last host-side error on this thread. */
+PTOF_API const char* ptof_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Self-tests of the sm_100a building blocks (no counterpart in the reference).
+ * selftest_umma: D[M,N] = (+-)A[M,K] * B[N,K]^T through one UMMA, A/B fp32 device
+ *   arrays rounded to bf16. mode bit0: A MN-major in smem; bit1: B MN-major;
+ *   bit2: A from TMEM; bit3: negate A. M in {64,128}, N%16==0 <= 256, K%32==0 <= 128.
+ * selftest_tma: TMA SWIZZLE_128B load of the [64 x 64] bf16 box at column x0,
+ *   row y0 of a row-major [rows, cols] bf16 matrix, de-swizzled into out[64*64].
+ * `status` is a device int that receives a nonzero code if a bounded wait gave up.
+ */
+PTOF_API int ptof_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,
+                                int mode, int* status, void* stream);
+PTOF_API int ptof_selftest_tma(const void* src, int rows, int cols, int x0, int y0, void* out,
+                               int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PTO_FUSER_GDN_H */

@@ -1,0 +1,219 @@
+"""CPU oracle for the chunked Gated DeltaNet forward — TEST INFRASTRUCTURE ONLY.
+
+This module is the checker, never the product: only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py`` (its CPU-baseline / reference arm) may
+import it. The product path (``pto_fuser``) never calls into it.
+
+It restates, in numpy, the reference's own fp32 torch algorithms (the reference
+package is vloncar/pto-fuser; paths below are relative to that project):
+
+  * ``gdn_forward``        examples/attention/_gdn_full.py:57-97 (``gdn_reference``),
+                           plus the final state (the ``final`` convention of
+                           src/pto_fuser/forwards/fused_stages.py:61) and an optional
+                           initial state S0 (the reference hard-codes S=0 at :67);
+  * ``deltanet_forward``   src/pto_fuser/forwards/deltanet.py:114-143;
+  * ``kkt_gated``          src/pto_fuser/forwards/fused_stages.py:140-156;
+  * ``chunk_h_scan``       src/pto_fuser/forwards/fused_stages.py:46-62;
+  * ``tri_inv``            src/pto_fuser/registry.py:107-127 semantics, (I+A)^-1 for a
+                           strictly-lower A (solve_triangular in _gdn_full.py:76-78);
+  * ``qkv_flash``          src/pto_fuser/fused.py:368-387 semantics (chunk_o intra term).
+
+Parity is pinned: tests/test_oracle.py checks every function here against golden
+vectors produced by running the reference's own torch code
+(tests/golden/make_golden.py, committed with the vectors).
+
+Arithmetic is float64 by default (``dtype=np.float32`` reproduces fp32 rounding).
+Chunk-parallel stages are vectorised over all chunks; the state scan loops over
+chunks, vectorised over the (batch, head) pairs.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+C_DEFAULT = 64
+
+
+def _f(x, dtype):
+    return np.asarray(x, dtype=dtype)
+
+
+def chunk_cumsum(g, C=C_DEFAULT, dtype=np.float64):
+    """Chunk-local inclusive prefix sum of the per-token log decay
+    (_gdn_full.py:63 ``g_in.cumsum(dim=3)`` on the [B,H,nc,C] view)."""
+    g = _f(g, dtype)
+    B, H, T = g.shape
+    return g.reshape(B, H, T // C, C).cumsum(axis=-1)
+
+
+def tri_inv(A, dtype=np.float64):
+    """(I + A)^-1 for strictly-lower A [..., C, C] by row-wise forward substitution
+    (unit lower-triangular solve, _gdn_full.py:76-78; registry.py:107-127)."""
+    A = _f(A, dtype)
+    C = A.shape[-1]
+    Tm = np.zeros_like(A)
+    eye = np.eye(C, dtype=dtype)
+    Tm[..., 0, :] = eye[0]
+    for i in range(1, C):
+        # row i of T: e_i - sum_{k<i} A[i,k] T[k,:]
+        Tm[..., i, :] = eye[i] - np.einsum("...k,...kc->...c", A[..., i, :i], Tm[..., :i, :])
+    return Tm
+
+
+def _kkt_A(k, beta, gs, dtype):
+    """A = tril((k k^T) * safe_exp(g_i - g_j) * beta_i, -1) per chunk (_gdn_full.py:73-75)."""
+    C = k.shape[-2]
+    kk = np.einsum("...id,...jd->...ij", k, k)
+    x = gs[..., :, None] - gs[..., None, :]
+    coef = np.where(x <= 0, np.exp(np.minimum(x, 0)), 0.0).astype(dtype)
+    A = kk * coef * beta[..., :, None]
+    return np.tril(A, -1)
+
+
+def kkt_inv(k, beta, g, C=C_DEFAULT, gate="raw", dtype=np.float64):
+    """The kkt + tri-inv stage alone: per chunk
+    A = tril(beta KK^T exp(g_i - g_j), -1) and T = (I + A)^-1.
+
+    k [B,H,T,D], beta [B,H,T], g [B,H,T] -> (A, T) each [B,H,nc,C,C]."""
+    k = _f(k, dtype)
+    B, H, T, D = k.shape
+    nc = T // C
+    kc = k.reshape(B, H, nc, C, D)
+    bc = _f(beta, dtype).reshape(B, H, nc, C)
+    gs = _gate(g, B, H, T, C, gate, dtype)
+    A = _kkt_A(kc, bc, gs, dtype)
+    return A, tri_inv(A, dtype)
+
+
+def _gate(g, B, H, T, C, gate, dtype):
+    if gate == "none" or g is None:
+        return np.zeros((B, H, T // C, C), dtype=dtype)
+    if gate == "cumsum":
+        return _f(g, dtype).reshape(B, H, T // C, C)
+    return chunk_cumsum(g, C, dtype)
+
+
+def gdn_forward(q, k, v, beta, g, scale, S0=None, C=C_DEFAULT, gate="raw",
+                dtype=np.float64):
+    """Full GDN chunk forward, restating gdn_reference (_gdn_full.py:57-97).
+
+    q,k [B,H,T,Dk], v [B,H,T,Dv], beta [B,H,T], g [B,H,T] (per-token log decay for
+    gate="raw", the chunk-local cumsum for gate="cumsum", ignored for gate="none"),
+    S0 [B,H,Dk,Dv] or None. Returns (o [B,H,T,Dv], S_final [B,H,Dk,Dv])."""
+    q, k, v = _f(q, dtype), _f(k, dtype), _f(v, dtype)
+    B, H, T, Dk = q.shape
+    Dv = v.shape[-1]
+    nc = T // C
+    qc = q.reshape(B, H, nc, C, Dk)
+    kc = k.reshape(B, H, nc, C, Dk)
+    vc = v.reshape(B, H, nc, C, Dv)
+    bc = _f(beta, dtype).reshape(B, H, nc, C)
+    gs = _gate(g, B, H, T, C, gate, dtype)
+
+    # chunk-independent stages, all chunks at once (_gdn_full.py:72-82)
+    A = _kkt_A(kc, bc, gs, dtype)
+    Tm = tri_inv(A, dtype)
+    eg = np.exp(gs)
+    W = np.einsum("...ij,...jd->...id", Tm, kc * (bc * eg)[..., None])
+    U = np.einsum("...ij,...jd->...id", Tm, vc * bc[..., None])
+
+    # intra-chunk gated causal scores (_gdn_full.py:88-92)
+    x = gs[..., :, None] - gs[..., None, :]
+    causal = np.tril(np.ones((C, C), dtype=dtype))
+    Aqk = np.einsum("...id,...jd->...ij", qc, kc) * np.exp(np.minimum(x, 0)) * causal
+
+    # the state scan over chunks (_gdn_full.py:83-87), then chunk_o (:88-94)
+    S = np.zeros((B, H, Dk, Dv), dtype=dtype) if S0 is None else _f(S0, dtype).copy()
+    o = np.empty((B, H, nc, C, Dv), dtype=dtype)
+    for c in range(nc):
+        gcc = gs[:, :, c]                               # [B,H,C]
+        gl = gcc[..., -1]                               # [B,H]
+        inter = np.einsum("bhid,bhde->bhie", qc[:, :, c], S) * np.exp(gcc)[..., None]
+        vn = U[:, :, c] - np.einsum("bhid,bhde->bhie", W[:, :, c], S)
+        o[:, :, c] = inter + np.einsum("bhij,bhje->bhie", Aqk[:, :, c], vn)
+        S = (np.exp(gl)[..., None, None] * S
+             + np.einsum("bhid,bhie->bhde", kc[:, :, c],
+                         vn * np.exp(gl[..., None] - gcc)[..., None]))
+    return (o * scale).reshape(B, H, T, Dv), S
+
+
+def deltanet_forward(q, k, v, beta, scale, C=C_DEFAULT, dtype=np.float64):
+    """Ungated DeltaNet forward, restating deltanet_reference
+    (src/pto_fuser/forwards/deltanet.py:114-143). Returns a dict with A, T, W, U,
+    v_new, h_state ([B,H,nc,...]) and o [B,H,nc,C,D], as the reference does."""
+    q, k, v = _f(q, dtype), _f(k, dtype), _f(v, dtype)
+    B, H, T, D = q.shape
+    Dv = v.shape[-1]
+    nc = T // C
+    qc, kc = q.reshape(B, H, nc, C, D), k.reshape(B, H, nc, C, D)
+    vc = v.reshape(B, H, nc, C, Dv)
+    bc = _f(beta, dtype).reshape(B, H, nc, C)
+    kb, vb = kc * bc[..., None], vc * bc[..., None]
+    A = np.tril(np.einsum("...id,...jd->...ij", kb, kc), -1)
+    Tm = tri_inv(A, dtype)
+    W = np.einsum("...ij,...jd->...id", Tm, kb)
+    U = np.einsum("...ij,...jd->...id", Tm, vb)
+    h = np.zeros((B, H, nc, D, Dv), dtype=dtype)
+    vn = np.zeros((B, H, nc, C, Dv), dtype=dtype)
+    S = np.zeros((B, H, D, Dv), dtype=dtype)
+    for c in range(nc):
+        h[:, :, c] = S
+        vn[:, :, c] = U[:, :, c] - np.einsum("bhid,bhde->bhie", W[:, :, c], S)
+        S = S + np.einsum("bhid,bhie->bhde", kc[:, :, c], vn[:, :, c])
+    o_inter = np.einsum("...id,...de->...ie", qc, h)
+    Aqk = np.tril(np.einsum("...id,...jd->...ij", qc, kc))
+    o = (o_inter + np.einsum("...ij,...je->...ie", Aqk, vn)) * scale
+    return dict(A=A, T=Tm, W=W, U=U, v_new=vn, h_state=h, o=o, S_final=S)
+
+
+def chunk_h_scan(w, u, k, decay, dtype=np.float64):
+    """Simplified resident-state recurrence, restating scan_reference
+    (src/pto_fuser/forwards/fused_stages.py:46-62): token-major operands
+    w,u,k [B,nc,C,H,D], decay [B,H,nc] -> h_out [B,nc,H,D,D], final [B,H,D,D]."""
+    w, u, k, decay = _f(w, dtype), _f(u, dtype), _f(k, dtype), _f(decay, dtype)
+    B, nc, C, H, D = w.shape
+    Dv = u.shape[-1]
+    h_out = np.zeros((B, nc, H, D, Dv), dtype=dtype)
+    S = np.zeros((B, H, D, Dv), dtype=dtype)
+    for c in range(nc):
+        h_out[:, c] = S
+        ws = np.einsum("bihd,bhde->bihe", w[:, c], S)
+        vcur = u[:, c] - ws
+        S = decay[:, :, c][..., None, None] * S + np.einsum("bihd,bihe->bhde", k[:, c], vcur)
+    return h_out, S
+
+
+def kkt_gated(a, b, g_sum, beta, causal=False, dtype=np.float64):
+    """Gated masked a@b^T per chunk, restating kkt_reference
+    (src/pto_fuser/forwards/fused_stages.py:140-156) for any chunk batch layout:
+    a, b [..., C, D], g_sum, beta [..., C];
+    L = a b^T * exp(min(g_i + log(beta_i) - g_j, 0)) * mask (strict-lower, or causal
+    incl. the diagonal when ``causal``)."""
+    a, b = _f(a, dtype), _f(b, dtype)
+    gs, bs = _f(g_sum, dtype), _f(beta, dtype)
+    C = a.shape[-2]
+    qk = np.einsum("...id,...jd->...ij", a, b)
+    with np.errstate(divide="ignore"):
+        gv = gs + np.log(bs)
+    coeff = np.exp(np.minimum(gv[..., :, None] - gs[..., None, :], 0.0))
+    mask = np.tril(np.ones((C, C), dtype=dtype), 0 if causal else -1)
+    return qk * coeff * mask
+
+
+def qkv_flash(q, k, v, g_sum, dtype=np.float64):
+    """chunk_o intra term o = tril(q k^T * exp(min(g_i - g_j, 0))) v per chunk
+    (the qkv_flash contract, src/pto_fuser/fused.py:368-387): q,k [...,C,D],
+    v [...,C,DV], g_sum [...,C] -> [...,C,DV]."""
+    q, k, v, gs = _f(q, dtype), _f(k, dtype), _f(v, dtype), _f(g_sum, dtype)
+    C = q.shape[-2]
+    s = np.einsum("...id,...jd->...ij", q, k)
+    s = s * np.exp(np.minimum(gs[..., :, None] - gs[..., None, :], 0.0))
+    s = s * np.tril(np.ones((C, C), dtype=dtype))
+    return np.einsum("...ij,...je->...ie", s, v)
+
+
+def rel_l2(got, ref) -> float:
+    """Relative Frobenius error ||got - ref|| / ||ref|| (gate.frob_rel,
+    src/pto_fuser/gate.py:25-27)."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))

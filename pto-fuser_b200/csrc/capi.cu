@@ -1,0 +1,215 @@
+// C ABI of the GDN kernel library: argument validation, library-owned
+// workspaces, TMA descriptor encoding and kernel selection. No function here
+// synchronises the caller's stream except ptof_check_status.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace ptof {
+
+// ---------------------------------------------------------------- errors ----
+static thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PTOF_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------ TMA descriptors ----
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(PTOF_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return fail(PTOF_EALIGN, "TMA base address not 16-byte aligned");
+  if (row_stride_bytes % 16 != 0)
+    return fail(PTOF_EALIGN, "TMA row stride %llu not a multiple of 16 bytes",
+                (unsigned long long)row_stride_bytes);
+  (void)elem_bytes;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PTOF_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PTOF_OK;
+}
+
+// ------------------------------------------------------------ workspace ----
+Workspace* ws_create(int kind, const ptof_gdn_params* p) {
+  Workspace* w = new Workspace();
+  w->kind = kind;
+  if (p) w->p = *p;
+  if (cudaGetDevice(&w->device) != cudaSuccess) {
+    fail(PTOF_ECUDA, "cudaGetDevice failed");
+    delete w;
+    return nullptr;
+  }
+  cudaError_t e = cudaMalloc(&w->d_status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(w->d_status, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    cuda_fail(e, "workspace allocation");
+    delete w;
+    return nullptr;
+  }
+  return w;
+}
+
+void ws_destroy(Workspace* w) {
+  if (!w) return;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != w->device) cudaSetDevice(w->device);
+  if (w->d_status) cudaFree(w->d_status);
+  if (w->d_scratch) cudaFree(w->d_scratch);
+  if (cur >= 0 && cur != w->device) cudaSetDevice(cur);
+  delete w;
+}
+
+static bool dtype_ok(int d) { return d == PTOF_F32 || d == PTOF_F16 || d == PTOF_BF16; }
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate_gdn(const ptof_gdn_params& p) {
+  if (p.B < 1 || p.H < 1 || p.T < 1) return fail(PTOF_EINVAL, "B, H, T must be >= 1");
+  if (p.C != kChunk) return fail(PTOF_EUNSUPPORTED, "chunk length C=%d (only 64)", p.C);
+  if (p.T % p.C != 0) return fail(PTOF_EINVAL, "T=%d is not a multiple of C=%d", p.T, p.C);
+  if (p.Dk < 1 || p.Dv < 1) return fail(PTOF_EINVAL, "Dk, Dv must be >= 1");
+  if (!dtype_ok(p.in_dtype) || !dtype_ok(p.beta_dtype) || !dtype_ok(p.out_dtype))
+    return fail(PTOF_EINVAL, "bad dtype code");
+  if (p.gate_mode < PTOF_GATE_RAW || p.gate_mode > PTOF_GATE_NONE)
+    return fail(PTOF_EINVAL, "bad gate_mode %d", p.gate_mode);
+  if (p.layout != PTOF_LAYOUT_BHTD && p.layout != PTOF_LAYOUT_BTHD)
+    return fail(PTOF_EINVAL, "bad layout %d", p.layout);
+  return PTOF_OK;
+}
+
+int check_ptrs(std::initializer_list<const void*> required,
+               std::initializer_list<const void*> optional) {
+  int i = 0;
+  for (const void* q : required) {
+    if (!q) return fail(PTOF_EINVAL, "required pointer #%d is NULL", i);
+    if (!aligned16(q)) return fail(PTOF_EALIGN, "pointer #%d not 16-byte aligned", i);
+    ++i;
+  }
+  for (const void* q : optional) {
+    if (q && !aligned16(q)) return fail(PTOF_EALIGN, "optional pointer not 16-byte aligned");
+  }
+  return PTOF_OK;
+}
+
+}  // namespace ptof
+
+using namespace ptof;
+
+extern "C" {
+
+const char* ptof_last_error(void) { return g_err; }
+
+// ------------------------------------------------------------ gdn forward ----
+void* ptof_gdn_fwd_setup(const ptof_gdn_params* p) {
+  if (!p) {
+    fail(PTOF_EINVAL, "null params");
+    return nullptr;
+  }
+  if (validate_gdn(*p) != PTOF_OK) return nullptr;
+  return ws_create(kWsGdnFwd, p);
+}
+
+int ptof_gdn_fwd_exec(void* wsv, const void* q, const void* k, const void* v, const void* beta,
+                      const float* g, const float* S0, void* o, float* S_final, void* stream) {
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w || w->kind != kWsGdnFwd) return fail(PTOF_EINVAL, "not a gdn_fwd workspace");
+  const ptof_gdn_params& p = w->p;
+  int rc = check_ptrs({q, k, v, beta, o}, {S0, S_final});
+  if (rc) return rc;
+  if (p.gate_mode != PTOF_GATE_NONE && !g) return fail(PTOF_EINVAL, "g is NULL for a gated forward");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (p.in_dtype == PTOF_F32 || !gdn_fwd_tc_supports(p)) {
+    if (!gdn_fwd_simt_supports(p))
+      return fail(PTOF_EUNSUPPORTED, "no kernel for Dk=%d Dv=%d", p.Dk, p.Dv);
+    e = launch_gdn_fwd_simt(p, q, k, v, beta, g, S0, o, S_final, st);
+    if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_simt launch");
+    return PTOF_OK;
+  }
+  return launch_gdn_fwd_tc(w, q, k, v, beta, g, S0, o, S_final, st);
+}
+
+void ptof_gdn_fwd_teardown(void* ws) { ws_destroy(static_cast<Workspace*>(ws)); }
+
+int ptof_check_status(void* wsv, void* stream) {
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w) return fail(PTOF_EINVAL, "null workspace");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+  int h = 0;
+  e = cudaMemcpy(&h, w->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "status read");
+  if (h != 0) {
+    cudaMemset(w->d_status, 0, sizeof(int));
+    return fail(PTOF_ETIMEOUT, "device wait gave up at site %d", h);
+  }
+  return PTOF_OK;
+}
+
+// --------------------------------------------------------------- selftests ----
+int ptof_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K, int mode,
+                       int* status, void* stream) {
+  if (!(M == 64 || M == 128) || N < 16 || N > 256 || N % 16 || K < 32 || K > 128 || K % 32)
+    return fail(PTOF_EINVAL, "selftest shape M=%d N=%d K=%d", M, N, K);
+  if ((mode & 4) && M != 128) return fail(PTOF_EINVAL, "TMEM A operand needs M=128");
+  if ((mode & 1) && M % 64) return fail(PTOF_EINVAL, "MN-major A needs M%%64==0");
+  if ((mode & 2) && N % 64) return fail(PTOF_EINVAL, "MN-major B needs N%%64==0");
+  cudaError_t e = launch_selftest_umma(A, B, D, M, N, K, mode, status,
+                                       static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "selftest_umma launch");
+}
+
+int ptof_selftest_tma(const void* src, int rows, int cols, int x0, int y0, void* out, int* status,
+                      void* stream) {
+  CUtensorMap map;
+  int rc = make_tmap_2d(&map, src, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows,
+                        static_cast<uint64_t>(cols) * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  cudaError_t e = launch_selftest_tma(map, x0, y0, out, status, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "selftest_tma launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,51 @@
+// Internal declarations shared by the C-ABI implementation and the kernel files.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <initializer_list>
+
+#include "../../include/pto_fuser_gdn.h"
+
+namespace ptof {
+
+enum WsKind { kWsGdnFwd = 1, kWsKkt = 2, kWsTriInv = 3, kWsScan = 4, kWsQkv = 5 };
+
+// Library-owned per-setup state.
+struct Workspace {
+  int kind = 0;
+  int device = 0;
+  ptof_gdn_params p{};
+  int* d_status = nullptr;       // device status word written by bounded waits
+  void* d_scratch = nullptr;     // optional kernel scratch, owned here
+  size_t scratch_bytes = 0;
+  int ex[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // per-kind extra integers
+};
+
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swz);
+Workspace* ws_create(int kind, const ptof_gdn_params* p);
+void ws_destroy(Workspace* w);
+int validate_gdn(const ptof_gdn_params& p);
+int check_ptrs(std::initializer_list<const void*> required,
+               std::initializer_list<const void*> optional);
+
+// kernels
+cudaError_t launch_gdn_fwd_simt(const ptof_gdn_params& p, const void* q, const void* k,
+                                const void* v, const void* beta, const float* g,
+                                const float* S0, void* o, float* S_final, cudaStream_t stream);
+bool gdn_fwd_simt_supports(const ptof_gdn_params& p);
+bool gdn_fwd_tc_supports(const ptof_gdn_params& p);
+int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v,
+                      const void* beta, const float* g, const float* S0, void* o,
+                      float* S_final, cudaStream_t stream);
+
+cudaError_t launch_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,
+                                 int mode, int* status, cudaStream_t stream);
+cudaError_t launch_selftest_tma(const CUtensorMap& map, int x0, int y0, void* out, int* status,
+                                cudaStream_t stream);
+
+}  // namespace ptof

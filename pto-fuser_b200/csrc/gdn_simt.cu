@@ -1,0 +1,275 @@
+// fp32 SIMT chunk forward of Gated DeltaNet.
+//
+// The full-precision path (fp32 inputs, reference tolerance 1e-4): every
+// contraction accumulates in fp32 FMA on the CUDA cores, the (I+A)^-1 solve is a
+// column-parallel forward substitution, and the state S[Dk, BV] of one
+// (batch, head, value-block) stays resident in shared memory across all chunks.
+// It restates, step for step, gdn_reference (examples/attention/_gdn_full.py:57-97):
+//   A   = tril((k k^T) * safe_exp(g_i - g_j) * beta_i, -1)          :73-75
+//   T   = solve_triangular(I + A, I, unitriangular)                   :76-78
+//   W   = T (k * beta * exp(g)),  U = T (v * beta)                     :79-82
+//   vn  = U - W S ; S = exp(g_last) S + k^T (vn * exp(g_last - g))    :83-87
+//   o   = (q S) * exp(g) + (q k^T * exp(min(g_i - g_j, 0)) * causal) vn  :88-94
+// with two additions the reference lacks: an initial state S0 and the final state.
+//
+// One CTA per (b*h, value block of kBV columns); the chunk loop is sequential.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace ptof {
+
+namespace simt {
+
+constexpr int kThreads = 256;
+constexpr int kBV = 32;       // value columns per CTA
+constexpr int kMaxDk = 128;
+constexpr int kC = kChunk;    // 64
+
+struct Args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* beta;
+  const float* g;
+  const float* S0;
+  void* o;
+  float* S_final;
+  int B, H, T, Dk, Dv;
+  int gate_mode;
+  float scale;
+  Strides4 sq, sv;   // q/k strides (Dk) and v/o strides (Dv)
+  Strides3 sg;       // beta / g strides
+};
+
+// shared-memory carve-up (floats); padded rows break bank conflicts
+struct Smem {
+  static constexpr int kLdK = kMaxDk + 1;
+  static constexpr int kLdC = kC + 1;
+  static constexpr int kLdV = kBV + 1;
+  float K[kC * kLdK];
+  float Q[kC * kLdK];
+  float W[kC * kLdK];
+  float V[kC * kLdV];
+  float U[kC * kLdV];
+  float Vn[kC * kLdV];
+  float A[kC * kLdC];
+  float Tm[kC * kLdC];
+  float Aqk[kC * kLdC];
+  float S[kMaxDk * kLdV];
+  float g[kC];
+  float beta[kC];
+};
+
+template <typename TI, typename TB, typename TO>
+__global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x;
+  const int b = bh / a.H, h = bh % a.H;
+  const int v0 = blockIdx.y * kBV;
+  const int nv = min(kBV, a.Dv - v0);
+  const int Dk = a.Dk;
+  constexpr int ldk = Smem::kLdK, ldc = Smem::kLdC, ldv = Smem::kLdV;
+
+  const TI* qp = static_cast<const TI*>(a.q) + b * a.sq.b + h * a.sq.h;
+  const TI* kp = static_cast<const TI*>(a.k) + b * a.sq.b + h * a.sq.h;
+  const TI* vp = static_cast<const TI*>(a.v) + b * a.sv.b + h * a.sv.h + v0;
+  TO* op = static_cast<TO*>(a.o) + b * a.sv.b + h * a.sv.h + v0;
+  const TB* bp = static_cast<const TB*>(a.beta) + b * a.sg.b + h * a.sg.h;
+  const float* gp = a.g ? a.g + b * a.sg.b + h * a.sg.h : nullptr;
+  const int64_t sbase = static_cast<int64_t>(bh) * Dk * a.Dv;
+
+  // initial state
+  for (int idx = tid; idx < Dk * kBV; idx += kThreads) {
+    const int d = idx / kBV, j = idx % kBV;
+    float x = 0.f;
+    if (a.S0 && j < nv) x = a.S0[sbase + static_cast<int64_t>(d) * a.Dv + v0 + j];
+    s.S[d * ldv + j] = x;
+  }
+
+  const int nc = a.T / kC;
+  for (int c = 0; c < nc; ++c) {
+    const int t0 = c * kC;
+    __syncthreads();
+    // ---- load the chunk -------------------------------------------------
+    for (int idx = tid; idx < kC * Dk; idx += kThreads) {
+      const int i = idx / Dk, d = idx % Dk;
+      const int64_t off = static_cast<int64_t>(t0 + i) * a.sq.t + d;
+      s.K[i * ldk + d] = to_f32(kp[off]);
+      s.Q[i * ldk + d] = to_f32(qp[off]);
+    }
+    for (int idx = tid; idx < kC * kBV; idx += kThreads) {
+      const int i = idx / kBV, j = idx % kBV;
+      s.V[i * ldv + j] = j < nv ? to_f32(vp[static_cast<int64_t>(t0 + i) * a.sv.t + j]) : 0.f;
+    }
+    if (tid < 32) {
+      // chunk-local inclusive cumsum of g, two tokens per lane (_gdn_full.py:63)
+      float x0 = 0.f, x1 = 0.f;
+      if (a.gate_mode != PTOF_GATE_NONE) {
+        x0 = gp[static_cast<int64_t>(t0 + 2 * tid) * a.sg.t];
+        x1 = gp[static_cast<int64_t>(t0 + 2 * tid + 1) * a.sg.t];
+      }
+      if (a.gate_mode == PTOF_GATE_RAW) {
+        x1 += x0;
+        float run = x1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, run, o);
+          if (tid >= o) run += y;
+        }
+        const float excl = run - x1;
+        x0 += excl;
+        x1 = run;
+      }
+      s.g[2 * tid] = x0;
+      s.g[2 * tid + 1] = x1;
+      s.beta[2 * tid] = to_f32(bp[static_cast<int64_t>(t0 + 2 * tid) * a.sg.t]);
+      s.beta[2 * tid + 1] = to_f32(bp[static_cast<int64_t>(t0 + 2 * tid + 1) * a.sg.t]);
+    }
+    __syncthreads();
+
+    // ---- A (strictly lower, gated) and Aqk (causal, gated) ----------------
+    for (int idx = tid; idx < kC * kC; idx += kThreads) {
+      const int i = idx / kC, j = idx % kC;
+      float akk = 0.f, aqk = 0.f;
+      if (j <= i) {
+        float dk = 0.f, dq = 0.f;
+        for (int d = 0; d < Dk; ++d) {
+          const float kj = s.K[j * ldk + d];
+          dk = fmaf(s.K[i * ldk + d], kj, dk);
+          dq = fmaf(s.Q[i * ldk + d], kj, dq);
+        }
+        const float x = s.g[i] - s.g[j];
+        if (j < i) akk = dk * (x <= 0.f ? expf(x) : 0.f) * s.beta[i];
+        aqk = dq * expf(fminf(x, 0.f));
+      }
+      s.A[i * ldc + j] = akk;
+      s.Aqk[i * ldc + j] = aqk;
+    }
+    __syncthreads();
+
+    // ---- T = (I + A)^-1: thread j solves column j by forward substitution --
+    if (tid < kC) {
+      const int j = tid;
+      for (int i = 0; i < kC; ++i) s.Tm[i * ldc + j] = (i == j) ? 1.f : 0.f;
+      for (int i = j + 1; i < kC; ++i) {
+        float acc = 0.f;
+        for (int kk = j; kk < i; ++kk) acc = fmaf(s.A[i * ldc + kk], s.Tm[kk * ldc + j], acc);
+        s.Tm[i * ldc + j] = -acc;
+      }
+    }
+    __syncthreads();
+
+    // ---- W = T (k * beta * exp(g)),  U = T (v * beta) ----------------------
+    for (int idx = tid; idx < kC * Dk; idx += kThreads) {
+      const int i = idx / Dk, d = idx % Dk;
+      float acc = 0.f;
+      for (int j = 0; j <= i; ++j)
+        acc = fmaf(s.Tm[i * ldc + j], s.K[j * ldk + d] * (s.beta[j] * expf(s.g[j])), acc);
+      s.W[i * ldk + d] = acc;
+    }
+    for (int idx = tid; idx < kC * kBV; idx += kThreads) {
+      const int i = idx / kBV, jv = idx % kBV;
+      float acc = 0.f;
+      for (int j = 0; j <= i; ++j) acc = fmaf(s.Tm[i * ldc + j], s.V[j * ldv + jv] * s.beta[j], acc);
+      s.U[i * ldv + jv] = acc;
+    }
+    __syncthreads();
+
+    // ---- v_new = U - W S --------------------------------------------------
+    for (int idx = tid; idx < kC * kBV; idx += kThreads) {
+      const int i = idx / kBV, jv = idx % kBV;
+      float acc = 0.f;
+      for (int d = 0; d < Dk; ++d) acc = fmaf(s.W[i * ldk + d], s.S[d * ldv + jv], acc);
+      s.Vn[i * ldv + jv] = s.U[i * ldv + jv] - acc;
+    }
+    __syncthreads();
+
+    // ---- o = scale * ((q S) * exp(g) + Aqk v_new) -------------------------
+    for (int idx = tid; idx < kC * kBV; idx += kThreads) {
+      const int i = idx / kBV, jv = idx % kBV;
+      float qs = 0.f;
+      for (int d = 0; d < Dk; ++d) qs = fmaf(s.Q[i * ldk + d], s.S[d * ldv + jv], qs);
+      float intra = 0.f;
+      for (int j = 0; j <= i; ++j) intra = fmaf(s.Aqk[i * ldc + j], s.Vn[j * ldv + jv], intra);
+      const float ov = a.scale * (qs * expf(s.g[i]) + intra);
+      if (jv < nv) op[static_cast<int64_t>(t0 + i) * a.sv.t + jv] = from_f32<TO>(ov);
+    }
+    __syncthreads();
+
+    // ---- S = exp(g_last) S + k^T (v_new * exp(g_last - g)) ----------------
+    const float gl = s.g[kC - 1];
+    const float egl = expf(gl);
+    for (int idx = tid; idx < Dk * kBV; idx += kThreads) {
+      const int d = idx / kBV, jv = idx % kBV;
+      float acc = 0.f;
+      for (int i = 0; i < kC; ++i)
+        acc = fmaf(s.K[i * ldk + d], s.Vn[i * ldv + jv] * expf(gl - s.g[i]), acc);
+      s.S[d * ldv + jv] = egl * s.S[d * ldv + jv] + acc;
+    }
+  }
+  __syncthreads();
+  if (a.S_final) {
+    for (int idx = tid; idx < Dk * kBV; idx += kThreads) {
+      const int d = idx / kBV, j = idx % kBV;
+      if (j < nv) a.S_final[sbase + static_cast<int64_t>(d) * a.Dv + v0 + j] = s.S[d * ldv + j];
+    }
+  }
+}
+
+template <typename TI, typename TB, typename TO>
+cudaError_t launch_typed(const Args& a, cudaStream_t stream) {
+  auto kern = gdn_fwd_simt_kernel<TI, TB, TO>;
+  const int smem = static_cast<int>(sizeof(Smem));
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.B * a.H, (a.Dv + kBV - 1) / kBV);
+  kern<<<grid, kThreads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename TI, typename TB>
+cudaError_t launch_out(const Args& a, int out_dtype, cudaStream_t st) {
+  switch (out_dtype) {
+    case PTOF_F32: return launch_typed<TI, TB, float>(a, st);
+    case PTOF_F16: return launch_typed<TI, TB, __half>(a, st);
+    default: return launch_typed<TI, TB, __nv_bfloat16>(a, st);
+  }
+}
+template <typename TI>
+cudaError_t launch_beta(const Args& a, int beta_dtype, int out_dtype, cudaStream_t st) {
+  switch (beta_dtype) {
+    case PTOF_F32: return launch_out<TI, float>(a, out_dtype, st);
+    case PTOF_F16: return launch_out<TI, __half>(a, out_dtype, st);
+    default: return launch_out<TI, __nv_bfloat16>(a, out_dtype, st);
+  }
+}
+
+}  // namespace simt
+
+// Host entry used by the C ABI. Shapes are validated by the caller.
+cudaError_t launch_gdn_fwd_simt(const ptof_gdn_params& p, const void* q, const void* k,
+                                const void* v, const void* beta, const float* g,
+                                const float* S0, void* o, float* S_final, cudaStream_t stream) {
+  simt::Args a;
+  a.q = q; a.k = k; a.v = v; a.beta = beta; a.g = g; a.S0 = S0; a.o = o; a.S_final = S_final;
+  a.B = p.B; a.H = p.H; a.T = p.T; a.Dk = p.Dk; a.Dv = p.Dv;
+  a.gate_mode = p.gate_mode;
+  a.scale = p.scale;
+  a.sq = make_strides4(p.layout, p.H, p.T, p.Dk);
+  a.sv = make_strides4(p.layout, p.H, p.T, p.Dv);
+  a.sg = make_strides3(p.layout, p.H, p.T);
+  switch (p.in_dtype) {
+    case PTOF_F32: return simt::launch_beta<float>(a, p.beta_dtype, p.out_dtype, stream);
+    case PTOF_F16: return simt::launch_beta<__half>(a, p.beta_dtype, p.out_dtype, stream);
+    default: return simt::launch_beta<__nv_bfloat16>(a, p.beta_dtype, p.out_dtype, stream);
+  }
+}
+
+bool gdn_fwd_simt_supports(const ptof_gdn_params& p) {
+  return p.C == kChunk && p.Dk >= 1 && p.Dk <= simt::kMaxDk && p.Dv >= 1;
+}
+
+}  // namespace ptof

@@ -1,0 +1,171 @@
+// Self-tests of the sm_100a building blocks the GDN kernels are made of.
+//
+//  * selftest_umma: one UMMA D = (+-)A * B^T with A [M,K] and B [N,K] written
+//    into shared memory in a chosen canonical layout (K-major or MN-major, 128-byte
+//    swizzle) or A placed in TMEM, then D read back from TMEM with the 32x32b
+//    load pattern the kernels use. Checks descriptors, instruction descriptor
+//    fields, the M=64 / M=128 accumulator lane maps and the TMEM A-operand packing.
+//  * selftest_tma: a TMA SWIZZLE_128B tile load, read back through sw128_off, so the
+//    software swizzle the kernels use for their own smem tiles matches the hardware.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace ptof {
+
+namespace selftest {
+
+constexpr int kMaxM = 128, kMaxN = 256, kMaxK = 128;
+
+__global__ void __launch_bounds__(128) umma_kernel(const float* A, const float* B, float* D,
+                                                   int M, int N, int K, int mode, int* status) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-align the dynamic smem base for the swizzle phase
+  const uint32_t base = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((base + 1023u) & ~1023u) - base);
+  unsigned char* sA = sm;                                  // up to 128x128 bf16 = 32 KB
+  unsigned char* sB = sm + kMaxM * kMaxK * 2;              // up to 256x128 bf16 = 64 KB
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sB + kMaxN * kMaxK * 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  __shared__ int abort_flag;
+
+  const bool a_mn = mode & 1, b_mn = mode & 2, a_tmem = mode & 4, neg = mode & 8;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t d_tmem = tmem;          // columns [0, N)
+  const uint32_t a_col = tmem + 256;     // A operand columns [256, 256 + K/2)
+
+  // ---- operands into smem (bf16) in the requested canonical layout ----
+  for (int idx = tid; idx < M * K; idx += 128) {
+    const int m = idx / K, k = idx % K;
+    const __nv_bfloat16 x = __float2bfloat16_rn(A[idx]);
+    uint32_t off;
+    if (!a_mn) off = (k / 64) * (M * 128) + sw128_off(m, (k % 64) * 2);
+    else off = (m / 64) * (K * 128) + sw128_off(k, (m % 64) * 2);
+    *reinterpret_cast<__nv_bfloat16*>(sA + off) = x;
+  }
+  for (int idx = tid; idx < N * K; idx += 128) {
+    const int n = idx / K, k = idx % K;
+    const __nv_bfloat16 x = __float2bfloat16_rn(B[idx]);
+    uint32_t off;
+    if (!b_mn) off = (k / 64) * (N * 128) + sw128_off(n, (k % 64) * 2);
+    else off = (n / 64) * (K * 128) + sw128_off(k, (n % 64) * 2);
+    *reinterpret_cast<__nv_bfloat16*>(sB + off) = x;
+  }
+  if (a_tmem) {
+    // row m -> lane m (M == 128); column c holds K elements 2c (low half), 2c+1 (high)
+    const int m = tid;
+    for (int c0 = 0; c0 < K / 2; c0 += 16) {
+      uint32_t r[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int k = 2 * (c0 + j);
+        r[j] = (m < M && k + 1 < K) ? pack_bf16(A[m * K + k], A[m * K + k + 1]) : 0u;
+      }
+      tmem_st16(a_col + ((32u * warp) << 16) + c0, r);
+    }
+    tmem_wait_st();
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (tid == 0) {
+    const uint32_t idesc = idesc_f16(M, N, a_mn, b_mn, true, neg);
+    const uint32_t sa = smem_u32(sA), sb = smem_u32(sB);
+    for (int ks = 0; ks < K / 16; ++ks) {
+      const int k0 = ks * 16;
+      uint64_t bdesc;
+      if (!b_mn) bdesc = sdesc_sw128(sb + (k0 / 64) * (N * 128) + (k0 % 64) * 2, 16, 1024);
+      else bdesc = sdesc_sw128(sb + k0 * 128, K * 128, 1024);
+      if (a_tmem) {
+        umma_ts(d_tmem, a_col + ks * 8, bdesc, idesc, ks > 0);
+      } else {
+        uint64_t adesc;
+        if (!a_mn) adesc = sdesc_sw128(sa + (k0 / 64) * (M * 128) + (k0 % 64) * 2, 16, 1024);
+        else adesc = sdesc_sw128(sa + k0 * 128, K * 128, 1024);
+        umma_ss(d_tmem, adesc, bdesc, idesc, ks > 0);
+      }
+    }
+    umma_commit(bar);
+  }
+  __syncwarp();
+  mbar_wait(bar, 0, &abort_flag, status, 100);
+  tc_fence_after();
+
+  // ---- read D back: M=128 -> lane m; M=64 -> lane 16*(m/16) + m%16 ----
+  int row = -1;
+  if (M == 128) row = warp * 32 + lane;
+  else if (lane < 16) row = warp * 16 + lane;
+  for (int c0 = 0; c0 < N; c0 += 16) {
+    float v[16];
+    tmem_ld16(d_tmem + ((32u * warp) << 16) + c0, v);
+    tmem_wait_ld();
+    if (row >= 0 && row < M) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) D[row * N + c0 + j] = v[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// TMA SWIZZLE_128B load of a [64 x 64] bf16 box at (x0, y0), de-swizzled in software.
+__global__ void tma_kernel(const __grid_constant__ CUtensorMap map, int x0, int y0,
+                           __nv_bfloat16* out, int* status) {
+  __shared__ __align__(1024) unsigned char tile[64 * 128];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar, 64 * 128);
+    tma_load_2d(tile, &map, &bar, x0, y0);
+  }
+  mbar_wait(&bar, 0, &abort_flag, status, 200);
+  for (int idx = tid; idx < 64 * 64; idx += blockDim.x) {
+    const int r = idx / 64, c = idx % 64;
+    out[idx] = *reinterpret_cast<const __nv_bfloat16*>(tile + sw128_off(r, c * 2));
+  }
+}
+
+}  // namespace selftest
+
+cudaError_t launch_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,
+                                 int mode, int* status, cudaStream_t stream) {
+  const int smem = selftest::kMaxM * selftest::kMaxK * 2 + selftest::kMaxN * selftest::kMaxK * 2 +
+                   64 + 1024;
+  cudaError_t e = cudaFuncSetAttribute(selftest::umma_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  selftest::umma_kernel<<<1, 128, smem, stream>>>(A, B, D, M, N, K, mode, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_selftest_tma(const CUtensorMap& map, int x0, int y0, void* out, int* status,
+                                cudaStream_t stream) {
+  selftest::tma_kernel<<<1, 128, 0, stream>>>(map, x0, y0, static_cast<__nv_bfloat16*>(out),
+                                              status);
+  return cudaGetLastError();
+}
+
+}  // namespace ptof

@@ -1,0 +1,136 @@
+"""Host side of the fused chunked Gated DeltaNet forward on B200.
+
+``GDNChunkForward`` is a persistent runner bound to one shape: its constructor
+calls ``ptof_gdn_fwd_setup`` (library-owned workspace, as ``FusedKernel`` does in
+the reference, fused.py:93-115) and ``__call__`` only launches on the current
+CUDA stream, so it can be captured in a CUDA graph. ``chunk_gdn_forward`` is the
+functional entry point with a per-shape runner cache.
+
+Semantics: gdn_reference (examples/attention/_gdn_full.py:57-97) with the output
+scale folded in, plus an optional initial state and the final state.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import native as nv
+
+_LAYOUTS = {"bhtd": nv.LAYOUT_BHTD, "bthd": nv.LAYOUT_BTHD}
+_GATES = {"raw": nv.GATE_RAW, "cumsum": nv.GATE_CUMSUM, "none": nv.GATE_NONE}
+
+
+class GDNChunkForward:
+    """One-shape persistent runner of the fused GDN chunk forward."""
+
+    def __init__(self, B: int, H: int, T: int, Dk: int, Dv: int, *,
+                 in_dtype=torch.bfloat16, beta_dtype=None, out_dtype=None,
+                 gate: str = "raw", layout: str = "bhtd", scale: Optional[float] = None,
+                 chunk: int = 64, device=None) -> None:
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        beta_dtype = beta_dtype or in_dtype
+        out_dtype = out_dtype or in_dtype
+        self.shape = (B, H, T, Dk, Dv)
+        self.in_dtype, self.beta_dtype, self.out_dtype = in_dtype, beta_dtype, out_dtype
+        self.gate, self.layout = gate, layout
+        self.scale = Dk ** -0.5 if scale is None else float(scale)
+        p = nv.GdnParams(B, H, T, chunk, Dk, Dv, nv.dtype_code(in_dtype),
+                         nv.dtype_code(beta_dtype), nv.dtype_code(out_dtype),
+                         _GATES[gate], _LAYOUTS[layout], self.scale)
+        L = nv.lib()
+        with torch.cuda.device(self.device):
+            self._ws = L.ptof_gdn_fwd_setup(ctypes.byref(p))
+        if not self._ws:
+            raise nv.NativeError(nv.EINVAL, nv.last_error())
+
+    # logical shapes of the operands in the chosen layout
+    def _qshape(self, D):
+        B, H, T = self.shape[:3]
+        return (B, H, T, D) if self.layout == "bhtd" else (B, T, H, D)
+
+    def _gshape(self):
+        B, H, T = self.shape[:3]
+        return (B, H, T) if self.layout == "bhtd" else (B, T, H)
+
+    def _check(self, name, t, shape, dtype):
+        if t is None:
+            raise ValueError(f"{name} is required")
+        if tuple(t.shape) != tuple(shape):
+            raise ValueError(f"{name} shape {tuple(t.shape)} != expected {tuple(shape)}")
+        if t.dtype != dtype:
+            raise TypeError(f"{name} dtype {t.dtype} != contract dtype {dtype}")
+        if t.device != self.device:
+            raise ValueError(f"{name} on {t.device}, runner on {self.device}")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+
+    def __call__(self, q, k, v, beta, g, initial_state=None, *, o=None,
+                 final_state=None, output_final_state: bool = True
+                 ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+        B, H, T, Dk, Dv = self.shape
+        self._check("q", q, self._qshape(Dk), self.in_dtype)
+        self._check("k", k, self._qshape(Dk), self.in_dtype)
+        self._check("v", v, self._qshape(Dv), self.in_dtype)
+        self._check("beta", beta, self._gshape(), self.beta_dtype)
+        if self.gate != "none":
+            self._check("g", g, self._gshape(), torch.float32)
+        else:
+            g = None
+        if initial_state is not None:
+            self._check("initial_state", initial_state, (B, H, Dk, Dv), torch.float32)
+        if o is None:
+            o = torch.empty(self._qshape(Dv), device=self.device, dtype=self.out_dtype)
+        if output_final_state and final_state is None:
+            final_state = torch.empty(B, H, Dk, Dv, device=self.device, dtype=torch.float32)
+        rc = nv.lib().ptof_gdn_fwd_exec(
+            self._ws, q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(), nv.ptr(g),
+            nv.ptr(initial_state), o.data_ptr(), nv.ptr(final_state),
+            nv.stream_handle(self.device))
+        nv.check(rc)
+        return o, final_state
+
+    def check_status(self) -> None:
+        """Synchronise and raise if a bounded device wait of the last launch gave up."""
+        nv.check(nv.lib().ptof_check_status(self._ws, nv.stream_handle(self.device)))
+
+    def close(self) -> None:
+        if getattr(self, "_ws", None):
+            nv.lib().ptof_gdn_fwd_teardown(self._ws)
+            self._ws = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_RUNNERS: Dict[tuple, GDNChunkForward] = {}
+
+
+def chunk_gdn_forward(q, k, v, beta, g, *, scale: Optional[float] = None,
+                      initial_state=None, output_final_state: bool = True,
+                      gate: str = "raw", layout: str = "bhtd", out_dtype=None):
+    """Fused chunked GDN forward on the current CUDA device.
+
+    q, k [B,H,T,Dk] and v [B,H,T,Dv] (or [B,T,H,D] with layout="bthd"), beta like
+    g [B,H,T]; g fp32 per-token log decay (gate="raw"), chunk-local cumsum
+    (gate="cumsum") or ignored (gate="none"). Returns (o, final_state)."""
+    if layout == "bhtd":
+        B, H, T, Dk = q.shape
+    else:
+        B, T, H, Dk = q.shape
+    Dv = v.shape[-1]
+    out_dtype = out_dtype or q.dtype
+    sc = Dk ** -0.5 if scale is None else float(scale)
+    key = (B, H, T, Dk, Dv, q.dtype, beta.dtype, out_dtype, gate, layout, sc, q.device)
+    r = _RUNNERS.get(key)
+    if r is None:
+        r = GDNChunkForward(B, H, T, Dk, Dv, in_dtype=q.dtype, beta_dtype=beta.dtype,
+                            out_dtype=out_dtype, gate=gate, layout=layout, scale=sc,
+                            device=q.device)
+        _RUNNERS[key] = r
+    return r(q, k, v, beta, g, initial_state, output_final_state=output_final_state)

@@ -1,0 +1,73 @@
+"""Parity of the CUDA GDN chunk forward (through the C ABI) with the CPU oracle,
+which is itself pinned to the reference's gdn_reference (tests/test_oracle.py)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle(inp, scale, gate="raw", layout="bhtd"):
+    f = lambda t: t.float().cpu().numpy()
+    q, k, v, b, g = (f(inp[n]) for n in ("q", "k", "v", "beta", "g"))
+    S0 = f(inp["S0"]) if "S0" in inp else None
+    if layout == "bthd":
+        q, k, v = (x.transpose(0, 2, 1, 3) for x in (q, k, v))
+        b, g = b.transpose(0, 2, 1), g.transpose(0, 2, 1)
+    if gate == "cumsum":
+        g = orc.chunk_cumsum(g).reshape(g.shape)
+    o, S = orc.gdn_forward(q, k, v, b, g, scale, S0=S0,
+                           gate={"raw": "raw", "cumsum": "cumsum", "none": "none"}[gate])
+    if layout == "bthd":
+        o = o.transpose(0, 2, 1, 3)
+    return o, S
+
+
+def _run(B, H, T, Dk, Dv, dtype, tol, gate="raw", layout="bhtd", s0=None, mu=2.0, seed=0):
+    from pto_fuser import chunk_gdn_forward, make_gdn_inputs
+    inp = make_gdn_inputs(B, H, T, Dk, Dv, dtype=dtype, device="cuda", mu=mu, seed=seed,
+                          layout=layout, s0_std=s0)
+    g = inp["g"]
+    if gate == "cumsum":
+        gl = g if layout == "bhtd" else g.transpose(1, 2)
+        gl = gl.reshape(B, H, T // 64, 64).cumsum(-1).reshape(B, H, T)
+        g = (gl if layout == "bhtd" else gl.transpose(1, 2)).contiguous()
+    scale = Dk ** -0.5
+    o, S = chunk_gdn_forward(inp["q"], inp["k"], inp["v"], inp["beta"], g, scale=scale,
+                             initial_state=inp.get("S0"), gate=gate, layout=layout)
+    torch.cuda.synchronize()
+    ref_o, ref_S = _oracle(inp, scale, gate=gate, layout=layout)
+    eo = orc.rel_l2(o.float().cpu().numpy(), ref_o)
+    eS = orc.rel_l2(S.cpu().numpy(), ref_S)
+    assert eo < tol and eS < tol, (eo, eS)
+    return o, S
+
+
+def test_fp32_config0():
+    """B1 H4 T512 D128 fp32, tolerance 1e-4."""
+    _run(1, 4, 512, 128, 128, torch.float32, 1e-4)
+
+
+@pytest.mark.parametrize("gate,layout", [("none", "bhtd"), ("cumsum", "bthd"), ("raw", "bthd")])
+def test_fp32_variants(gate, layout):
+    _run(2, 2, 256, 64, 64, torch.float32, 1e-4, gate=gate, layout=layout)
+
+
+def test_fp32_initial_state_and_dk_ne_dv():
+    _run(1, 2, 256, 128, 64, torch.float32, 1e-4, s0=0.02, mu=3.0)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_bf16_small(D):
+    _run(2, 2, 256, D, D, torch.bfloat16, 1e-2)
+
+
+def test_deterministic():
+    from pto_fuser import chunk_gdn_forward, make_gdn_inputs
+    inp = make_gdn_inputs(1, 2, 256, 128, dtype=torch.bfloat16, device="cuda")
+    a = chunk_gdn_forward(inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"])
+    b = chunk_gdn_forward(inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"])
+    torch.cuda.synchronize()
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
