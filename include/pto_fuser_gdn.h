@@ -92,6 +92,13 @@ PTOF_API int ptof_gdn_fwd_exec(void* ws, const void* q, const void* k, const voi
                       const float* g, const float* S0, void* o, float* S_final, void* stream);
 PTOF_API void ptof_gdn_fwd_teardown(void* ws);
 
+/* Stage timing trace (no counterpart in the reference, which attributes cost with
+ * compile-time knock-out flags, kernels/kkt_fused.h:49-56): while set, every
+ * tensor-core launch on this workspace writes, for CTA 0 and its first `chunks`
+ * chunks, 16 globaltimer stamps (ns) per chunk into the caller's device buffer
+ * dev_buf[chunks][16]. chunks = 0 turns tracing off. */
+PTOF_API int ptof_gdn_fwd_set_trace(void* ws, void* dev_buf, int chunks);
+
 /* Reads (and clears) the workspace's device status word after synchronising
  * `stream`: PTOF_OK, or PTOF_ETIMEOUT when a bounded device wait gave up. */
 PTOF_API int ptof_check_status(void* ws, void* stream);

@@ -71,6 +71,26 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return PTOF_OK;
 }
 
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(PTOF_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return fail(PTOF_EALIGN, "TMA base address not 16-byte aligned");
+  for (int i = 0; i < 2; ++i)
+    if (strides_bytes[i] % 16 != 0)
+      return fail(PTOF_EALIGN, "TMA stride %llu not a multiple of 16 bytes",
+                  (unsigned long long)strides_bytes[i]);
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t s[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t e[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PTOF_ECUDA, "cuTensorMapEncodeTiled(3d) failed (%d)", (int)r);
+  return PTOF_OK;
+}
+
 // ------------------------------------------------------------ workspace ----
 Workspace* ws_create(int kind, const ptof_gdn_params* p) {
   Workspace* w = new Workspace();
@@ -172,6 +192,15 @@ int ptof_gdn_fwd_exec(void* wsv, const void* q, const void* k, const void* v, co
 }
 
 void ptof_gdn_fwd_teardown(void* ws) { ws_destroy(static_cast<Workspace*>(ws)); }
+
+int ptof_gdn_fwd_set_trace(void* wsv, void* dev_buf, int chunks) {
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w || w->kind != kWsGdnFwd) return fail(PTOF_EINVAL, "not a gdn_fwd workspace");
+  if (chunks < 0 || (chunks > 0 && !dev_buf)) return fail(PTOF_EINVAL, "bad trace buffer");
+  w->trace = chunks > 0 ? dev_buf : nullptr;
+  w->trace_chunks = chunks;
+  return PTOF_OK;
+}
 
 int ptof_check_status(void* wsv, void* stream) {
   Workspace* w = static_cast<Workspace*>(wsv);

@@ -20,6 +20,8 @@ struct Workspace {
   void* d_scratch = nullptr;     // optional kernel scratch, owned here
   size_t scratch_bytes = 0;
   int ex[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // per-kind extra integers
+  void* trace = nullptr;         // caller-owned device buffer of stage timestamps
+  int trace_chunks = 0;
 };
 
 int fail(int code, const char* fmt, ...);
@@ -27,6 +29,8 @@ int cuda_fail(cudaError_t e, const char* what);
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                  uint32_t box_outer, CUtensorMapSwizzle swz);
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
 Workspace* ws_create(int kind, const ptof_gdn_params* p);
 void ws_destroy(Workspace* w);
 int validate_gdn(const ptof_gdn_params& p);

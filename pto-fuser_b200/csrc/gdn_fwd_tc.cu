@@ -1,9 +1,992 @@
-// placeholder: tensor-core forward (filled in below)
+// Fused chunked Gated DeltaNet forward on B200 tensor cores (tcgen05 + TMEM + TMA).
+//
+// One CTA owns one (batch, head) pair and walks its chunks (C = 64 tokens) in order.
+// Per chunk c, with g the chunk-local cumsum of the log decay and gl = g[63]:
+//   A    = tril(beta_i * k_i.k_j * exp(g_i - g_j), -1)      T = (I + A)^-1
+//   W^T  = K^T (T * (beta e^g)_j)^T        U^T = V^T (T * beta_j)^T
+//   Vn^T = U^T - S^T W^T                                  (S = state [Dk, Dv])
+//   O^T  = S^T (Q * e^g)^T + Vn^T Aqk^T,   Aqk = tril(q_i.k_j * exp(min(g_i - g_j, 0)))
+//   S^T  = e^gl S^T + (Vn^T * e^(gl - g)) K
+// which is the reference's gdn_reference (examples/attention/_gdn_full.py:57-97) with
+// every contraction transposed so the value dimension Dv is the UMMA M dimension:
+// all chain MMAs have M = Dv (128 -> full datapath), the state lives in TMEM as
+// fp32 S^T (TMEM lane = value column), and its bf16 copy feeds the next chunk's
+// MMAs straight from TMEM.
+//
+// Warp roles (384 threads):
+//   warp 0     TMA producer: K, Q, V tiles (128B-swizzled), g, beta -> 2-stage ring
+//   warp 1     UMMA issuer (one thread)
+//   warp 2     TMEM allocator
+//   warps 4-7  "prep": kkt/qk epilogue from TMEM, Q*e^g, (I+A)^-1 (blocked forward
+//              substitution in fp32), T' and T'' for the WY MMAs, W^T readout
+//   warps 8-11 "scan": V_new readout, state update, output epilogue
+// Chunk c+1's prep overlaps chunk c's scan.
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+
 #include "capi_internal.h"
+#include "common.cuh"
+#include "ptx.cuh"
+
 namespace ptof {
-bool gdn_fwd_tc_supports(const ptof_gdn_params&) { return false; }
-int launch_gdn_fwd_tc(Workspace*, const void*, const void*, const void*, const void*, const float*,
-                      const float*, void*, float*, cudaStream_t) {
-  return fail(PTOF_EUNSUPPORTED, "tensor-core forward not built");
+namespace tcfwd {
+
+constexpr int kC = kChunk;  // 64
+constexpr int kThreads = 512;
+constexpr int kPrepThreads = 256;
+constexpr int kPrepBar = 1, kScanBar = 2;  // named barrier ids
+
+// ------------------------------------------------------------------ layout ----
+template <int DK, int DV>
+struct Layout {
+  static constexpr int NKB = DK / 64;               // 64-wide d blocks
+  static constexpr int NVB = DV / 64;
+  static constexpr bool SA_TMEM = (DV == 128);       // bf16 S^T as a TMEM A operand
+  static_assert(DV <= DK, "the W^T tile doubles as the slow-chunk V_new*gamma tile");
+  // input ring (3 stages): [K | Q] per 64-wide d block, then the per-token arrays
+  static constexpr int NIN = 3;
+  static constexpr int KQ_REGION = 2 * kC * 128;     // K rows 0-63 | Q rows 64-127, 16 KB
+  static constexpr int OFF_KQ = 0;                   // within an input stage
+  static constexpr int OFF_MISC = NKB * KQ_REGION;
+  static constexpr int IN_STAGE = OFF_MISC + 3072;
+  // misc sub-offsets (bytes within MISC): per-token fp32 arrays of the chunk
+  static constexpr int M_GRAW = 0, M_BRAW = 256, M_GCUM = 512, M_EG = 768, M_BK = 1024,
+                       M_BV = 1280, M_GAM = 1536, M_ROWF = 1792, M_ROWFB = 2048,
+                       M_COLF = 2304, M_EGL = 2560, M_FAST = 2564, M_ENGL = 2568;
+  // V ring (2 stages)
+  static constexpr int V_REGION = kC * 128;          // 8 KB per 64-wide block
+  static constexpr int OFF_V = NIN * IN_STAGE;
+  static constexpr int V_STAGE = NVB * V_REGION;
+  // Aqk (2 buffers), W^T (1 buffer; slow chunks reuse it for V_new*gamma)
+  static constexpr int OFF_AQK = OFF_V + 2 * V_STAGE;
+  static constexpr int OFF_WT = OFF_AQK + 2 * kC * 128;
+  // prep buffers
+  static constexpr int OFF_TP = OFF_WT + DK * 128;   // T' bf16 [64 x 64] (also inverse scratch)
+  static constexpr int OFF_TPP = OFF_TP + 8192;      // T''
+  static constexpr int AW_LD = 68;                   // fp32 row stride of the inverse workspace
+  static constexpr int OFF_AW = OFF_TPP + 8192;
+  static constexpr int AW_BYTES = ((kC * AW_LD * 4 + 1023) / 1024) * 1024;
+  // chain buffers
+  static constexpr int OFF_VNT = OFF_AW + AW_BYTES;  // bf16 Vn^T [DV x 64]
+  static constexpr int OFF_SA = OFF_VNT + DV * 128;  // bf16 S^T [DV x DK] (smem variant)
+  static constexpr int SA_BYTES = SA_TMEM ? 0 : NKB * DV * 128;
+  static constexpr int OFF_OSC = OFF_SA + SA_BYTES;  // fp32 [64] output multipliers (scan)
+  static constexpr int OFF_BAR = OFF_OSC + 256;
+  static constexpr int BYTES = OFF_BAR + 512 + 1024;  // + alignment slack
+  // TMEM columns
+  static constexpr int T_SM = 0;                     // fp32 S^T master: DK columns
+  static constexpr int T_SA = DK;                    // bf16 S^T: DK/2 columns
+  static constexpr int T_VN0 = DK + (SA_TMEM ? DK / 2 : 0);
+  static constexpr int T_VN1 = T_VN0 + kC;
+  static constexpr int T_O = T_VN1 + kC;
+  static constexpr int T_KQ = T_O + kC;             // [K;Q] K^T of the chunk in prep
+  static constexpr int T_RW = T_KQ + kC;             // W^T of the chunk in prep
+  static constexpr int T_COLS = 512;
+  static_assert(T_RW + kC <= T_COLS, "TMEM budget");
+  static_assert(BYTES <= 227 * 1024, "smem budget");
+};
+
+// barrier slots (uint64 each) inside the BAR area
+enum Bar {
+  B_FULL0 = 0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_GREADY0, B_GREADY1, B_GREADY2,
+  B_VFULL0, B_VFULL1, B_VEMPTY0, B_VEMPTY1, B_WREADY,
+  B_KQFULL, B_TREADY, B_WUFULL, B_RWFREE, B_VNFREE0, B_VNFREE1, B_SREADY, B_VNFULL,
+  B_VNREADY, B_SFULL, B_OFULL, B_OFREE, B_DONE, B_KQFREE, B_COUNT
+};
+
+struct Params {
+  CUtensorMap mapK, mapQ, mapV;   // 3D maps, box = 64 d x 64 tokens
+  const float* g;                  // [B,H,T] / [B,T,H] fp32 (may be null: ungated)
+  const void* beta;
+  const float* S0;                 // [B,H,DK,DV] or null
+  void* o;
+  float* S_final;                  // or null
+  int* status;
+  unsigned long long* trace;       // optional [chunks x kTraceSlots] timestamps of CTA 0
+  int trace_chunks;
+  int knockout;                    // cost-attribution knock-outs (results invalid): bit0 skip
+                                   // (I+A)^-1, bit1 skip the kkt/qk epilogue math
+  int B, H, T, nc;
+  int gate_mode, beta_dtype, layout;
+  int64_t gs_b, gs_h, gs_t;        // g / beta strides (elements)
+  int64_t os_b, os_h, os_t;        // o strides (elements)
+  float scale;
+};
+
+// Optional stage timestamps (globaltimer, ns) of CTA 0: slot layout per chunk.
+constexpr int kTraceSlots = 16;
+enum TraceSlot {
+  TR_TMA_ISSUE = 0, TR_PREP_FULL, TR_PREP_KQ, TR_PREP_EPI, TR_PREP_INV, TR_PREP_TREADY,
+  TR_PREP_WU, TR_PREP_END, TR_SCAN_VNFULL, TR_SCAN_VNREADY, TR_SCAN_SFULL, TR_SCAN_SREADY,
+  TR_SCAN_OFULL, TR_SCAN_END, TR_MMA_C1, TR_MMA_C2
+};
+__device__ __forceinline__ void trace_mark(const Params& P, int c, int slot) {
+  if (P.trace != nullptr && blockIdx.x == 0 && c < P.trace_chunks)
+    P.trace[c * kTraceSlots + slot] = globaltimer_ns();
 }
+
+// ------------------------------------------------------------ small helpers ----
+struct Sync {
+  volatile int* abort;
+  int* status;
+  __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, int site) const {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait(bar, parity, abort, status, site);
+  }
+};
+
+__device__ __forceinline__ float ld_beta(const void* p, int dt, int64_t i) {
+  if (dt == PTOF_F32) return static_cast<const float*>(p)[i];
+  if (dt == PTOF_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  return F16 ? pack_f16(a, b) : pack_bf16(a, b);
+}
+template <bool F16>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+  return F16 ? unpack_f16(u) : unpack_bf16(u);
+}
+
+// Write 8 consecutive 16-bit values (one 16-byte chunk) of a 128B-swizzled row.
+__device__ __forceinline__ void st_chunk(unsigned char* region, int row, int chunk, uint4 v) {
+  *reinterpret_cast<uint4*>(region + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
+}
+__device__ __forceinline__ uint4 ld_chunk(const unsigned char* region, int row, int chunk) {
+  return *reinterpret_cast<const uint4*>(region + row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// ------------------------------------------------------- (I + A)^-1, 64 x 64 ----
+// Blocked forward substitution for T = (I + A)^-1 (A strictly lower, fp32, in place in
+// Aw with row stride LD; zeros on and above the diagonal on entry).
+//
+// Level 0: the four 16x16 diagonal blocks, one column of T per thread (64 threads):
+// right-looking substitution, x_i -= A[i][k] x_k as soon as x_k is final, so the
+// dependency chain is 15 FMAs long and every A[i][k] load is independent of x.
+// Returns the column in x (x[i] = T[16b+i][16b+j]); the caller stores it after a
+// barrier (other columns still read A from the block).
+template <int LD>
+__device__ __forceinline__ void diag16_col(const float* Aw, int b, int j, float (&x)[16]) {
+  const float* blk = Aw + 16 * b * LD + 16 * b;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;
+#pragma unroll
+  for (int k = 0; k < 15; ++k) {
+    const float xk = x[k];
+#pragma unroll
+    for (int i = k + 1; i < 16; ++i) x[i] = fmaf(-blk[i * LD + k], xk, x[i]);
+  }
+}
+
+// Levels 1-2 over 256 threads, in place on Aw (diagonal 16-blocks already hold T).
+// 16 -> 32: T21 = -T22 (A21 T11) for block pairs (1,0), (3,2);
+// 32 -> 64: T[32:64, 0:32] = -T_B (A_BA T_A). Loops run over full ranges: the zero
+// upper triangles of T11 / T22 / T_A / T_B make the extra terms vanish, and the
+// fixed trip counts let every load be issued ahead of its FMAs. X: >= 32 x 36 floats.
+template <int LD, int BAR, int NT>
+__device__ __forceinline__ void tri_inv64_merge(float* Aw, float* X, int p) {
+  static_assert(NT == 256, "merge mapping assumes 256 threads");
+  constexpr int XLD = 36;
+  {  // 16 -> 32: pair P = p >> 7; 2 outputs per thread
+    const int P = p >> 7, e = p & 127, r = e >> 3, c0 = (e & 7) * 2;
+    const int r1 = 32 * P + 16, c1 = 32 * P;
+    float2 xx = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float a = Aw[(r1 + r) * LD + c1 + k];
+      const float2 t = *reinterpret_cast<const float2*>(Aw + (c1 + k) * LD + c1 + c0);
+      xx = __ffma2_rn(make_float2(a, a), t, xx);
+    }
+    *reinterpret_cast<float2*>(X + (P * 16 + r) * XLD + c0) = xx;
+    named_bar_sync(BAR, NT);
+    float2 yy = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float a = Aw[(r1 + r) * LD + r1 + k];
+      const float2 t = *reinterpret_cast<const float2*>(X + (P * 16 + k) * XLD + c0);
+      yy = __ffma2_rn(make_float2(a, a), t, yy);
+    }
+    *reinterpret_cast<float2*>(Aw + (r1 + r) * LD + c1 + c0) = make_float2(-yy.x, -yy.y);
+  }
+  named_bar_sync(BAR, NT);
+  {  // 32 -> 64: 4 outputs per thread
+    const int r = p >> 3, c0 = (p & 7) * 4;
+    float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float a = Aw[(32 + r) * LD + k];
+      const float4 t = *reinterpret_cast<const float4*>(Aw + k * LD + c0);
+      lo = __ffma2_rn(make_float2(a, a), make_float2(t.x, t.y), lo);
+      hi = __ffma2_rn(make_float2(a, a), make_float2(t.z, t.w), hi);
+    }
+    *reinterpret_cast<float4*>(X + r * XLD + c0) = make_float4(lo.x, lo.y, hi.x, hi.y);
+    named_bar_sync(BAR, NT);
+    float2 ylo = make_float2(0.f, 0.f), yhi = make_float2(0.f, 0.f);
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float a = Aw[(32 + r) * LD + 32 + k];
+      const float4 x = *reinterpret_cast<const float4*>(X + k * XLD + c0);
+      ylo = __ffma2_rn(make_float2(a, a), make_float2(x.x, x.y), ylo);
+      yhi = __ffma2_rn(make_float2(a, a), make_float2(x.z, x.w), yhi);
+    }
+    // A_BA (read only before the previous barrier) is overwritten by T_BA
+    *reinterpret_cast<float4*>(Aw + (32 + r) * LD + c0) = make_float4(-ylo.x, -ylo.y, -yhi.x, -yhi.y);
+  }
+  named_bar_sync(BAR, NT);
+}
+
+// ------------------------------------------------------------------ kernel ----
+template <int DK, int DV, bool F16, typename TO>
+__global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_constant__ Params P) {
+  using L = Layout<DK, DV>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t sbase = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((sbase + 1023u) & ~1023u) - sbase);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_COUNT);
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.x, b = bh / P.H, h = bh % P.H;
+  const int nc = P.nc;
+  Sync sy{&abort_flag, P.status};
+
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < B_COUNT; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[B_EMPTY0 + i], 2);
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, L::T_COLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // chunk c lives in input stage c % 3 (use index c / 3), V stage c & 1, Aqk buffer c & 1
+  auto stage = [&](int c) { return sm + (c % 3) * L::IN_STAGE; };
+  auto misc = [&](int c) { return reinterpret_cast<float*>(stage(c) + L::OFF_MISC); };
+  auto vstage = [&](int c) { return sm + L::OFF_V + (c & 1) * L::V_STAGE; };
+  auto aqk = [&](int c) { return sm + L::OFF_AQK + (c & 1) * (kC * 128); };
+  auto in_par = [&](int c) { return static_cast<uint32_t>((c / 3) & 1); };
+
+  // ================================================================ TMA ====
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&P.mapK);
+      prefetch_tmap(&P.mapQ);
+      prefetch_tmap(&P.mapV);
+    }
+    const int gelt = P.beta_dtype == PTOF_F32 ? 4 : 2;
+    const bool contiguous = (P.gs_t == 1);
+    const bool bhtd = (P.layout == PTOF_LAYOUT_BHTD);
+    for (int c = 0; c < nc; ++c) {
+      const int s = c % 3;
+      if (c >= 3) sy.wait(&bars[B_EMPTY0 + s], in_par(c) ^ 1, 1);
+      unsigned char* st = stage(c);
+      float* ms = misc(c);
+      const int t0 = c * kC;
+      const int y = bhtd ? t0 : h;
+      const int z = bhtd ? bh : b * P.T + t0;
+      const int64_t gb = b * P.gs_b + h * P.gs_h + static_cast<int64_t>(t0) * P.gs_t;
+      if (!contiguous) {
+        // token-strided g / beta (token-major layout): plain loads, 2 tokens per lane
+        for (int i = lane; i < kC; i += 32) {
+          ms[L::M_GRAW / 4 + i] = P.g ? P.g[gb + i * P.gs_t] : 0.f;
+          reinterpret_cast<float*>(st + L::OFF_MISC + L::M_BRAW)[i] =
+              ld_beta(P.beta, P.beta_dtype, gb + i * P.gs_t);
+        }
+        __threadfence_block();
+      }
+      __syncwarp();
+      if (lane == 0) {
+        uint32_t bytes = 2 * DK * kC * 2;
+        if (contiguous) bytes += (P.g ? kC * 4 : 0) + kC * gelt;
+        mbar_arrive_expect_tx(&bars[B_FULL0 + s], bytes);
+#pragma unroll
+        for (int kb = 0; kb < L::NKB; ++kb) {
+          tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION, &P.mapK, &bars[B_FULL0 + s], kb * 64, y, z);
+          tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION + kC * 128, &P.mapQ, &bars[B_FULL0 + s],
+                      kb * 64, y, z);
+        }
+        if (contiguous) {
+          if (P.g) bulk_load(st + L::OFF_MISC + L::M_GRAW, P.g + gb, kC * 4, &bars[B_FULL0 + s]);
+          bulk_load(st + L::OFF_MISC + L::M_BRAW,
+                    static_cast<const unsigned char*>(P.beta) + gb * gelt, kC * gelt,
+                    &bars[B_FULL0 + s]);
+        }
+        trace_mark(P, c, TR_TMA_ISSUE);
+      }
+      // V tile of chunk c (consumed by the U^T UMMA only)
+      if (c >= 2) sy.wait(&bars[B_VEMPTY0 + (c & 1)], ((c >> 1) + 1) & 1, 2);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars[B_VFULL0 + (c & 1)], DV * kC * 2);
+#pragma unroll
+        for (int vb = 0; vb < L::NVB; ++vb)
+          tma_load_3d(vstage(c) + vb * L::V_REGION, &P.mapV, &bars[B_VFULL0 + (c & 1)], vb * 64, y, z);
+      }
+      __syncwarp();
+    }
+  }
+  // ================================================================ MMA ====
+  // One thread issues every UMMA. Five in-order streams, polled without blocking,
+  // chain work first:
+  //   C2 (S^T += (Vn^T g) K ; O += Vn^T Aqk^T)  C1a (Vn^T = U^T - S^T W^T)
+  //   C1b (O = S^T Q'^T)  P1 (W^T, U^T)  P0 ([K;Q] K^T)
+  else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_KQ = idesc_f16(128, kC, false, false, !F16);
+      constexpr uint32_t ID_WT = idesc_f16(DK, kC, true, false, !F16);
+      constexpr uint32_t ID_UT = idesc_f16(DV, kC, true, false, !F16);
+      constexpr uint32_t ID_VN = idesc_f16(DV, kC, false, true, !F16, true);   // -S^T W^T
+      constexpr uint32_t ID_O1 = idesc_f16(DV, kC, false, false, !F16);        //  S^T Q'^T
+      constexpr uint32_t ID_S = idesc_f16(DV, DK, false, true, !F16);          // (Vn g) K
+      constexpr uint32_t ID_O2 = idesc_f16(DV, kC, false, false, !F16);        //  Vn^T Aqk^T
+      const uint32_t t_sm = tmem + L::T_SM, t_sa = tmem + L::T_SA, t_o = tmem + L::T_O,
+                     t_kq = tmem + L::T_KQ, t_rw = tmem + L::T_RW;
+      const uint32_t s_tp = smem_u32(sm + L::OFF_TP), s_tpp = smem_u32(sm + L::OFF_TPP);
+      const uint32_t s_vnt = smem_u32(sm + L::OFF_VNT), s_wt = smem_u32(sm + L::OFF_WT);
+      const uint32_t s_sa = smem_u32(sm + L::OFF_SA);
+      auto a_desc_sa = [&](int ks) {  // smem S^T (K-major, DV rows x DK)
+        return sdesc_sw128(s_sa + (ks >> 2) * (DV * 128) + (ks & 3) * 32, 16, 1024);
+      };
+      auto t_vn = [&](int c) { return tmem + ((c & 1) ? L::T_VN1 : L::T_VN0); };
+      int cp0 = 0, cp1 = 0, c1a = 0, c1b = 0, c2 = 0;
+      uint64_t t_last = globaltimer_ns();
+      while (c2 < nc) {
+        bool prog = false;
+        // ---- C2(c2): needs Vn^T operands (scan) ----
+        if (c2 < c1b && mbar_test_wait(&bars[B_VNREADY], c2 & 1)) {
+          tc_fence_after();
+          trace_mark(P, c2, TR_MMA_C2);
+          const uint32_t kq = smem_u32(stage(c2) + L::OFF_KQ);
+          const uint32_t aq = smem_u32(aqk(c2));
+          // fast chunks carry V_new*gamma in the Vn^T tile itself; slow chunks in the
+          // (then free) W^T tile
+          const bool fastc = reinterpret_cast<const int*>(misc(c2))[L::M_FAST / 4] != 0;
+          const uint32_t s_vs = fastc ? s_vnt : s_wt;
+#pragma unroll
+          for (int ks = 0; ks < kC / 16; ++ks)
+            umma_ss(t_sm, sdesc_sw128(s_vs + ks * 32, 16, 1024),
+                    sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
+          umma_commit(&bars[B_SFULL]);
+#pragma unroll
+          for (int ks = 0; ks < kC / 16; ++ks)
+            umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024),
+                    sdesc_sw128(aq + ks * 32, 16, 1024), ID_O2, 1);
+          umma_commit(&bars[B_OFULL]);
+          umma_commit(&bars[B_EMPTY0 + (c2 % 3)]);
+          ++c2;
+          prog = true;
+        }
+        // ---- C1a(c1a): needs S^T_c (scan) and W^T_c (prep) ----
+        if (c1a < cp1 && c1a == c2 && mbar_test_wait(&bars[B_SREADY], c1a & 1) &&
+            mbar_test_wait(&bars[B_WREADY], c1a & 1)) {
+          tc_fence_after();
+          trace_mark(P, c1a, TR_MMA_C1);
+#pragma unroll
+          for (int ks = 0; ks < DK / 16; ++ks) {
+            const uint64_t bd = sdesc_sw128(s_wt + ks * 2048, DK * 128, 1024);
+            if constexpr (L::SA_TMEM) umma_ts(t_vn(c1a), t_sa + ks * 8, bd, ID_VN, 1);
+            else umma_ss(t_vn(c1a), a_desc_sa(ks), bd, ID_VN, 1);
+          }
+          umma_commit(&bars[B_VNFULL]);
+          ++c1a;
+          prog = true;
+        }
+        // ---- C1b(c1b): O = S^T Q'^T once the previous output was read ----
+        if (c1b < c1a && (c1b == 0 || mbar_test_wait(&bars[B_OFREE], (c1b - 1) & 1))) {
+          tc_fence_after();
+          const uint32_t kq = smem_u32(stage(c1b) + L::OFF_KQ);
+#pragma unroll
+          for (int ks = 0; ks < DK / 16; ++ks) {
+            const uint64_t bd =
+                sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + kC * 128 + (ks & 3) * 32, 16, 1024);
+            if constexpr (L::SA_TMEM) umma_ts(t_o, t_sa + ks * 8, bd, ID_O1, ks > 0);
+            else umma_ss(t_o, a_desc_sa(ks), bd, ID_O1, ks > 0);
+          }
+          ++c1b;
+          prog = true;
+        }
+        // ---- P1(cp1): W^T = K^T T'^T -> RW ; U^T = V^T T''^T -> VN[cp1&1] ----
+        if (cp1 < cp0 && mbar_test_wait(&bars[B_TREADY], cp1 & 1) &&
+            mbar_test_wait(&bars[B_VFULL0 + (cp1 & 1)], (cp1 >> 1) & 1) &&
+            (cp1 < 2 || mbar_test_wait(&bars[B_VNFREE0 + (cp1 & 1)], ((cp1 >> 1) + 1) & 1)) &&
+            (cp1 == 0 || mbar_test_wait(&bars[B_RWFREE], (cp1 - 1) & 1))) {
+          tc_fence_after();
+          const uint32_t kq = smem_u32(stage(cp1) + L::OFF_KQ);
+          const uint32_t vt = smem_u32(vstage(cp1));
+#pragma unroll
+          for (int ks = 0; ks < kC / 16; ++ks) {
+            umma_ss(t_rw, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024),
+                    sdesc_sw128(s_tp + ks * 32, 16, 1024), ID_WT, ks > 0);
+            umma_ss(t_vn(cp1), sdesc_sw128(vt + ks * 2048, L::V_REGION, 1024),
+                    sdesc_sw128(s_tpp + ks * 32, 16, 1024), ID_UT, ks > 0);
+          }
+          umma_commit(&bars[B_WUFULL]);
+          umma_commit(&bars[B_VEMPTY0 + (cp1 & 1)]);
+          ++cp1;
+          prog = true;
+        }
+        // ---- P0(cp0): [K;Q] K^T -> KQ ----
+        if (cp0 < nc && cp0 <= cp1 + 1 &&
+            mbar_test_wait(&bars[B_FULL0 + (cp0 % 3)], in_par(cp0)) &&
+            (cp0 == 0 || mbar_test_wait(&bars[B_KQFREE], (cp0 - 1) & 1))) {
+          tc_fence_after();
+          const uint32_t kq = smem_u32(stage(cp0) + L::OFF_KQ);
+#pragma unroll
+          for (int ks = 0; ks < DK / 16; ++ks) {
+            const uint32_t a = kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32;
+            umma_ss(t_kq, sdesc_sw128(a, 16, 1024), sdesc_sw128(a, 16, 1024), ID_KQ, ks > 0);
+          }
+          umma_commit(&bars[B_KQFULL]);
+          ++cp0;
+          prog = true;
+        }
+        if (prog) {
+          t_last = globaltimer_ns();
+        } else {
+          __nanosleep(32);
+          if (abort_flag) break;
+          if (globaltimer_ns() - t_last > kWaitTimeoutNs) {
+            abort_flag = 1;
+            atomicCAS(P.status, 0, 10);
+            break;
+          }
+        }
+      }
+      umma_commit(&bars[B_DONE]);
+    }
+  }
+  // =============================================================== PREP ====
+  // 256 threads: warps 4-11. Warp quadrant q = warp & 3 selects TMEM lanes 32q..32q+31
+  // (row r = 32q + lane); column half gh = (warp - 4) >> 2 selects tile columns
+  // [32 gh, 32 gh + 32). Software-pipelined over chunks:
+  //   E(c): coefficients, [K;Q]K^T epilogue -> A (fp32 workspace) and Aqk (bf16 tile)
+  //   I(c): (I + A)^-1, Q' = Q e^g, T' and T''            -> UMMA W^T, U^T
+  //   R(c): W^T readout                                    -> chain of chunk c
+  // in the order E(0), [I(c), E(c+1), R(c)] so the two UMMA latencies hide behind E.
+  else if (warp >= 4 && warp < 12) {
+    const int p = tid - 128, q = warp & 3, gh = (warp - 4) >> 2, l = lane;
+    const int r = 32 * q + l;
+    float* Aw = reinterpret_cast<float*>(sm + L::OFF_AW);
+    float* Xs = reinterpret_cast<float*>(sm + L::OFF_TP);
+    unsigned char* s_tp = sm + L::OFF_TP;
+    unsigned char* s_tpp = sm + L::OFF_TPP;
+    const uint32_t lane_off = (32u * q) << 16;
+    const uint32_t t_kq = tmem + L::T_KQ + lane_off + 32 * gh;
+    const uint32_t t_rw = tmem + L::T_RW + lane_off + 32 * gh;
+
+    auto stage_E = [&](int c) {
+      unsigned char* st = stage(c);
+      float* ms = misc(c);
+      const float* gcum = ms + L::M_GCUM / 4;
+      sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 20);
+      if (p == 0) trace_mark(P, c, TR_PREP_FULL);
+      // ---- per-token coefficients (warp 4: tokens 2l, 2l+1) ----
+      if (warp == 4) {
+        float g0 = 0.f, g1 = 0.f;
+        if (P.gate_mode != PTOF_GATE_NONE) {
+          g0 = ms[L::M_GRAW / 4 + 2 * l];
+          g1 = ms[L::M_GRAW / 4 + 2 * l + 1];
+        }
+        bool mono = true;  // the chunk-local cumsum never increases
+        if (P.gate_mode == PTOF_GATE_RAW) {
+          mono = (g1 <= 0.f) && (l == 0 || g0 <= 0.f);
+          g1 += g0;
+          float run = g1;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, run, o);
+            if (l >= o) run += y;
+          }
+          g0 += run - g1;
+          g1 = run;
+        } else if (P.gate_mode == PTOF_GATE_CUMSUM) {
+          const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
+          mono = (g1 <= g0) && (l == 0 || g0 <= prev);
+        }
+        const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
+        const float gl = __shfl_sync(0xffffffffu, g1, 31);
+        // exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j): overflow-free when the chunk's
+        // total decay is below 80 and the cumsum is monotone; otherwise the exact form
+        const bool fast = !F16 && __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
+        float b0, b1;
+        if (P.gs_t == 1 && P.beta_dtype != PTOF_F32) {
+          const uint32_t u = reinterpret_cast<const uint32_t*>(st + L::OFF_MISC + L::M_BRAW)[l];
+          const float2 f = (P.beta_dtype == PTOF_F16) ? unpack_f16(u) : unpack_bf16(u);
+          b0 = f.x; b1 = f.y;
+        } else {
+          const float* bf = reinterpret_cast<const float*>(st + L::OFF_MISC + L::M_BRAW);
+          b0 = bf[2 * l]; b1 = bf[2 * l + 1];
+        }
+        const float e0 = __expf(g0), e1 = __expf(g1);
+        const float rf0 = __expf(g0 - gfirst), rf1 = __expf(g1 - gfirst);
+        float2* m2 = reinterpret_cast<float2*>(ms);
+        m2[L::M_GCUM / 8 + l] = make_float2(g0, g1);
+        m2[L::M_EG / 8 + l] = make_float2(e0, e1);
+        m2[L::M_BK / 8 + l] = make_float2(b0 * e0, b1 * e1);
+        m2[L::M_BV / 8 + l] = make_float2(b0, b1);
+        m2[L::M_GAM / 8 + l] = make_float2(__expf(gl - g0), __expf(gl - g1));
+        m2[L::M_ROWF / 8 + l] = make_float2(rf0, rf1);
+        m2[L::M_ROWFB / 8 + l] = make_float2(rf0 * b0, rf1 * b1);
+        m2[L::M_COLF / 8 + l] = make_float2(__expf(gfirst - g0), __expf(gfirst - g1));
+        if (l == 0) {
+          ms[L::M_EGL / 4] = __expf(gl);
+          ms[L::M_ENGL / 4] = fast ? __expf(-gl) : 0.f;
+          reinterpret_cast<int*>(ms)[L::M_FAST / 4] = fast ? 1 : 0;
+        }
+      }
+      named_bar_sync(kPrepBar, kPrepThreads);
+      if (p == 0) mbar_arrive(&bars[B_GREADY0 + (c % 3)]);
+      const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
+      // ---- A = gated strict-lower KK^T (rows 0-63), Aqk = gated causal QK^T (64-127) ----
+      // the Aqk buffer of chunk c last fed chunk c-2's output UMMA
+      if (c >= 2) sy.wait(&bars[B_OFULL], c & 1, 23);
+      sy.wait(&bars[B_KQFULL], c & 1, 21);
+      tc_fence_after();
+      if (p == 0) trace_mark(P, c, TR_PREP_KQ);
+      float v[32];
+      {
+        float a0[16], a1[16];
+        tmem_ld16(t_kq, a0);
+        tmem_ld16(t_kq + 16, a1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int m = 0; m < 16; ++m) { v[m] = a0[m]; v[16 + m] = a1[m]; }
+      }
+      tc_fence_before();
+      const int i = r & 63, j0 = 32 * gh;
+      const bool is_k = r < 64;
+      const float* colf = ms + L::M_COLF / 4 + j0;
+      if (P.knockout & 2) {
+      } else if (fast && is_k) {
+        const float rf = ms[L::M_ROWFB / 4 + i];
+#pragma unroll
+        for (int m = 0; m < 32; ++m) v[m] = (j0 + m < i) ? v[m] * rf * colf[m] : 0.f;
+      } else if (fast) {
+        // fast chunks: O^T = e^g (S^T Q^T + e^{-gl} (Vn g)^T QK_causal^T), the e^g applied
+        // at the output, so the score only needs the causal mask and one scale
+        const float eng = ms[L::M_ENGL / 4];
+#pragma unroll
+        for (int m = 0; m < 32; ++m) v[m] = (j0 + m <= i) ? v[m] * eng : 0.f;
+      } else {
+        const float gi = gcum[i], bi = ms[L::M_BV / 4 + i];
+#pragma unroll
+        for (int m = 0; m < 32; ++m) {
+          const int j = j0 + m;
+          const float cf = is_k ? bi * kkt_coef(gi, gcum[j]) : qk_coef(gi, gcum[j]);
+          v[m] = (j < (is_k ? i : i + 1)) ? v[m] * cf : 0.f;
+        }
+      }
+      if (is_k) {
+        float4* dst = reinterpret_cast<float4*>(Aw + i * L::AW_LD + j0);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) dst[m] = make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
+      } else {
+        uint32_t pk[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) pk[m] = pack2<F16>(v[2 * m], v[2 * m + 1]);
+        unsigned char* aq = aqk(c);
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch)
+          st_chunk(aq, i, j0 / 8 + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
+      }
+      named_bar_sync(kPrepBar, kPrepThreads);
+      if (p == 0) {
+        mbar_arrive(&bars[B_KQFREE]);
+        trace_mark(P, c, TR_PREP_EPI);
+      }
+    };
+
+    auto stage_I = [&](int c) {
+      unsigned char* st = stage(c);
+      float* ms = misc(c);
+      const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
+      // ---- level 0 (warps 4, 5: one column per thread) || Q' = Q e^g (warps 6-11) ----
+      if (warp < 6) {
+        float x[16];
+        const int b = p >> 4, j = p & 15;
+        if (!(P.knockout & 1)) diag16_col<L::AW_LD>(Aw, b, j, x);
+        named_bar_sync(3, 64);
+        if (!(P.knockout & 1)) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) Aw[(16 * b + i) * L::AW_LD + 16 * b + j] = x[i];
+        }
+      } else if (!fast) {
+        const int pq = p - 64;  // 0..191
+        const float* eg = ms + L::M_EG / 4;
+        constexpr int NCH = DK / 8;
+        for (int idx = pq; idx < kC * NCH; idx += 192) {
+          const int i = idx / NCH, ch = idx % NCH;
+          unsigned char* reg = st + L::OFF_KQ + (ch >> 3) * L::KQ_REGION + kC * 128;
+          uint4 u = ld_chunk(reg, i, ch & 7);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+          const float e = eg[i];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const float2 f = unpack2<F16>(w[m]);
+            w[m] = pack2<F16>(f.x * e, f.y * e);
+          }
+          st_chunk(reg, i, ch & 7, u);
+        }
+      }
+      named_bar_sync(kPrepBar, kPrepThreads);
+      // ---- levels 1-2 ----
+      if (!(P.knockout & 1)) tri_inv64_merge<L::AW_LD, kPrepBar, kPrepThreads>(Aw, Xs, p);
+      if (p == 0) trace_mark(P, c, TR_PREP_INV);
+      // ---- T' = T * (beta e^g)_j, T'' = T * beta_j (K-major B operands) ----
+      {
+        const int i = p >> 2, j0 = (p & 3) * 16;
+        const float4* trow = reinterpret_cast<const float4*>(Aw + i * L::AW_LD + j0);
+        const float4* bk = reinterpret_cast<const float4*>(ms + L::M_BK / 4 + j0);
+        const float4* bv = reinterpret_cast<const float4*>(ms + L::M_BV / 4 + j0);
+        // fast chunks: rows scaled by gamma_i so the UMMAs yield W^T g and U^T g
+        const float gi = fast ? ms[L::M_GAM / 4 + i] : 1.f;
+        uint32_t a[8], bb[8];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          float4 t = trow[m];
+          t.x *= gi; t.y *= gi; t.z *= gi; t.w *= gi;
+          const float4 k4 = bk[m], v4 = bv[m];
+          a[2 * m] = pack2<F16>(t.x * k4.x, t.y * k4.y);
+          a[2 * m + 1] = pack2<F16>(t.z * k4.z, t.w * k4.w);
+          bb[2 * m] = pack2<F16>(t.x * v4.x, t.y * v4.y);
+          bb[2 * m + 1] = pack2<F16>(t.z * v4.z, t.w * v4.w);
+        }
+        st_chunk(s_tp, i, j0 / 8, make_uint4(a[0], a[1], a[2], a[3]));
+        st_chunk(s_tp, i, j0 / 8 + 1, make_uint4(a[4], a[5], a[6], a[7]));
+        st_chunk(s_tpp, i, j0 / 8, make_uint4(bb[0], bb[1], bb[2], bb[3]));
+        st_chunk(s_tpp, i, j0 / 8 + 1, make_uint4(bb[4], bb[5], bb[6], bb[7]));
+      }
+      fence_async_smem();
+      named_bar_sync(kPrepBar, kPrepThreads);
+      if (p == 0) {
+        mbar_arrive(&bars[B_TREADY]);
+        trace_mark(P, c, TR_PREP_TREADY);
+      }
+    };
+
+    auto stage_R = [&](int c) {
+      sy.wait(&bars[B_WUFULL], c & 1, 22);
+      // the single W^T tile: chunk c-1's UMMAs (and its slow-path V_new*gamma) are done
+      if (c >= 1) sy.wait(&bars[B_SFULL], (c - 1) & 1, 24);
+      tc_fence_after();
+      if (p == 0) trace_mark(P, c, TR_PREP_WU);
+      const int d = (DK == 128) ? r : (l < 16 ? 16 * q + l : -1);
+      float a0[16], a1[16];
+      tmem_ld16(t_rw, a0);
+      tmem_ld16(t_rw + 16, a1);
+      tmem_wait_ld();
+      if (d >= 0) {
+        unsigned char* wt = sm + L::OFF_WT;
+        uint32_t pk[16];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
+          pk[8 + m] = pack2<F16>(a1[2 * m], a1[2 * m + 1]);
+        }
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch)
+          st_chunk(wt, d, 4 * gh + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
+      }
+      tc_fence_before();
+      fence_async_smem();
+      named_bar_sync(kPrepBar, kPrepThreads);
+      if (p == 0) {
+        mbar_arrive(&bars[B_WREADY]);
+        mbar_arrive(&bars[B_RWFREE]);
+        trace_mark(P, c, TR_PREP_END);
+      }
+    };
+
+    stage_E(0);
+    for (int c = 0; c < nc; ++c) {
+      stage_I(c);
+      if (c + 1 < nc) stage_E(c + 1);
+      stage_R(c);
+    }
+  }
+  // =============================================================== SCAN ====
+  else if (warp >= 12) {
+    const int s = tid - 384, q = warp & 3, l = lane;
+    const int v = (DV == 128) ? (32 * q + l) : (l < 16 ? 16 * q + l : -1);
+    const uint32_t lane_off = (32u * q) << 16;
+    const uint32_t t_sm = tmem + L::T_SM + lane_off, t_sa = tmem + L::T_SA + lane_off;
+    const uint32_t t_o = tmem + L::T_O + lane_off;
+    unsigned char* s_vnt = sm + L::OFF_VNT;
+    unsigned char* s_vng = sm + L::OFF_WT;   // slow chunks: V_new*gamma in the free W^T tile
+    unsigned char* s_sa = sm + L::OFF_SA;
+    (void)s_sa;
+    float* osc = reinterpret_cast<float*>(sm + L::OFF_OSC);
+    const int64_t sbase = static_cast<int64_t>(bh) * DK * DV;
+    TO* obase = static_cast<TO*>(P.o) + b * P.os_b + h * P.os_h;
+
+    // smem variant of the bf16 S^T copy (K-major A operand, rows v, DK columns)
+    auto put_sa = [&](int d0, const float (&x)[16]) {
+      if (v >= 0) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(x[2 * m], x[2 * m + 1]);
+        unsigned char* reg = s_sa + (d0 >> 6) * (DV * 128);
+        st_chunk(reg, v, (d0 & 63) / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+        st_chunk(reg, v, (d0 & 63) / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
+      }
+    };
+    // One pass over S^T row v in 32-column pieces: optional source (global S0),
+    // bf16 copy -> SA, then master <- scale * value.
+    auto state_pass = [&](bool from_global, float mult, float* final_out) {
+#pragma unroll 1
+      for (int d0 = 0; d0 < DK; d0 += 32) {
+        float x[32];
+        if (from_global) {
+#pragma unroll
+          for (int m = 0; m < 32; ++m)
+            x[m] = (P.S0 && v >= 0) ? P.S0[sbase + static_cast<int64_t>(d0 + m) * DV + v] : 0.f;
+        } else {
+          float a[16], bq[16];
+          tmem_ld16(t_sm + d0, a);
+          tmem_ld16(t_sm + d0 + 16, bq);
+          tmem_wait_ld();
+#pragma unroll
+          for (int m = 0; m < 16; ++m) { x[m] = a[m]; x[16 + m] = bq[m]; }
+        }
+        if (final_out) {
+          if (v >= 0) {
+#pragma unroll
+            for (int m = 0; m < 32; ++m) final_out[sbase + static_cast<int64_t>(d0 + m) * DV + v] = x[m];
+          }
+          continue;
+        }
+        if constexpr (L::SA_TMEM) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int m = 0; m < 16; ++m) pk[m] = pack2<F16>(x[2 * m], x[2 * m + 1]);
+          tmem_st16(t_sa + d0 / 2, pk);
+        } else {
+          float lo[16], hi[16];
+#pragma unroll
+          for (int m = 0; m < 16; ++m) { lo[m] = x[m]; hi[m] = x[16 + m]; }
+          put_sa(d0, lo);
+          put_sa(d0 + 16, hi);
+        }
+        float y0[16], y1[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) { y0[m] = x[m] * mult; y1[m] = x[16 + m] * mult; }
+        tmem_st16f(t_sm + d0, y0);
+        tmem_st16f(t_sm + d0 + 16, y1);
+      }
+      tmem_wait_st();
+    };
+
+    // initial state: S^T <- S0 (or 0), master pre-scaled by e^{g_last} of chunk 0
+    sy.wait(&bars[B_GREADY0], 0, 30);  // chunk 0
+    state_pass(true, misc(0)[L::M_EGL / 4], nullptr);
+    tc_fence_before();
+    if (!L::SA_TMEM) fence_async_smem();
+    named_bar_sync(kScanBar, 128);
+    if (s == 0) mbar_arrive(&bars[B_SREADY]);
+
+    for (int c = 0; c < nc; ++c) {
+      const float* ms = misc(c);
+      // ---- (a) V_new^T row v -> bf16 A operands Vn^T and Vn^T*gamma ----
+      sy.wait(&bars[B_VNFULL], c & 1, 31);
+      tc_fence_after();
+      if (s == 0) trace_mark(P, c, TR_SCAN_VNFULL);
+      const bool fastc = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
+      if (s < kC) osc[s] = fastc ? P.scale * ms[L::M_EG / 4 + s] : P.scale;
+      {
+        const uint32_t t_vn = tmem + ((c & 1) ? L::T_VN1 : L::T_VN0) + lane_off;
+        const float* gam = ms + L::M_GAM / 4;
+#pragma unroll
+        for (int c0 = 0; c0 < kC; c0 += 16) {
+          float x[16];
+          tmem_ld16(t_vn + c0, x);
+          tmem_wait_ld();
+          if (v >= 0) {
+            uint32_t a[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) a[m] = pack2<F16>(x[2 * m], x[2 * m + 1]);
+            st_chunk(s_vnt, v, c0 / 8, make_uint4(a[0], a[1], a[2], a[3]));
+            st_chunk(s_vnt, v, c0 / 8 + 1, make_uint4(a[4], a[5], a[6], a[7]));
+            if (!fastc) {
+              uint32_t gq[8];
+#pragma unroll
+              for (int m = 0; m < 8; ++m)
+                gq[m] = pack2<F16>(x[2 * m] * gam[c0 + 2 * m], x[2 * m + 1] * gam[c0 + 2 * m + 1]);
+              st_chunk(s_vng, v, c0 / 8, make_uint4(gq[0], gq[1], gq[2], gq[3]));
+              st_chunk(s_vng, v, c0 / 8 + 1, make_uint4(gq[4], gq[5], gq[6], gq[7]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      fence_async_smem();
+      named_bar_sync(kScanBar, 128);
+      if (s == 0) {
+        mbar_arrive(&bars[B_VNREADY]);
+        trace_mark(P, c, TR_SCAN_VNREADY);
+        mbar_arrive(&bars[B_VNFREE0 + (c & 1)]);
+        mbar_arrive(&bars[B_EMPTY0 + (c % 3)]);
+      }
+      // ---- (b) state: S^T_{c+1} ready -> bf16 copy, pre-scale by e^{gl_{c+1}} ----
+      sy.wait(&bars[B_SFULL], c & 1, 32);
+      tc_fence_after();
+      if (s == 0) trace_mark(P, c, TR_SCAN_SFULL);
+      if (c + 1 < nc) {
+        sy.wait(&bars[B_GREADY0 + ((c + 1) % 3)], in_par(c + 1), 33);
+        state_pass(false, misc(c + 1)[L::M_EGL / 4], nullptr);
+        tc_fence_before();
+        if (!L::SA_TMEM) fence_async_smem();
+        named_bar_sync(kScanBar, 128);
+        if (s == 0) {
+          mbar_arrive(&bars[B_SREADY]);
+          trace_mark(P, c, TR_SCAN_SREADY);
+        }
+      } else if (P.S_final) {
+        state_pass(false, 1.f, P.S_final);
+      }
+      // ---- (c) output: O^T row v -> o[t0 + i, v] ----
+      sy.wait(&bars[B_OFULL], c & 1, 34);
+      tc_fence_after();
+      if (s == 0) trace_mark(P, c, TR_SCAN_OFULL);
+      {
+        const int t0 = c * kC;
+#pragma unroll
+        for (int c0 = 0; c0 < kC; c0 += 16) {
+          float x[16];
+          tmem_ld16(t_o + c0, x);
+          tmem_wait_ld();
+          if (v >= 0) {
+#pragma unroll
+            for (int m = 0; m < 16; ++m)
+              obase[static_cast<int64_t>(t0 + c0 + m) * P.os_t + v] = from_f32<TO>(x[m] * osc[c0 + m]);
+          }
+        }
+      }
+      tc_fence_before();
+      named_bar_sync(kScanBar, 128);
+      if (s == 0) {
+        mbar_arrive(&bars[B_OFREE]);
+        trace_mark(P, c, TR_SCAN_END);
+      }
+    }
+  }
+
+  // ============================================================ teardown ====
+  if (warp == 1 && lane == 0) {
+    // every UMMA has retired before TMEM is released (bounded, even after an abort)
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&bars[B_DONE], 0) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
+    }
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, L::T_COLS);
+}
+
+}  // namespace tcfwd
+
+// ------------------------------------------------------------------- host ----
+namespace {
+
+// 3D TMA map over a [.., D]-innermost activation so that one box is 64 tokens x 64
+// features of one (batch, head): heads-outer layout -> dims {D, T, B*H};
+// token-major layout -> dims {D, H, B*T}.
+int make_act_map(CUtensorMap* m, const void* base, int dt, const ptof_gdn_params& p, int D) {
+  const CUtensorMapDataType t =
+      dt == PTOF_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  uint64_t dims[3], strides[2];
+  uint32_t box[3];
+  if (p.layout == PTOF_LAYOUT_BHTD) {
+    dims[0] = D; dims[1] = p.T; dims[2] = static_cast<uint64_t>(p.B) * p.H;
+    strides[0] = static_cast<uint64_t>(D) * 2;
+    strides[1] = static_cast<uint64_t>(p.T) * D * 2;
+    box[0] = 64; box[1] = 64; box[2] = 1;
+  } else {
+    dims[0] = D; dims[1] = p.H; dims[2] = static_cast<uint64_t>(p.B) * p.T;
+    strides[0] = static_cast<uint64_t>(D) * 2;
+    strides[1] = static_cast<uint64_t>(p.H) * D * 2;
+    box[0] = 64; box[1] = 1; box[2] = 64;
+  }
+  return make_tmap_3d(m, base, t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int DK, int DV, bool F16, typename TO>
+int launch_t(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
+             const float* g, const float* S0, void* o, float* S_final, cudaStream_t stream) {
+  using L = tcfwd::Layout<DK, DV>;
+  const ptof_gdn_params& p = w->p;
+  tcfwd::Params P;
+  int rc = make_act_map(&P.mapK, k, p.in_dtype, p, DK);
+  if (!rc) rc = make_act_map(&P.mapQ, q, p.in_dtype, p, DK);
+  if (!rc) rc = make_act_map(&P.mapV, v, p.in_dtype, p, DV);
+  if (rc) return rc;
+  P.g = (p.gate_mode == PTOF_GATE_NONE) ? nullptr : g;
+  P.beta = beta;
+  P.S0 = S0;
+  P.o = o;
+  P.S_final = S_final;
+  P.status = w->d_status;
+  P.trace = static_cast<unsigned long long*>(w->trace);
+  P.trace_chunks = w->trace_chunks;
+  {
+    const char* ko = getenv("PTOF_KNOCKOUT");
+    P.knockout = ko ? atoi(ko) : 0;
+  }
+  P.B = p.B; P.H = p.H; P.T = p.T; P.nc = p.T / kChunk;
+  P.gate_mode = p.gate_mode;
+  P.beta_dtype = p.beta_dtype;
+  P.layout = p.layout;
+  const Strides3 sg = make_strides3(p.layout, p.H, p.T);
+  const Strides4 so = make_strides4(p.layout, p.H, p.T, DV);
+  P.gs_b = sg.b; P.gs_h = sg.h; P.gs_t = sg.t;
+  P.os_b = so.b; P.os_h = so.h; P.os_t = so.t;
+  P.scale = p.scale;
+  auto kern = tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_tc smem attribute");
+  kern<<<p.B * p.H, tcfwd::kThreads, L::BYTES, stream>>>(P);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "gdn_fwd_tc launch");
+}
+
+template <int DK, int DV, bool F16>
+int launch_o(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
+             const float* g, const float* S0, void* o, float* S_final, cudaStream_t st) {
+  switch (w->p.out_dtype) {
+    case PTOF_F32: return launch_t<DK, DV, F16, float>(w, q, k, v, beta, g, S0, o, S_final, st);
+    case PTOF_F16: return launch_t<DK, DV, F16, __half>(w, q, k, v, beta, g, S0, o, S_final, st);
+    default: return launch_t<DK, DV, F16, __nv_bfloat16>(w, q, k, v, beta, g, S0, o, S_final, st);
+  }
+}
+
+template <int DK, int DV>
+int launch_d(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
+             const float* g, const float* S0, void* o, float* S_final, cudaStream_t st) {
+  if (w->p.in_dtype == PTOF_F16) return launch_o<DK, DV, true>(w, q, k, v, beta, g, S0, o, S_final, st);
+  return launch_o<DK, DV, false>(w, q, k, v, beta, g, S0, o, S_final, st);
+}
+
+}  // namespace
+
+bool gdn_fwd_tc_supports(const ptof_gdn_params& p) {
+  if (p.in_dtype != PTOF_F16 && p.in_dtype != PTOF_BF16) return false;
+  if (p.C != kChunk) return false;
+  return (p.Dk == 128 && p.Dv == 128) || (p.Dk == 64 && p.Dv == 64);
+}
+
+int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
+                      const float* g, const float* S0, void* o, float* S_final,
+                      cudaStream_t stream) {
+  const ptof_gdn_params& p = w->p;
+  if (p.Dk == 128) return launch_d<128, 128>(w, q, k, v, beta, g, S0, o, S_final, stream);
+  return launch_d<64, 64>(w, q, k, v, beta, g, S0, o, S_final, stream);
+}
+
 }  // namespace ptof

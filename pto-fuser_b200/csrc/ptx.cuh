@@ -66,15 +66,52 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of phase `parity` (returns immediately).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+#ifndef PTOF_SPIN_MODE
+#define PTOF_SPIN_MODE 1
+#endif
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or
+// `hint_ns` elapses, so waiting warps do not compete for issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on phase `parity` of `bar`. Returns false (and raises the abort
 // flag, recording `site` in *status) when the wait gives up, or immediately when
 // another thread of the CTA already aborted.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                       int* status, int site) {
-  if (mbar_try_wait(bar, parity)) return true;
+static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, int* status, int site) {
   const uint64_t t0 = globaltimer_ns();
   while (true) {
+#if PTOF_SPIN_MODE == 0
     if (mbar_try_wait(bar, parity)) return true;
+#elif PTOF_SPIN_MODE == 1
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+#else
+    for (int i = 0; i < 64; ++i) {
+      if (mbar_try_wait(bar, parity)) return true;
+      __nanosleep(64);
+    }
+#endif
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1;

@@ -49,6 +49,7 @@ _SIGNATURES = {
     "ptof_gdn_fwd_exec": (_i32, [_vp] * 10),
     "ptof_gdn_fwd_teardown": (None, [_vp]),
     "ptof_check_status": (_i32, [_vp, _vp]),
+    "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),
     "ptof_last_error": (ctypes.c_char_p, []),
     "ptof_selftest_umma": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
     "ptof_selftest_tma": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
