@@ -64,11 +64,15 @@ struct Layout {
   // prep buffers
   static constexpr int OFF_TP = OFF_WT + DK * 128;   // T' bf16 [64 x 64] (also inverse scratch)
   static constexpr int OFF_TPP = OFF_TP + 8192;      // T''
-  static constexpr int AW_LD = 68;                   // fp32 row stride of the inverse workspace
-  static constexpr int OFF_AW = OFF_TPP + 8192;
-  static constexpr int AW_BYTES = ((kC * AW_LD * 4 + 1023) / 1024) * 1024;
+  // inverse workspace: fp16 tiles (128B-swizzled, 64 rows x 64) of A and of the
+  // block-diagonal partial inverse D, plus the fp32 16x16 diagonal blocks of A
+  static constexpr int OFF_TA = OFF_TPP + 8192;
+  static constexpr int OFF_TD = OFF_TA + 8192;
+  static constexpr int ADG_LD = 20;                  // fp32 row stride of a diagonal block
+  static constexpr int OFF_ADG = OFF_TD + 8192;
+  static constexpr int ADG_BYTES = 5120;             // 4 x 16 x 20 floats
   // chain buffers
-  static constexpr int OFF_VNT = OFF_AW + AW_BYTES;  // bf16 Vn^T [DV x 64]
+  static constexpr int OFF_VNT = OFF_ADG + ADG_BYTES;  // bf16 Vn^T [DV x 64]
   static constexpr int OFF_SA = OFF_VNT + DV * 128;  // bf16 S^T [DV x DK] (smem variant)
   static constexpr int SA_BYTES = SA_TMEM ? 0 : NKB * DV * 128;
   static constexpr int OFF_OSC = OFF_SA + SA_BYTES;  // fp32 [64] output multipliers (scan)
@@ -92,7 +96,7 @@ enum Bar {
   B_FULL0 = 0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_GREADY0, B_GREADY1, B_GREADY2,
   B_VFULL0, B_VFULL1, B_VEMPTY0, B_VEMPTY1, B_WREADY,
   B_KQFULL, B_TREADY, B_WUFULL, B_RWFREE, B_VNFREE0, B_VNFREE1, B_SREADY, B_VNFULL,
-  B_VNREADY, B_SFULL, B_OFULL, B_OFREE, B_DONE, B_KQFREE, B_COUNT
+  B_VNREADY, B_SFULL, B_OFULL, B_OFREE, B_DONE, B_KQFREE, B_INVREQ, B_INVDONE, B_O1DONE, B_COUNT
 };
 
 struct Params {
@@ -105,8 +109,8 @@ struct Params {
   int* status;
   unsigned long long* trace;       // optional [chunks x kTraceSlots] timestamps of CTA 0
   int trace_chunks;
-  int knockout;                    // cost-attribution knock-outs (results invalid): bit0 skip
-                                   // (I+A)^-1, bit1 skip the kkt/qk epilogue math
+  int knockout;                    // cost-attribution knock-out (results invalid): bit1 skips
+                                   // the kkt/qk epilogue math
   int B, H, T, nc;
   int gate_mode, beta_dtype, layout;
   int64_t gs_b, gs_h, gs_t;        // g / beta strides (elements)
@@ -131,7 +135,11 @@ struct Sync {
   volatile int* abort;
   int* status;
   __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, int site) const {
+#if PTOF_SPIN_MODE == 3
+    if (mbar_test_wait(bar, parity)) return true;
+#else
     if (mbar_try_wait(bar, parity)) return true;
+#endif
     return mbar_wait(bar, parity, abort, status, site);
   }
 };
@@ -160,17 +168,18 @@ __device__ __forceinline__ uint4 ld_chunk(const unsigned char* region, int row, 
 }
 
 // ------------------------------------------------------- (I + A)^-1, 64 x 64 ----
-// Blocked forward substitution for T = (I + A)^-1 (A strictly lower, fp32, in place in
-// Aw with row stride LD; zeros on and above the diagonal on entry).
-//
-// Level 0: the four 16x16 diagonal blocks, one column of T per thread (64 threads):
-// right-looking substitution, x_i -= A[i][k] x_k as soon as x_k is final, so the
-// dependency chain is 15 FMAs long and every A[i][k] load is independent of x.
-// Returns the column in x (x[i] = T[16b+i][16b+j]); the caller stores it after a
-// barrier (other columns still read A from the block).
+// T = (I + A)^-1 (A strictly lower) in two levels:
+//  level 0 (SIMT): the four 16x16 diagonal blocks T_bb, one column per thread,
+//    right-looking substitution (x_i -= A[i][k] x_k once x_k is final), so the
+//    dependency chain is 15 FMAs and every A load is independent of x;
+//  levels 1-2 (tensor cores, fp16 operands, fp32 accumulate): with D the block
+//    diagonal of already-inverted blocks, X = A D has X_IJ = A_IJ T_JJ and
+//    Y = D X has Y_IJ = T_II A_IJ T_JJ, so T_IJ = -Y_IJ for the blocks one level
+//    below the diagonal. Two rounds (16 -> 32 on blocks (1,0),(3,2), then 32 -> 64
+//    on the lower-left 32x32 block) = four 64x64x64 UMMAs.
+// blk: fp32 16x16 diagonal block of A, row stride LD. Returns column j of T_bb in x.
 template <int LD>
-__device__ __forceinline__ void diag16_col(const float* Aw, int b, int j, float (&x)[16]) {
-  const float* blk = Aw + 16 * b * LD + 16 * b;
+__device__ __forceinline__ void diag16_col(const float* blk, int j, float (&x)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;
 #pragma unroll
@@ -181,61 +190,10 @@ __device__ __forceinline__ void diag16_col(const float* Aw, int b, int j, float 
   }
 }
 
-// Levels 1-2 over 256 threads, in place on Aw (diagonal 16-blocks already hold T).
-// 16 -> 32: T21 = -T22 (A21 T11) for block pairs (1,0), (3,2);
-// 32 -> 64: T[32:64, 0:32] = -T_B (A_BA T_A). Loops run over full ranges: the zero
-// upper triangles of T11 / T22 / T_A / T_B make the extra terms vanish, and the
-// fixed trip counts let every load be issued ahead of its FMAs. X: >= 32 x 36 floats.
-template <int LD, int BAR, int NT>
-__device__ __forceinline__ void tri_inv64_merge(float* Aw, float* X, int p) {
-  static_assert(NT == 256, "merge mapping assumes 256 threads");
-  constexpr int XLD = 36;
-  {  // 16 -> 32: pair P = p >> 7; 2 outputs per thread
-    const int P = p >> 7, e = p & 127, r = e >> 3, c0 = (e & 7) * 2;
-    const int r1 = 32 * P + 16, c1 = 32 * P;
-    float2 xx = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float a = Aw[(r1 + r) * LD + c1 + k];
-      const float2 t = *reinterpret_cast<const float2*>(Aw + (c1 + k) * LD + c1 + c0);
-      xx = __ffma2_rn(make_float2(a, a), t, xx);
-    }
-    *reinterpret_cast<float2*>(X + (P * 16 + r) * XLD + c0) = xx;
-    named_bar_sync(BAR, NT);
-    float2 yy = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float a = Aw[(r1 + r) * LD + r1 + k];
-      const float2 t = *reinterpret_cast<const float2*>(X + (P * 16 + k) * XLD + c0);
-      yy = __ffma2_rn(make_float2(a, a), t, yy);
-    }
-    *reinterpret_cast<float2*>(Aw + (r1 + r) * LD + c1 + c0) = make_float2(-yy.x, -yy.y);
-  }
-  named_bar_sync(BAR, NT);
-  {  // 32 -> 64: 4 outputs per thread
-    const int r = p >> 3, c0 = (p & 7) * 4;
-    float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      const float a = Aw[(32 + r) * LD + k];
-      const float4 t = *reinterpret_cast<const float4*>(Aw + k * LD + c0);
-      lo = __ffma2_rn(make_float2(a, a), make_float2(t.x, t.y), lo);
-      hi = __ffma2_rn(make_float2(a, a), make_float2(t.z, t.w), hi);
-    }
-    *reinterpret_cast<float4*>(X + r * XLD + c0) = make_float4(lo.x, lo.y, hi.x, hi.y);
-    named_bar_sync(BAR, NT);
-    float2 ylo = make_float2(0.f, 0.f), yhi = make_float2(0.f, 0.f);
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      const float a = Aw[(32 + r) * LD + 32 + k];
-      const float4 x = *reinterpret_cast<const float4*>(X + k * XLD + c0);
-      ylo = __ffma2_rn(make_float2(a, a), make_float2(x.x, x.y), ylo);
-      yhi = __ffma2_rn(make_float2(a, a), make_float2(x.z, x.w), yhi);
-    }
-    // A_BA (read only before the previous barrier) is overwritten by T_BA
-    *reinterpret_cast<float4*>(Aw + (32 + r) * LD + c0) = make_float4(-ylo.x, -ylo.y, -yhi.x, -yhi.y);
-  }
-  named_bar_sync(BAR, NT);
+// 16-bit element (row, col) of a 64-column 128B-swizzled tile
+__device__ __forceinline__ __half* tile_elem(unsigned char* tile, int row, int col) {
+  return reinterpret_cast<__half*>(tile + row * 128 + ((((col >> 3) ^ (row & 7)) << 4) |
+                                                       ((col & 7) << 1)));
 }
 
 // ------------------------------------------------------------------ kernel ----
@@ -257,7 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   if (tid == 0) {
     abort_flag = 0;
     for (int i = 0; i < B_COUNT; ++i) mbar_init(&bars[i], 1);
-    for (int i = 0; i < 3; ++i) mbar_init(&bars[B_EMPTY0 + i], 2);
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[B_EMPTY0 + i], 3);  // 2 issuers + scan
+    mbar_init(&bars[B_DONE], 3);  // the three UMMA issuers
     fence_mbar_init();
   }
   if (warp == 2) {
@@ -334,134 +293,135 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     }
   }
   // ================================================================ MMA ====
-  // One thread issues every UMMA. Five in-order streams, polled without blocking,
-  // chain work first:
-  //   C2 (S^T += (Vn^T g) K ; O += Vn^T Aqk^T)  C1a (Vn^T = U^T - S^T W^T)
-  //   C1b (O = S^T Q'^T)  P1 (W^T, U^T)  P0 ([K;Q] K^T)
-  else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t ID_KQ = idesc_f16(128, kC, false, false, !F16);
-      constexpr uint32_t ID_WT = idesc_f16(DK, kC, true, false, !F16);
-      constexpr uint32_t ID_UT = idesc_f16(DV, kC, true, false, !F16);
-      constexpr uint32_t ID_VN = idesc_f16(DV, kC, false, true, !F16, true);   // -S^T W^T
-      constexpr uint32_t ID_O1 = idesc_f16(DV, kC, false, false, !F16);        //  S^T Q'^T
-      constexpr uint32_t ID_S = idesc_f16(DV, DK, false, true, !F16);          // (Vn g) K
-      constexpr uint32_t ID_O2 = idesc_f16(DV, kC, false, false, !F16);        //  Vn^T Aqk^T
-      const uint32_t t_sm = tmem + L::T_SM, t_sa = tmem + L::T_SA, t_o = tmem + L::T_O,
-                     t_kq = tmem + L::T_KQ, t_rw = tmem + L::T_RW;
-      const uint32_t s_tp = smem_u32(sm + L::OFF_TP), s_tpp = smem_u32(sm + L::OFF_TPP);
-      const uint32_t s_vnt = smem_u32(sm + L::OFF_VNT), s_wt = smem_u32(sm + L::OFF_WT);
-      const uint32_t s_sa = smem_u32(sm + L::OFF_SA);
-      auto a_desc_sa = [&](int ks) {  // smem S^T (K-major, DV rows x DK)
-        return sdesc_sw128(s_sa + (ks >> 2) * (DV * 128) + (ks & 3) * 32, 16, 1024);
-      };
-      auto t_vn = [&](int c) { return tmem + ((c & 1) ? L::T_VN1 : L::T_VN0); };
-      int cp0 = 0, cp1 = 0, c1a = 0, c1b = 0, c2 = 0;
-      uint64_t t_last = globaltimer_ns();
-      while (c2 < nc) {
-        bool prog = false;
-        // ---- C2(c2): needs Vn^T operands (scan) ----
-        if (c2 < c1b && mbar_test_wait(&bars[B_VNREADY], c2 & 1)) {
-          tc_fence_after();
-          trace_mark(P, c2, TR_MMA_C2);
-          const uint32_t kq = smem_u32(stage(c2) + L::OFF_KQ);
-          const uint32_t aq = smem_u32(aqk(c2));
-          // fast chunks carry V_new*gamma in the Vn^T tile itself; slow chunks in the
-          // (then free) W^T tile
-          const bool fastc = reinterpret_cast<const int*>(misc(c2))[L::M_FAST / 4] != 0;
-          const uint32_t s_vs = fastc ? s_vnt : s_wt;
+  // Two single-thread UMMA issuers, each blocking on its own in-order stream (a
+  // commit tracks only the issuing thread's UMMAs, so the streams stay independent):
+  //   warp 1, chain:  C1a (Vn^T = U^T - S^T W^T), C1b (O = S^T Q'^T),
+  //                   C2 (S^T += (Vn^T g) K ; O += Vn^T Aqk^T)
+  //   warp 2, prep:   P0 ([K;Q] K^T), INV x4 ((I+A)^-1 merges), P1 (W^T, U^T)
+  else if (warp >= 1 && warp <= 3 && lane == 0) {
+    constexpr uint32_t ID_KQ = idesc_f16(128, kC, false, false, !F16);
+    constexpr uint32_t ID_WT = idesc_f16(DK, kC, true, false, !F16);
+    constexpr uint32_t ID_UT = idesc_f16(DV, kC, true, false, !F16);
+    constexpr uint32_t ID_VN = idesc_f16(DV, kC, false, true, !F16, true);   // -S^T W^T
+    constexpr uint32_t ID_O1 = idesc_f16(DV, kC, false, false, !F16);        //  S^T Q'^T
+    constexpr uint32_t ID_S = idesc_f16(DV, DK, false, true, !F16);          // (Vn g) K
+    constexpr uint32_t ID_O2 = idesc_f16(DV, kC, false, false, !F16);        //  Vn^T Aqk^T
+    constexpr uint32_t ID_INV = idesc_f16(64, kC, false, true, false);       // fp16, B MN-major
+    const uint32_t t_sm = tmem + L::T_SM, t_sa = tmem + L::T_SA, t_o = tmem + L::T_O,
+                   t_kq = tmem + L::T_KQ, t_rw = tmem + L::T_RW;
+    const uint32_t s_tp = smem_u32(sm + L::OFF_TP), s_tpp = smem_u32(sm + L::OFF_TPP);
+    const uint32_t s_vnt = smem_u32(sm + L::OFF_VNT), s_wt = smem_u32(sm + L::OFF_WT);
+    const uint32_t s_sa = smem_u32(sm + L::OFF_SA);
+    const uint32_t s_ta = smem_u32(sm + L::OFF_TA), s_td = smem_u32(sm + L::OFF_TD);
+    auto a_desc_sa = [&](int ks) {  // smem S^T (K-major, DV rows x DK)
+      return sdesc_sw128(s_sa + (ks >> 2) * (DV * 128) + (ks & 3) * 32, 16, 1024);
+    };
+    auto t_vn = [&](int c) { return tmem + ((c & 1) ? L::T_VN1 : L::T_VN0); };
+    if (warp == 1) {
+      // chain critical path: C1a (Vn^T = U^T - S^T W^T), C2a (S^T += (Vn^T g) K)
+      for (int c = 0; c < nc; ++c) {
+        sy.wait(&bars[B_SREADY], c & 1, 14);
+        sy.wait(&bars[B_WREADY], c & 1, 15);
+        tc_fence_after();
+        trace_mark(P, c, TR_MMA_C1);
 #pragma unroll
-          for (int ks = 0; ks < kC / 16; ++ks)
-            umma_ss(t_sm, sdesc_sw128(s_vs + ks * 32, 16, 1024),
-                    sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
-          umma_commit(&bars[B_SFULL]);
+        for (int ks = 0; ks < DK / 16; ++ks) {
+          const uint64_t bd = sdesc_sw128(s_wt + ks * 2048, DK * 128, 1024);
+          if constexpr (L::SA_TMEM) umma_ts(t_vn(c), t_sa + ks * 8, bd, ID_VN, 1);
+          else umma_ss(t_vn(c), a_desc_sa(ks), bd, ID_VN, 1);
+        }
+        umma_commit(&bars[B_VNFULL]);
+        sy.wait(&bars[B_VNREADY], c & 1, 17);
+        tc_fence_after();
+        trace_mark(P, c, TR_MMA_C2);
+        const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
+        // fast chunks carry V_new*gamma in the Vn^T tile itself; slow chunks in the
+        // (then free) W^T tile
+        const bool fastc = reinterpret_cast<const int*>(misc(c))[L::M_FAST / 4] != 0;
+        const uint32_t s_vs = fastc ? s_vnt : s_wt;
 #pragma unroll
-          for (int ks = 0; ks < kC / 16; ++ks)
-            umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024),
-                    sdesc_sw128(aq + ks * 32, 16, 1024), ID_O2, 1);
-          umma_commit(&bars[B_OFULL]);
-          umma_commit(&bars[B_EMPTY0 + (c2 % 3)]);
-          ++c2;
-          prog = true;
-        }
-        // ---- C1a(c1a): needs S^T_c (scan) and W^T_c (prep) ----
-        if (c1a < cp1 && c1a == c2 && mbar_test_wait(&bars[B_SREADY], c1a & 1) &&
-            mbar_test_wait(&bars[B_WREADY], c1a & 1)) {
-          tc_fence_after();
-          trace_mark(P, c1a, TR_MMA_C1);
-#pragma unroll
-          for (int ks = 0; ks < DK / 16; ++ks) {
-            const uint64_t bd = sdesc_sw128(s_wt + ks * 2048, DK * 128, 1024);
-            if constexpr (L::SA_TMEM) umma_ts(t_vn(c1a), t_sa + ks * 8, bd, ID_VN, 1);
-            else umma_ss(t_vn(c1a), a_desc_sa(ks), bd, ID_VN, 1);
-          }
-          umma_commit(&bars[B_VNFULL]);
-          ++c1a;
-          prog = true;
-        }
-        // ---- C1b(c1b): O = S^T Q'^T once the previous output was read ----
-        if (c1b < c1a && (c1b == 0 || mbar_test_wait(&bars[B_OFREE], (c1b - 1) & 1))) {
-          tc_fence_after();
-          const uint32_t kq = smem_u32(stage(c1b) + L::OFF_KQ);
-#pragma unroll
-          for (int ks = 0; ks < DK / 16; ++ks) {
-            const uint64_t bd =
-                sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + kC * 128 + (ks & 3) * 32, 16, 1024);
-            if constexpr (L::SA_TMEM) umma_ts(t_o, t_sa + ks * 8, bd, ID_O1, ks > 0);
-            else umma_ss(t_o, a_desc_sa(ks), bd, ID_O1, ks > 0);
-          }
-          ++c1b;
-          prog = true;
-        }
-        // ---- P1(cp1): W^T = K^T T'^T -> RW ; U^T = V^T T''^T -> VN[cp1&1] ----
-        if (cp1 < cp0 && mbar_test_wait(&bars[B_TREADY], cp1 & 1) &&
-            mbar_test_wait(&bars[B_VFULL0 + (cp1 & 1)], (cp1 >> 1) & 1) &&
-            (cp1 < 2 || mbar_test_wait(&bars[B_VNFREE0 + (cp1 & 1)], ((cp1 >> 1) + 1) & 1)) &&
-            (cp1 == 0 || mbar_test_wait(&bars[B_RWFREE], (cp1 - 1) & 1))) {
-          tc_fence_after();
-          const uint32_t kq = smem_u32(stage(cp1) + L::OFF_KQ);
-          const uint32_t vt = smem_u32(vstage(cp1));
-#pragma unroll
-          for (int ks = 0; ks < kC / 16; ++ks) {
-            umma_ss(t_rw, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024),
-                    sdesc_sw128(s_tp + ks * 32, 16, 1024), ID_WT, ks > 0);
-            umma_ss(t_vn(cp1), sdesc_sw128(vt + ks * 2048, L::V_REGION, 1024),
-                    sdesc_sw128(s_tpp + ks * 32, 16, 1024), ID_UT, ks > 0);
-          }
-          umma_commit(&bars[B_WUFULL]);
-          umma_commit(&bars[B_VEMPTY0 + (cp1 & 1)]);
-          ++cp1;
-          prog = true;
-        }
-        // ---- P0(cp0): [K;Q] K^T -> KQ ----
-        if (cp0 < nc && cp0 <= cp1 + 1 &&
-            mbar_test_wait(&bars[B_FULL0 + (cp0 % 3)], in_par(cp0)) &&
-            (cp0 == 0 || mbar_test_wait(&bars[B_KQFREE], (cp0 - 1) & 1))) {
-          tc_fence_after();
-          const uint32_t kq = smem_u32(stage(cp0) + L::OFF_KQ);
-#pragma unroll
-          for (int ks = 0; ks < DK / 16; ++ks) {
-            const uint32_t a = kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32;
-            umma_ss(t_kq, sdesc_sw128(a, 16, 1024), sdesc_sw128(a, 16, 1024), ID_KQ, ks > 0);
-          }
-          umma_commit(&bars[B_KQFULL]);
-          ++cp0;
-          prog = true;
-        }
-        if (prog) {
-          t_last = globaltimer_ns();
-        } else {
-          __nanosleep(32);
-          if (abort_flag) break;
-          if (globaltimer_ns() - t_last > kWaitTimeoutNs) {
-            abort_flag = 1;
-            atomicCAS(P.status, 0, 10);
-            break;
-          }
-        }
+        for (int ks = 0; ks < kC / 16; ++ks)
+          umma_ss(t_sm, sdesc_sw128(s_vs + ks * 32, 16, 1024),
+                  sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
+        umma_commit(&bars[B_SFULL]);
+        umma_commit(&bars[B_EMPTY0 + (c % 3)]);
       }
-      umma_commit(&bars[B_DONE]);
+    } else if (warp == 3) {
+      // output: C1b (O = S^T Q'^T), C2b (O += Vn^T Aqk^T)
+      for (int c = 0; c < nc; ++c) {
+        sy.wait(&bars[B_SREADY], c & 1, 40);
+        sy.wait(&bars[B_WREADY], c & 1, 42);   // Q' of slow chunks is written by then
+        if (c >= 1) sy.wait(&bars[B_OFREE], (c - 1) & 1, 16);
+        tc_fence_after();
+        const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
+#pragma unroll
+        for (int ks = 0; ks < DK / 16; ++ks) {
+          const uint64_t bd =
+              sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + kC * 128 + (ks & 3) * 32, 16, 1024);
+          if constexpr (L::SA_TMEM) umma_ts(t_o, t_sa + ks * 8, bd, ID_O1, ks > 0);
+          else umma_ss(t_o, a_desc_sa(ks), bd, ID_O1, ks > 0);
+        }
+        umma_commit(&bars[B_O1DONE]);   // the bf16 S^T copy may be overwritten after this
+        sy.wait(&bars[B_VNREADY], c & 1, 41);
+        tc_fence_after();
+        const uint32_t aq = smem_u32(aqk(c));
+#pragma unroll
+        for (int ks = 0; ks < kC / 16; ++ks)
+          umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024),
+                  sdesc_sw128(aq + ks * 32, 16, 1024), ID_O2, 1);
+        umma_commit(&bars[B_OFULL]);
+        umma_commit(&bars[B_EMPTY0 + (c % 3)]);
+      }
+    } else {
+      // P0(c): [K;Q] K^T -> KQ
+      auto issue_p0 = [&](int c) {
+        sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 10);
+        if (c >= 1) sy.wait(&bars[B_KQFREE], (c - 1) & 1, 11);
+        tc_fence_after();
+        const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
+#pragma unroll
+        for (int ks = 0; ks < DK / 16; ++ks) {
+          const uint32_t a = kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32;
+          umma_ss(t_kq, sdesc_sw128(a, 16, 1024), sdesc_sw128(a, 16, 1024), ID_KQ, ks > 0);
+        }
+        umma_commit(&bars[B_KQFULL]);
+      };
+      issue_p0(0);
+      int ki = 0;
+      for (int c = 0; c < nc; ++c) {
+        if (c + 1 < nc) issue_p0(c + 1);   // KQFREE(c) arrives at the end of E(c)
+        // ---- inverse: X = A D, Y = D X, twice -> RW ----
+        for (int r = 0; r < 2; ++r, ++ki) {
+          sy.wait(&bars[B_INVREQ], ki & 1, 12);
+          tc_fence_after();
+          const uint32_t a0 = (ki & 1) ? s_td : s_ta;
+          const uint32_t b0 = (ki & 1) ? s_tpp : s_td;
+#pragma unroll
+          for (int ks = 0; ks < kC / 16; ++ks)
+            umma_ss(t_rw, sdesc_sw128(a0 + ks * 32, 16, 1024),
+                    sdesc_sw128(b0 + ks * 2048, 8192, 1024), ID_INV, ks > 0);
+          umma_commit(&bars[B_INVDONE]);
+        }
+        // ---- P1(c): W^T = K^T T'^T -> RW ; U^T = V^T T''^T -> VN[c&1] ----
+        sy.wait(&bars[B_TREADY], c & 1, 13);
+        sy.wait(&bars[B_VFULL0 + (c & 1)], (c >> 1) & 1, 18);
+        if (c >= 2) sy.wait(&bars[B_VNFREE0 + (c & 1)], ((c >> 1) + 1) & 1, 19);
+        if (c >= 1) sy.wait(&bars[B_RWFREE], (c - 1) & 1, 9);
+        tc_fence_after();
+        const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
+        const uint32_t vt = smem_u32(vstage(c));
+#pragma unroll
+        for (int ks = 0; ks < kC / 16; ++ks) {
+          umma_ss(t_rw, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024),
+                  sdesc_sw128(s_tp + ks * 32, 16, 1024), ID_WT, ks > 0);
+          umma_ss(t_vn(c), sdesc_sw128(vt + ks * 2048, L::V_REGION, 1024),
+                  sdesc_sw128(s_tpp + ks * 32, 16, 1024), ID_UT, ks > 0);
+        }
+        umma_commit(&bars[B_WUFULL]);
+        umma_commit(&bars[B_VEMPTY0 + (c & 1)]);
+      }
     }
+    umma_commit(&bars[B_DONE]);
   }
   // =============================================================== PREP ====
   // 256 threads: warps 4-11. Warp quadrant q = warp & 3 selects TMEM lanes 32q..32q+31
@@ -474,8 +434,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   else if (warp >= 4 && warp < 12) {
     const int p = tid - 128, q = warp & 3, gh = (warp - 4) >> 2, l = lane;
     const int r = 32 * q + l;
-    float* Aw = reinterpret_cast<float*>(sm + L::OFF_AW);
-    float* Xs = reinterpret_cast<float*>(sm + L::OFF_TP);
+    unsigned char* s_ta = sm + L::OFF_TA;   // A (fp16)
+    unsigned char* s_td = sm + L::OFF_TD;   // D: block-diagonal partial inverse (fp16)
+    float* adg = reinterpret_cast<float*>(sm + L::OFF_ADG);  // fp32 diagonal blocks of A
     unsigned char* s_tp = sm + L::OFF_TP;
     unsigned char* s_tpp = sm + L::OFF_TPP;
     const uint32_t lane_off = (32u * q) << 16;
@@ -585,9 +546,21 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         }
       }
       if (is_k) {
-        float4* dst = reinterpret_cast<float4*>(Aw + i * L::AW_LD + j0);
+        uint32_t pk[16];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) dst[m] = make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
+        for (int m = 0; m < 16; ++m) pk[m] = pack_f16(v[2 * m], v[2 * m + 1]);
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch)
+          st_chunk(s_ta, i, j0 / 8 + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
+        const int bb = i >> 4;                 // this row's diagonal block
+        if ((bb >> 1) == gh) {                 // ... lies in this warp's 32 columns
+          const bool hi = bb & 1;
+          float4* dst = reinterpret_cast<float4*>(adg + (bb * 16 + (i & 15)) * L::ADG_LD);
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            dst[m] = hi ? make_float4(v[16 + 4 * m], v[17 + 4 * m], v[18 + 4 * m], v[19 + 4 * m])
+                        : make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
+        }
       } else {
         uint32_t pk[16];
 #pragma unroll
@@ -608,42 +581,138 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       unsigned char* st = stage(c);
       float* ms = misc(c);
       const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
-      // ---- level 0 (warps 4, 5: one column per thread) || Q' = Q e^g (warps 6-11) ----
+      unsigned char* s_tx = s_tpp;  // X operand of the inverse UMMAs (T'' buffer, free here)
+      // ---- level 0 (warps 4, 5: one column of a diagonal block per thread) ||
+      //      zero the off-diagonal 16x16 blocks of D (warps 6-11) ----
       if (warp < 6) {
         float x[16];
         const int b = p >> 4, j = p & 15;
-        if (!(P.knockout & 1)) diag16_col<L::AW_LD>(Aw, b, j, x);
-        named_bar_sync(3, 64);
-        if (!(P.knockout & 1)) {
+        diag16_col<L::ADG_LD>(adg + b * 16 * L::ADG_LD, j, x);
+        named_bar_sync(3, 64);  // every column solve has read A's diagonal blocks
 #pragma unroll
-          for (int i = 0; i < 16; ++i) Aw[(16 * b + i) * L::AW_LD + 16 * b + j] = x[i];
+        for (int i = 0; i < 16; ++i) {
+          *tile_elem(s_td, 16 * b + i, 16 * b + j) = __float2half_rn(x[i]);
+          adg[(b * 16 + i) * L::ADG_LD + j] = x[i];   // T_bb, fp32, for the 16 -> 32 merge
         }
-      } else if (!fast) {
-        const int pq = p - 64;  // 0..191
-        const float* eg = ms + L::M_EG / 4;
-        constexpr int NCH = DK / 8;
-        for (int idx = pq; idx < kC * NCH; idx += 192) {
-          const int i = idx / NCH, ch = idx % NCH;
-          unsigned char* reg = st + L::OFF_KQ + (ch >> 3) * L::KQ_REGION + kC * 128;
-          uint4 u = ld_chunk(reg, i, ch & 7);
-          uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-          const float e = eg[i];
+      } else {
+        const int pq = p - 64;  // 0..191: two of the 384 off-diagonal 16-byte chunks each
 #pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float2 f = unpack2<F16>(w[m]);
-            w[m] = pack2<F16>(f.x * e, f.y * e);
+        for (int u = 0; u < 2; ++u) {
+          const int idx = pq + 192 * u, row = idx / 6, k6 = idx % 6;
+          const int blk = row >> 4, ch = k6 + (k6 >= 2 * blk ? 2 : 0);  // skip chunks 2blk, 2blk+1
+          st_chunk(s_td, row, ch, make_uint4(0u, 0u, 0u, 0u));
+        }
+        if (!fast) {  // slow chunks: Q' = Q e^g in place
+          const float* eg = ms + L::M_EG / 4;
+          constexpr int NCH = DK / 8;
+          for (int idx = pq; idx < kC * NCH; idx += 192) {
+            const int i = idx / NCH, ch = idx % NCH;
+            unsigned char* reg = st + L::OFF_KQ + (ch >> 3) * L::KQ_REGION + kC * 128;
+            uint4 u4 = ld_chunk(reg, i, ch & 7);
+            uint32_t* w = reinterpret_cast<uint32_t*>(&u4);
+            const float e = eg[i];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              const float2 f = unpack2<F16>(w[m]);
+              w[m] = pack2<F16>(f.x * e, f.y * e);
+            }
+            st_chunk(reg, i, ch & 7, u4);
           }
-          st_chunk(reg, i, ch & 7, u);
         }
       }
       named_bar_sync(kPrepBar, kPrepThreads);
-      // ---- levels 1-2 ----
-      if (!(P.knockout & 1)) tri_inv64_merge<L::AW_LD, kPrepBar, kPrepThreads>(Aw, Xs, p);
+      // ---- level 1 (SIMT): T21 = -T22 (A21 T11) for block pairs (1,0), (3,2) ----
+      {
+        float* X = reinterpret_cast<float*>(s_tp);  // T' buffer as fp32 scratch [32][18]
+        const int P2 = p >> 7, e = p & 127, r = e >> 3, c0 = (e & 7) * 2;
+        const int r1 = 32 * P2 + 16, c1 = 32 * P2;
+        const float* T11 = adg + (2 * P2) * 16 * L::ADG_LD;
+        const float* T22 = adg + (2 * P2 + 1) * 16 * L::ADG_LD;
+        float2 xx = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float a = __half2float(*tile_elem(s_ta, r1 + r, c1 + k));
+          const float2 t = *reinterpret_cast<const float2*>(T11 + k * L::ADG_LD + c0);
+          xx = __ffma2_rn(make_float2(a, a), t, xx);
+        }
+        *reinterpret_cast<float2*>(X + (P2 * 16 + r) * 18 + c0) = xx;
+        named_bar_sync(kPrepBar, kPrepThreads);
+        float2 yy = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float a = T22[r * L::ADG_LD + k];
+          const float2 t = *reinterpret_cast<const float2*>(X + (P2 * 16 + k) * 18 + c0);
+          yy = __ffma2_rn(make_float2(a, a), t, yy);
+        }
+        *reinterpret_cast<__half2*>(tile_elem(s_td, r1 + r, c1 + c0)) = __floats2half2_rn(-yy.x, -yy.y);
+      }
+      // ---- level 2 (tensor cores): X = A D32, Y = D32 X, T[32:64, 0:32] = -Y ----
+      const int rowq = (l < 16) ? 16 * q + l : -1;  // M=64 accumulator row of this lane
+      {
+        fence_async_smem();
+        named_bar_sync(kPrepBar, kPrepThreads);
+        if (p == 0) mbar_arrive(&bars[B_INVREQ]);
+        sy.wait(&bars[B_INVDONE], 0, 25);          // phases alternate X, Y: X even
+        tc_fence_after();
+        {
+          float a0[16], a1[16];
+          tmem_ld16(t_rw, a0);
+          tmem_ld16(t_rw + 16, a1);
+          tmem_wait_ld();
+          if (rowq >= 0) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+              pk[m] = pack_f16(a0[2 * m], a0[2 * m + 1]);
+              pk[8 + m] = pack_f16(a1[2 * m], a1[2 * m + 1]);
+            }
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch)
+              st_chunk(s_tx, rowq, 4 * gh + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
+          }
+        }
+        tc_fence_before();
+        fence_async_smem();
+        named_bar_sync(kPrepBar, kPrepThreads);
+        if (p == 0) mbar_arrive(&bars[B_INVREQ]);
+        sy.wait(&bars[B_INVDONE], 1, 26);
+        tc_fence_after();
+        if (warp == 6 || warp == 7) {  // rows 32-63 x cols 0-31
+          float a0[16], a1[16];
+          tmem_ld16(t_rw, a0);
+          tmem_ld16(t_rw + 16, a1);
+          tmem_wait_ld();
+          if (rowq >= 0) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+              pk[m] = pack_f16(-a0[2 * m], -a0[2 * m + 1]);
+              pk[8 + m] = pack_f16(-a1[2 * m], -a1[2 * m + 1]);
+            }
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch)
+              st_chunk(s_td, rowq, ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
+          }
+        }
+        tc_fence_before();
+      }
+      named_bar_sync(kPrepBar, kPrepThreads);
       if (p == 0) trace_mark(P, c, TR_PREP_INV);
       // ---- T' = T * (beta e^g)_j, T'' = T * beta_j (K-major B operands) ----
       {
         const int i = p >> 2, j0 = (p & 3) * 16;
-        const float4* trow = reinterpret_cast<const float4*>(Aw + i * L::AW_LD + j0);
+        float tv[16];
+        {
+          const uint4 u0 = ld_chunk(s_td, i, j0 / 8), u1 = ld_chunk(s_td, i, j0 / 8 + 1);
+          const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            const float2 f = unpack_f16(w[m]);
+            tv[2 * m] = f.x;
+            tv[2 * m + 1] = f.y;
+          }
+        }
+
         const float4* bk = reinterpret_cast<const float4*>(ms + L::M_BK / 4 + j0);
         const float4* bv = reinterpret_cast<const float4*>(ms + L::M_BV / 4 + j0);
         // fast chunks: rows scaled by gamma_i so the UMMAs yield W^T g and U^T g
@@ -651,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         uint32_t a[8], bb[8];
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          float4 t = trow[m];
+          float4 t = make_float4(tv[4 * m], tv[4 * m + 1], tv[4 * m + 2], tv[4 * m + 3]);
           t.x *= gi; t.y *= gi; t.z *= gi; t.w *= gi;
           const float4 k4 = bk[m], v4 = bv[m];
           a[2 * m] = pack2<F16>(t.x * k4.x, t.y * k4.y);
@@ -836,6 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       }
       // ---- (b) state: S^T_{c+1} ready -> bf16 copy, pre-scale by e^{gl_{c+1}} ----
       sy.wait(&bars[B_SFULL], c & 1, 32);
+      sy.wait(&bars[B_O1DONE], c & 1, 35);  // the output UMMA has read the bf16 S^T copy
       tc_fence_after();
       if (s == 0) trace_mark(P, c, TR_SCAN_SFULL);
       if (c + 1 < nc) {
@@ -879,7 +949,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   }
 
   // ============================================================ teardown ====
-  if (warp == 1 && lane == 0) {
+  if (warp >= 1 && warp <= 3 && lane == 0) {
     // every UMMA has retired before TMEM is released (bounded, even after an abort)
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(&bars[B_DONE], 0) && globaltimer_ns() - t0 < kWaitTimeoutNs) {

@@ -102,7 +102,10 @@ static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, int* status, int site) {
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-#if PTOF_SPIN_MODE == 0
+#if PTOF_SPIN_MODE == 3
+    for (int i = 0; i < 256; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+#elif PTOF_SPIN_MODE == 0
     if (mbar_try_wait(bar, parity)) return true;
 #elif PTOF_SPIN_MODE == 1
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
