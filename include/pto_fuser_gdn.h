@@ -92,6 +92,47 @@ PTOF_API int ptof_gdn_fwd_exec(void* ws, const void* q, const void* k, const voi
                       const float* g, const float* S0, void* o, float* S_final, void* stream);
 PTOF_API void ptof_gdn_fwd_teardown(void* ws);
 
+/* ---------------------------------------------------------------------------
+ * Kernels behind the reference's finer-grained fused-node keys. They share one
+ * library-owned workspace (status word) from ptof_ws_setup / ptof_ws_teardown,
+ * replacing the per-kernel setup/teardown pairs kkt_setup, scan_setup and qkv_setup
+ * (kernels/kkt_fused_lib.cpp:401-443, scan_lib.cpp:343-365, qkv_fused_lib.cpp:296-344).
+ * All chunk batches are native [M, C, ...] with M = B*H*nc; C <= 128, D <= 256.
+ */
+PTOF_API void* ptof_ws_setup(void);
+PTOF_API void ptof_ws_teardown(void* ws);
+
+/* Gated masked a b^T per chunk (replaces kkt_exec / kkt_exec_v2,
+ * kernels/kkt_fused_lib.cpp:411-441):
+ *   L[m,i,j] = (a_i . b_j) * exp(min(g_i + log beta_i - g_j, 0)) * mask(i,j)
+ * mask: strict lower (causal = 0, the kkt A) or lower incl. diagonal (causal = 1).
+ * a, b [M,C,D] in_dtype; g [M,C] fp32; beta [M,C] beta_dtype; L [M,C,C] fp16. */
+PTOF_API int ptof_gated_qk_exec(void* ws, const void* a, const void* b, const float* g,
+                                const void* beta, void* L, int M, int C, int D, int in_dtype,
+                                int beta_dtype, int causal, void* stream);
+
+/* (I + A)^-1 for strictly-lower A [M,C,C] (a_dtype), fp32 out [M,C,C]; replaces the
+ * opaque tri_inv_rec_unroll kernel (registry.py:96-140). Unlike the reference it takes
+ * A lower-triangular directly (no transpose round trip). ws may be NULL. */
+PTOF_API int ptof_tri_inv_exec(void* ws, const void* A, int a_dtype, float* T, int M, int C,
+                               void* stream);
+
+/* Resident-state chunk recurrence (replaces scan_exec, kernels/scan_lib.cpp:354-361):
+ *   h_out[b,c,h] = S; S = decay[b,h,c] * S + k_c^T (u_c - w_c S); final = S.
+ * w, k [B,nc,C,H,D], u [B,nc,C,H,Dv] in_dtype; decay [B,H,nc] fp32;
+ * h_out [B,nc,H,D,Dv], final [B,H,D,Dv] in out_dtype (fp16 / bf16 / fp32). */
+PTOF_API int ptof_chunk_h_scan_exec(void* ws, const void* w, const void* u, const void* k,
+                                    const float* decay, void* h_out, void* final_state, int B,
+                                    int H, int nc, int C, int D, int Dv, int in_dtype,
+                                    int out_dtype, void* stream);
+
+/* chunk_o score -> output in one launch (replaces qkv_exec / qkv_exec_v2,
+ * kernels/qkv_fused_lib.cpp:296-344): o = tril(q k^T * exp(min(g_i - g_j, 0))) v.
+ * q, k [M,C,D], v [M,C,Dv] in_dtype; g [M,C] fp32; o [M,C,Dv] fp32. */
+PTOF_API int ptof_qkv_flash_exec(void* ws, const void* q, const void* k, const void* v,
+                                 const float* g, float* o, int M, int C, int D, int Dv,
+                                 int in_dtype, void* stream);
+
 /* Stage timing trace (no counterpart in the reference, which attributes cost with
  * compile-time knock-out flags, kernels/kkt_fused.h:49-56): while set, every
  * tensor-core launch on this workspace writes, for CTA 0 and its first `chunks`

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include "capi_internal.h"
 #include "common.cuh"
@@ -89,6 +90,17 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, con
                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(PTOF_ECUDA, "cuTensorMapEncodeTiled(3d) failed (%d)", (int)r);
   return PTOF_OK;
+}
+
+cudaError_t set_smem_attr_once(const void* kern, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find(kern);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[kern] = bytes;
+  return e;
 }
 
 // ------------------------------------------------------------ workspace ----
@@ -216,6 +228,55 @@ int ptof_check_status(void* wsv, void* stream) {
     return fail(PTOF_ETIMEOUT, "device wait gave up at site %d", h);
   }
   return PTOF_OK;
+}
+
+// ------------------------------------------------- reference-key kernels ----
+void* ptof_ws_setup(void) { return ws_create(kWsGeneric, nullptr); }
+void ptof_ws_teardown(void* ws) { ws_destroy(static_cast<Workspace*>(ws)); }
+
+static bool dt16(int d) { return d == PTOF_F16 || d == PTOF_BF16 || d == PTOF_F32; }
+
+int ptof_gated_qk_exec(void* ws, const void* a, const void* b, const float* g, const void* beta,
+                       void* L, int M, int C, int D, int in_dtype, int beta_dtype, int causal,
+                       void* stream) {
+  (void)ws;
+  if (M < 1 || C < 1 || C > 128 || D < 1 || D > 256) return fail(PTOF_EINVAL, "gated_qk shape");
+  if (!dt16(in_dtype) || !dt16(beta_dtype)) return fail(PTOF_EINVAL, "gated_qk dtype");
+  if (!a || !b || !g || !beta || !L) return fail(PTOF_EINVAL, "gated_qk: NULL pointer");
+  return launch_gated_qk(in_dtype, beta_dtype, a, b, g, beta, L, M, C, D, causal,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int ptof_tri_inv_exec(void* ws, const void* A, int a_dtype, float* T, int M, int C, void* stream) {
+  (void)ws;
+  if (M < 1 || C < 1 || C > 128) return fail(PTOF_EINVAL, "tri_inv shape M=%d C=%d", M, C);
+  if (!dt16(a_dtype)) return fail(PTOF_EINVAL, "tri_inv dtype");
+  if (!A || !T) return fail(PTOF_EINVAL, "tri_inv: NULL pointer");
+  return launch_tri_inv(a_dtype, A, T, M, C, static_cast<cudaStream_t>(stream));
+}
+
+int ptof_chunk_h_scan_exec(void* ws, const void* w, const void* u, const void* k,
+                           const float* decay, void* h_out, void* final_state, int B, int H,
+                           int nc, int C, int D, int Dv, int in_dtype, int out_dtype,
+                           void* stream) {
+  (void)ws;
+  if (B < 1 || H < 1 || nc < 1 || C < 1 || C > 128 || D < 1 || D > 128 || Dv < 1)
+    return fail(PTOF_EINVAL, "chunk_h_scan shape");
+  if (!dt16(in_dtype) || !dt16(out_dtype)) return fail(PTOF_EINVAL, "chunk_h_scan dtype");
+  if (!w || !u || !k || !decay || !h_out || !final_state)
+    return fail(PTOF_EINVAL, "chunk_h_scan: NULL pointer");
+  return launch_scan(in_dtype, out_dtype, w, u, k, decay, h_out, final_state, B, H, nc, C, D,
+                     Dv, static_cast<cudaStream_t>(stream));
+}
+
+int ptof_qkv_flash_exec(void* ws, const void* q, const void* k, const void* v, const float* g,
+                        float* o, int M, int C, int D, int Dv, int in_dtype, void* stream) {
+  (void)ws;
+  if (M < 1 || C < 1 || C > 128 || D < 1 || D > 256 || Dv < 1 || Dv > 256)
+    return fail(PTOF_EINVAL, "qkv_flash shape");
+  if (!dt16(in_dtype)) return fail(PTOF_EINVAL, "qkv_flash dtype");
+  if (!q || !k || !v || !g || !o) return fail(PTOF_EINVAL, "qkv_flash: NULL pointer");
+  return launch_qkv_flash(in_dtype, q, k, v, g, o, M, C, D, Dv, static_cast<cudaStream_t>(stream));
 }
 
 // --------------------------------------------------------------- selftests ----

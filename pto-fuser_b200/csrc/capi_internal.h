@@ -9,7 +9,16 @@
 
 namespace ptof {
 
-enum WsKind { kWsGdnFwd = 1, kWsKkt = 2, kWsTriInv = 3, kWsScan = 4, kWsQkv = 5 };
+// Raise a kernel's dynamic shared-memory limit once per kernel (keyed by its
+// address). The first launch of every kernel happens outside stream capture (warm-up),
+// so no attribute call is ever recorded into a graph.
+cudaError_t set_smem_attr_once(const void* kern, int bytes);
+template <typename K>
+inline cudaError_t set_smem_once(K kern, int bytes) {
+  return set_smem_attr_once(reinterpret_cast<const void*>(kern), bytes);
+}
+
+enum WsKind { kWsGdnFwd = 1, kWsGeneric = 2 };
 
 // Library-owned per-setup state.
 struct Workspace {
@@ -46,6 +55,15 @@ bool gdn_fwd_tc_supports(const ptof_gdn_params& p);
 int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v,
                       const void* beta, const float* g, const float* S0, void* o,
                       float* S_final, cudaStream_t stream);
+
+int launch_gated_qk(int in_dtype, int beta_dtype, const void* a, const void* b, const float* g,
+                    const void* beta, void* L, int M, int C, int D, int causal, cudaStream_t st);
+int launch_tri_inv(int a_dtype, const void* A, float* T, int M, int C, cudaStream_t st);
+int launch_scan(int in_dtype, int out_dtype, const void* w, const void* u, const void* k,
+                const float* decay, void* h_out, void* final_state, int B, int H, int nc, int C,
+                int D, int Dv, cudaStream_t st);
+int launch_qkv_flash(int in_dtype, const void* q, const void* k, const void* v, const float* g,
+                     float* o, int M, int C, int D, int Dv, cudaStream_t st);
 
 cudaError_t launch_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,
                                  int mode, int* status, cudaStream_t stream);

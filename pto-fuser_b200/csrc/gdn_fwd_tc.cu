@@ -1019,7 +1019,7 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.os_b = so.b; P.os_h = so.h; P.os_t = so.t;
   P.scale = p.scale;
   auto kern = tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+  cudaError_t e = set_smem_once(kern, L::BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_tc smem attribute");
   kern<<<p.B * p.H, tcfwd::kThreads, L::BYTES, stream>>>(P);
   e = cudaGetLastError();

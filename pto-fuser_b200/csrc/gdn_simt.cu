@@ -15,6 +15,7 @@
 // One CTA per (b*h, value block of kBV columns); the chunk loop is sequential.
 #include <cuda_runtime.h>
 
+#include "capi_internal.h"
 #include "common.cuh"
 
 namespace ptof {
@@ -223,7 +224,7 @@ template <typename TI, typename TB, typename TO>
 cudaError_t launch_typed(const Args& a, cudaStream_t stream) {
   auto kern = gdn_fwd_simt_kernel<TI, TB, TO>;
   const int smem = static_cast<int>(sizeof(Smem));
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once(kern, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.B * a.H, (a.Dv + kBV - 1) / kBV);
   kern<<<grid, kThreads, smem, stream>>>(a);

@@ -51,6 +51,12 @@ _SIGNATURES = {
     "ptof_check_status": (_i32, [_vp, _vp]),
     "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),
     "ptof_last_error": (ctypes.c_char_p, []),
+    "ptof_ws_setup": (_vp, []),
+    "ptof_ws_teardown": (None, [_vp]),
+    "ptof_gated_qk_exec": (_i32, [_vp] * 6 + [_i32] * 6 + [_vp]),
+    "ptof_tri_inv_exec": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _vp]),
+    "ptof_chunk_h_scan_exec": (_i32, [_vp] * 7 + [_i32] * 8 + [_vp]),
+    "ptof_qkv_flash_exec": (_i32, [_vp] * 6 + [_i32] * 5 + [_vp]),
     "ptof_selftest_umma": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
     "ptof_selftest_tma": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
 }

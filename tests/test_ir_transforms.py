@@ -1,0 +1,118 @@
+"""Device-free structural tests of the IR, transforms, templates, cost model,
+policy and the unverified compile driver (mirroring the reference's test_ir.py,
+test_transform.py, test_template.py and test_compile.py)."""
+import pytest
+import torch
+
+from pto_fuser import (CostModel, EinsumNode, Features, FusedNode, OpaqueNode, Policy, Program,
+                       TensorOp, VecGlueNode, canonicalize, compile_program, epilogue_report)
+from pto_fuser.forwards import build_deltanet_program, build_gdn_program
+from pto_fuser.ir import node_outputs
+from pto_fuser.template import FuseChunkOFlash, FuseContractionEpilogue
+from pto_fuser.transforms import FuseGDNForward, LowerResidentScan
+
+B, H, NC, C, D = 1, 4, 4, 64, 128
+
+
+def _gdn():
+    return build_gdn_program(B, H, NC, C, D, D ** -0.5)
+
+
+def test_program_rejects_use_before_def():
+    with pytest.raises(ValueError):
+        Program(nodes=[VecGlueNode("add", ["a", "b"], "c")], inputs=["a"], outputs=["c"])
+
+
+def test_program_rejects_missing_output():
+    with pytest.raises(ValueError):
+        Program(nodes=[VecGlueNode("add", ["a", "a"], "c")], inputs=["a"], outputs=["d"])
+
+
+def test_fused_node_multi_output():
+    n = FusedNode(kernel="chunk_h_scan", inputs=["w"], outputs=["h_out", "final"])
+    assert node_outputs(n) == ["h_out", "final"] and n.output == "h_out"
+    Program(nodes=[n], inputs=["w"], outputs=["h_out", "final"])
+
+
+def test_gdn_program_shape():
+    prog = _gdn()
+    kinds = {}
+    for n in prog.nodes:
+        kinds[type(n).__name__] = kinds.get(type(n).__name__, 0) + 1
+    assert kinds["OpaqueNode"] == 1 and prog.outputs == ["o"]
+    assert kinds["EinsumNode"] == 6 + 2 * NC
+
+
+def test_canonicalize_is_idempotent_and_nn():
+    c1 = canonicalize(_gdn())
+    c2 = canonicalize(c1)
+    es = [n for n in c1.nodes if isinstance(n, EinsumNode)]
+    assert all(n.read_mode == "NN" and not n.fuse_out for n in es)
+    assert [str(n) for n in c1.nodes] == [str(n) for n in c2.nodes]
+
+
+def test_fuse_gdn_forward_single_node():
+    t = FuseGDNForward(B, H, NC, C, D)
+    prog = _gdn()
+    assert t.match(prog) == 1
+    out = t.apply(prog).program
+    assert len(out.nodes) == 1 and out.nodes[0].kernel == "gdn_chunk_fwd"
+    assert out.nodes[0].params["scale"] == pytest.approx(D ** -0.5)
+    assert t.match(out) == 0
+
+
+def test_fuse_gdn_forward_not_on_deltanet():
+    assert FuseGDNForward(B, H, NC, C, D).match(build_deltanet_program(B, H, NC, C, D, 0.1)) == 0
+
+
+def test_resident_scan_rewrite():
+    t = LowerResidentScan(B, H, NC, C, D)
+    prog = canonicalize(_gdn())
+    assert t.match(prog) == 1
+    out = t.apply(prog).program
+    kernels = [n.kernel for n in out.nodes if isinstance(n, FusedNode)]
+    assert kernels == ["chunk_h_scan"]
+    assert not any(n.output.startswith("WS0") for n in out.nodes)
+    assert t.match(out) == 0
+
+
+def test_templates_and_flash():
+    prog = canonicalize(_gdn())
+    rep = str(epilogue_report(prog))
+    assert "template kkt-gated-native" in rep and "template chunk-o-gated-native" in rep
+    flash = FuseChunkOFlash(B, H, NC, C, D)
+    assert flash.match(prog) == 1
+    prog2 = flash.apply(prog).program
+    assert any(isinstance(n, FusedNode) and n.kernel == "qkv_flash_native_v2" for n in prog2.nodes)
+    gen = FuseContractionEpilogue(B, H, NC, C, D, v2=True)
+    prog3 = gen.apply(prog2).program
+    ks = {n.kernel for n in prog3.nodes if isinstance(n, FusedNode)}
+    assert ks == {"qkv_flash_native_v2", "kkt_gated_native_v2"}
+
+
+def test_cost_and_policy():
+    f = Features(B, H, NC, C, D)
+    cm = CostModel()
+    assert cm.predict("fuse-gdn-forward", f).worth_trying
+    assert not cm.predict("fuse-gdn-forward", Features(B, H, NC, 32, 128)).worth_trying
+    assert not cm.predict("enable-direct-reads", f).worth_trying
+    assert not cm.predict("unknown", f).worth_trying
+    names = [p.name for p in Policy().pipeline(canonicalize(_gdn()), f)]
+    assert names[0] == "fuse-gdn-forward"
+    assert names.index("lower-resident-scan") < names.index("fuse-contraction-epilogue")
+    assert f.M == B * H * NC and f.N == B * H and f.T == NC * C
+
+
+def test_compile_unverified_whole_forward():
+    res = compile_program(_gdn(), Features(B, H, NC, C, D), verify=False)
+    assert [n.kernel for n in res.program.nodes] == ["gdn_chunk_fwd"]
+    assert not res.report.verified and [r.name for r in res.report.kept] == ["fuse-gdn-forward"]
+    assert "transforms kept" in str(res.report)
+
+
+def test_compile_unverified_partial_lowering():
+    """With the whole-forward fusion not proposed (C=32), the partial fusions fire."""
+    prog = build_gdn_program(B, H, NC, 32, D, D ** -0.5)
+    res = compile_program(prog, Features(B, H, NC, 32, D), verify=False)
+    ks = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
+    assert ks == {"chunk_h_scan", "qkv_flash_native_v2", "kkt_gated_native_v2"}
