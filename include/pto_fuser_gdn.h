@@ -136,8 +136,9 @@ PTOF_API int ptof_qkv_flash_exec(void* ws, const void* q, const void* k, const v
 /* Stage timing trace (no counterpart in the reference, which attributes cost with
  * compile-time knock-out flags, kernels/kkt_fused.h:49-56): while set, every
  * tensor-core launch on this workspace writes, for CTA 0 and its first `chunks`
- * chunks, 16 globaltimer stamps (ns) per chunk into the caller's device buffer
- * dev_buf[chunks][16]. chunks = 0 turns tracing off. */
+ * chunks, 24 globaltimer stamps (ns) per chunk into the caller's device buffer
+ * dev_buf[chunks][24], followed by one record {start ns, end ns, SM id, 0} per CTA
+ * (B*H records). chunks = 0 turns tracing off. */
 PTOF_API int ptof_gdn_fwd_set_trace(void* ws, void* dev_buf, int chunks);
 
 /* Reads (and clears) the workspace's device status word after synchronising

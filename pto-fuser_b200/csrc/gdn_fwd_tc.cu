@@ -13,14 +13,14 @@
 // fp32 S^T (TMEM lane = value column), and its bf16 copy feeds the next chunk's
 // MMAs straight from TMEM.
 //
-// Warp roles (384 threads):
-//   warp 0     TMA producer: K, Q, V tiles (128B-swizzled), g, beta -> 2-stage ring
-//   warp 1     UMMA issuer (one thread)
-//   warp 2     TMEM allocator
-//   warps 4-7  "prep": kkt/qk epilogue from TMEM, Q*e^g, (I+A)^-1 (blocked forward
-//              substitution in fp32), T' and T'' for the WY MMAs, W^T readout
-//   warps 8-11 "scan": V_new readout, state update, output epilogue
-// Chunk c+1's prep overlaps chunk c's scan.
+// Warp roles (512 threads):
+//   warp 0       TMA producer: [K|Q] tiles, g, beta -> 3-stage ring; V -> 2-stage ring
+//   warps 1-3    single-thread UMMA issuers, one in-order stream each: chain (V_new,
+//                state update), prep ([K;Q]K^T, W^T / U^T), output (S^T Q'^T, Vn^T Aqk^T);
+//                warp 2 also owns the TMEM allocation
+//   warps 4-11   prep: kkt/qk epilogue from TMEM, (I + A)^-1, T' and T'' for the WY
+//                UMMAs, W^T readout; software-pipelined one chunk ahead of the chain
+//   warps 12-15  scan: V_new readout, state copy / decay, output epilogue
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -64,15 +64,11 @@ struct Layout {
   // prep buffers
   static constexpr int OFF_TP = OFF_WT + DK * 128;   // T' bf16 [64 x 64] (also inverse scratch)
   static constexpr int OFF_TPP = OFF_TP + 8192;      // T''
-  // inverse workspace: fp16 tiles (128B-swizzled, 64 rows x 64) of A and of the
-  // block-diagonal partial inverse D, plus the fp32 16x16 diagonal blocks of A
+  // inverse workspace: fp16 tiles (128B-swizzled, 64 rows x 64) of A and of T
   static constexpr int OFF_TA = OFF_TPP + 8192;
   static constexpr int OFF_TD = OFF_TA + 8192;
-  static constexpr int ADG_LD = 20;                  // fp32 row stride of a diagonal block
-  static constexpr int OFF_ADG = OFF_TD + 8192;
-  static constexpr int ADG_BYTES = 5120;             // 4 x 16 x 20 floats
   // chain buffers
-  static constexpr int OFF_VNT = OFF_ADG + ADG_BYTES;  // bf16 Vn^T [DV x 64]
+  static constexpr int OFF_VNT = OFF_TD + 8192;      // bf16 Vn^T [DV x 64]
   static constexpr int OFF_SA = OFF_VNT + DV * 128;  // bf16 S^T [DV x DK] (smem variant)
   static constexpr int SA_BYTES = SA_TMEM ? 0 : NKB * DV * 128;
   static constexpr int OFF_OSC = OFF_SA + SA_BYTES;  // fp32 [64] output multipliers (scan)
@@ -96,7 +92,7 @@ enum Bar {
   B_FULL0 = 0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_GREADY0, B_GREADY1, B_GREADY2,
   B_VFULL0, B_VFULL1, B_VEMPTY0, B_VEMPTY1, B_WREADY,
   B_KQFULL, B_TREADY, B_WUFULL, B_RWFREE, B_VNFREE0, B_VNFREE1, B_SREADY, B_VNFULL,
-  B_VNREADY, B_SFULL, B_OFULL, B_OFREE, B_DONE, B_KQFREE, B_INVREQ, B_INVDONE, B_O1DONE, B_COUNT
+  B_VNREADY, B_SFULL, B_OFULL, B_OFREE, B_DONE, B_KQFREE, B_O1DONE, B_COUNT
 };
 
 struct Params {
@@ -109,8 +105,6 @@ struct Params {
   int* status;
   unsigned long long* trace;       // optional [chunks x kTraceSlots] timestamps of CTA 0
   int trace_chunks;
-  int knockout;                    // cost-attribution knock-out (results invalid): bit1 skips
-                                   // the kkt/qk epilogue math
   int B, H, T, nc;
   int gate_mode, beta_dtype, layout;
   int64_t gs_b, gs_h, gs_t;        // g / beta strides (elements)
@@ -119,14 +113,18 @@ struct Params {
 };
 
 // Optional stage timestamps (globaltimer, ns) of CTA 0: slot layout per chunk.
-constexpr int kTraceSlots = 16;
+constexpr int kTraceSlots = 24;
 enum TraceSlot {
   TR_TMA_ISSUE = 0, TR_PREP_FULL, TR_PREP_KQ, TR_PREP_EPI, TR_PREP_INV, TR_PREP_TREADY,
   TR_PREP_WU, TR_PREP_END, TR_SCAN_VNFULL, TR_SCAN_VNREADY, TR_SCAN_SFULL, TR_SCAN_SREADY,
-  TR_SCAN_OFULL, TR_SCAN_END, TR_MMA_C1, TR_MMA_C2
+  TR_SCAN_OFULL, TR_SCAN_END, TR_MMA_C1, TR_MMA_C2, TR_INV_START, TR_INV_L0, TR_INV_L1,
+  TR_INV_L2, TR_PREP_COEF, TR_PREP_OFULL, TR_X0, TR_X1
 };
+// Compiled only into the traced instantiation (TRACE = true), so the production
+// kernel's loops carry no trace code.
+template <bool TRACE>
 __device__ __forceinline__ void trace_mark(const Params& P, int c, int slot) {
-  if (P.trace != nullptr && blockIdx.x == 0 && c < P.trace_chunks)
+  if (TRACE && blockIdx.x == 0 && c < P.trace_chunks)
     P.trace[c * kTraceSlots + slot] = globaltimer_ns();
 }
 
@@ -168,27 +166,17 @@ __device__ __forceinline__ uint4 ld_chunk(const unsigned char* region, int row, 
 }
 
 // ------------------------------------------------------- (I + A)^-1, 64 x 64 ----
-// T = (I + A)^-1 (A strictly lower) in two levels:
-//  level 0 (SIMT): the four 16x16 diagonal blocks T_bb, one column per thread,
-//    right-looking substitution (x_i -= A[i][k] x_k once x_k is final), so the
-//    dependency chain is 15 FMAs and every A load is independent of x;
-//  levels 1-2 (tensor cores, fp16 operands, fp32 accumulate): with D the block
-//    diagonal of already-inverted blocks, X = A D has X_IJ = A_IJ T_JJ and
-//    Y = D X has Y_IJ = T_II A_IJ T_JJ, so T_IJ = -Y_IJ for the blocks one level
-//    below the diagonal. Two rounds (16 -> 32 on blocks (1,0),(3,2), then 32 -> 64
-//    on the lower-left 32x32 block) = four 64x64x64 UMMAs.
-// blk: fp32 16x16 diagonal block of A, row stride LD. Returns column j of T_bb in x.
-template <int LD>
-__device__ __forceinline__ void diag16_col(const float* blk, int j, float (&x)[16]) {
-#pragma unroll
-  for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;
-#pragma unroll
-  for (int k = 0; k < 15; ++k) {
-    const float xk = x[k];
-#pragma unroll
-    for (int i = k + 1; i < 16; ++i) x[i] = fmaf(-blk[i * LD + k], xk, x[i]);
-  }
-}
+// T = (I + A)^-1 (A strictly lower), blocked over 16x16 blocks:
+//  level 0: the four diagonal blocks T_bb = (I + N)^-1, N = A_bb nilpotent, by
+//    the product form (I - N)(I + N^2)(I + N^4)(I + N^8) on warp MMAs (inv16_diag);
+//  level 1 (16 -> 32) and level 2 (32 -> 64): the block below the diagonal of a
+//    lower-triangular [[T11, 0], [A21, T22]]-pair is T21 = -(T22 A21) T11, two
+//    chained products done with warp-level fp16 MMAs (fp32 accumulate) whose first
+//    result is fed to the second straight from registers. A tcgen05 round trip
+//    (issue, commit, mbarrier, TMEM readout) costs ~0.5 us for these 16x16 / 32x32
+//    products, the warp-level form a few tens of cycles each.
+// All operands are fp16 (A and T entries are bounded by small multiples of 1 for
+// beta <= 1, decays <= 1 and unit-norm keys), accumulation fp32.
 
 // 16-bit element (row, col) of a 64-column 128B-swizzled tile
 __device__ __forceinline__ __half* tile_elem(unsigned char* tile, int row, int col) {
@@ -196,8 +184,98 @@ __device__ __forceinline__ __half* tile_elem(unsigned char* tile, int row, int c
                                                        ((col & 7) << 1)));
 }
 
+// Warp-level MMA fragments (layouts in ptx.cuh) of 64-column 128B-swizzled fp16 tiles.
+// A fragment of the 16x16 block at (r0, c0).
+__device__ __forceinline__ void frag_a(const unsigned char* tile, int r0, int c0, int lane,
+                                       uint32_t (&a)[4]) {
+  const int mi = lane >> 3, row = r0 + (lane & 7) + ((mi & 1) << 3), ch = (c0 >> 3) + (mi >> 1);
+  ldsm_x4(smem_u32(tile + row * 128 + ((ch ^ (row & 7)) << 4)), a);
+}
+// B fragments of the two 8-column n-tiles (n0, n0 + 8) over the k rows k0..k0+15 of a
+// row-major [k][n] tile: b[0], b[1] for n-tile n0 and b[2], b[3] for n0 + 8.
+__device__ __forceinline__ void frag_b2(const unsigned char* tile, int k0, int n0, int lane,
+                                        uint32_t (&b)[4]) {
+  const int mi = lane >> 3, row = k0 + (lane & 7) + ((mi & 1) << 3), ch = (n0 >> 3) + (mi >> 1);
+  ldsm_x4_t(smem_u32(tile + row * 128 + ((ch ^ (row & 7)) << 4)), b);
+}
+// The fp32 accumulators of a 16x16 product (two n-tiles) as the fp16 A fragment of
+// the next product (the C layout of m16n8 equals the A layout of m16k16).
+__device__ __forceinline__ void c_to_a(const float (&d0)[4], const float (&d1)[4], uint32_t (&a)[4]) {
+  a[0] = pack_f16(d0[0], d0[1]);
+  a[1] = pack_f16(d0[2], d0[3]);
+  a[2] = pack_f16(d1[0], d1[1]);
+  a[3] = pack_f16(d1[2], d1[3]);
+}
+// Store s * C (one 16x8 n-tile at (r0, n0)) into a 64-column swizzled fp16 tile.
+__device__ __forceinline__ void st_c(unsigned char* tile, int r0, int n0, int lane,
+                                     const float (&d)[4], float sgn) {
+  const int g = lane >> 2, t = lane & 3;
+  *reinterpret_cast<__half2*>(tile_elem(tile, r0 + g, n0 + 2 * t)) =
+      __floats2half2_rn(sgn * d[0], sgn * d[1]);
+  *reinterpret_cast<__half2*>(tile_elem(tile, r0 + g + 8, n0 + 2 * t)) =
+      __floats2half2_rn(sgn * d[2], sgn * d[3]);
+}
+// A fragment of the transpose of the 16x16 block at (r0, c0).
+__device__ __forceinline__ void frag_at(const unsigned char* tile, int r0, int c0, int lane,
+                                        uint32_t (&a)[4]) {
+  const int mi = lane >> 3, row = r0 + (lane & 7) + ((mi >> 1) << 3), ch = (c0 >> 3) + (mi & 1);
+  ldsm_x4_t(smem_u32(tile + row * 128 + ((ch ^ (row & 7)) << 4)), a);
+}
+// 16x16 products on register pairs (X, X^T), each held as an A fragment: an A
+// fragment of X^T is exactly the pair of B fragments of X, so P X needs no data
+// movement: n-tile 0 uses (xt[0], xt[2]), n-tile 1 (xt[1], xt[3]).
+__device__ __forceinline__ void mma16(float (&d0)[4], float (&d1)[4], const uint32_t (&pa)[4],
+                                      const uint32_t (&xt)[4]) {
+  mma_f16_16816(d0, pa, xt[0], xt[2]);
+  mma_f16_16816(d1, pa, xt[1], xt[3]);
+}
+__device__ __forceinline__ void zero4(float (&d)[4]) { d[0] = d[1] = d[2] = d[3] = 0.f; }
+// T = (I + N)^-1 of the strictly lower 16x16 block N at (r0, r0) of the fp16 tile
+// `a_tile`, written (fp16) to the same block of `t_tile`. N is nilpotent (N^16 = 0),
+// so (I + N)^-1 = (I - N)(I + N^2)(I + N^4)(I + N^8): 16 warp MMAs on a dependency
+// chain five products deep, fp32 accumulate, fp16 intermediates. One warp.
+__device__ __forceinline__ void inv16_diag(const unsigned char* a_tile, unsigned char* t_tile,
+                                           int r0, int lane) {
+  uint32_t na[4], nt[4], x2a[4], x2t[4], x4a[4], x4t[4], x8t[4], pa[4];
+  frag_a(a_tile, r0, r0, lane, na);
+  frag_at(a_tile, r0, r0, lane, nt);
+  float d0[4], d1[4], e0[4], e1[4];
+  zero4(d0); zero4(d1); zero4(e0); zero4(e1);
+  mma16(d0, d1, na, nt);          // N^2
+  mma16(e0, e1, nt, na);          // (N^2)^T = N^T N^T
+  c_to_a(d0, d1, x2a);
+  c_to_a(e0, e1, x2t);
+  // P1 = I - N + N^2 - N N^2 (accumulated on top of N^2 in fp32)
+  const int g = lane >> 2, t = lane & 3;
+  const float2 n00 = unpack_f16(na[0]), n10 = unpack_f16(na[1]);
+  const float2 n01 = unpack_f16(na[2]), n11 = unpack_f16(na[3]);
+  float p0[4] = {d0[0] - n00.x + (g == 2 * t ? 1.f : 0.f), d0[1] - n00.y + (g == 2 * t + 1 ? 1.f : 0.f),
+                 d0[2] - n10.x, d0[3] - n10.y};
+  float p1[4] = {d1[0] - n01.x, d1[1] - n01.y, d1[2] - n11.x + (g == 2 * t ? 1.f : 0.f),
+                 d1[3] - n11.y + (g == 2 * t + 1 ? 1.f : 0.f)};
+  zero4(d0); zero4(d1); zero4(e0); zero4(e1);
+  mma16(d0, d1, x2a, x2t);        // N^4
+  mma16(e0, e1, x2t, x2a);        // (N^4)^T
+  float q0[4], q1[4];
+  zero4(q0); zero4(q1);
+  mma16(q0, q1, na, x2t);         // N^3 = N N^2
+#pragma unroll
+  for (int m = 0; m < 4; ++m) { p0[m] -= q0[m]; p1[m] -= q1[m]; }
+  c_to_a(d0, d1, x4a);
+  c_to_a(e0, e1, x4t);
+  zero4(e0); zero4(e1);
+  mma16(e0, e1, x4t, x4a);        // (N^8)^T
+  c_to_a(e0, e1, x8t);
+  c_to_a(p0, p1, pa);
+  mma16(p0, p1, pa, x4t);         // P2 = P1 + P1 N^4
+  c_to_a(p0, p1, pa);
+  mma16(p0, p1, pa, x8t);         // T  = P2 + P2 N^8
+  st_c(t_tile, r0, r0, lane, p0, 1.f);
+  st_c(t_tile, r0, r0 + 8, lane, p1, 1.f);
+}
+
 // ------------------------------------------------------------------ kernel ----
-template <int DK, int DV, bool F16, typename TO>
+template <int DK, int DV, bool F16, typename TO, bool TRACE>
 __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_constant__ Params P) {
   using L = Layout<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -226,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint64_t t_start = (TRACE && tid == 0) ? globaltimer_ns() : 0;
 
   // chunk c lives in input stage c % 3 (use index c / 3), V stage c & 1, Aqk buffer c & 1
   auto stage = [&](int c) { return sm + (c % 3) * L::IN_STAGE; };
@@ -279,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
                     static_cast<const unsigned char*>(P.beta) + gb * gelt, kC * gelt,
                     &bars[B_FULL0 + s]);
         }
-        trace_mark(P, c, TR_TMA_ISSUE);
+        trace_mark<TRACE>(P, c, TR_TMA_ISSUE);
       }
       // V tile of chunk c (consumed by the U^T UMMA only)
       if (c >= 2) sy.wait(&bars[B_VEMPTY0 + (c & 1)], ((c >> 1) + 1) & 1, 2);
@@ -306,13 +385,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     constexpr uint32_t ID_O1 = idesc_f16(DV, kC, false, false, !F16);        //  S^T Q'^T
     constexpr uint32_t ID_S = idesc_f16(DV, DK, false, true, !F16);          // (Vn g) K
     constexpr uint32_t ID_O2 = idesc_f16(DV, kC, false, false, !F16);        //  Vn^T Aqk^T
-    constexpr uint32_t ID_INV = idesc_f16(64, kC, false, true, false);       // fp16, B MN-major
     const uint32_t t_sm = tmem + L::T_SM, t_sa = tmem + L::T_SA, t_o = tmem + L::T_O,
                    t_kq = tmem + L::T_KQ, t_rw = tmem + L::T_RW;
     const uint32_t s_tp = smem_u32(sm + L::OFF_TP), s_tpp = smem_u32(sm + L::OFF_TPP);
     const uint32_t s_vnt = smem_u32(sm + L::OFF_VNT), s_wt = smem_u32(sm + L::OFF_WT);
     const uint32_t s_sa = smem_u32(sm + L::OFF_SA);
-    const uint32_t s_ta = smem_u32(sm + L::OFF_TA), s_td = smem_u32(sm + L::OFF_TD);
     auto a_desc_sa = [&](int ks) {  // smem S^T (K-major, DV rows x DK)
       return sdesc_sw128(s_sa + (ks >> 2) * (DV * 128) + (ks & 3) * 32, 16, 1024);
     };
@@ -323,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         sy.wait(&bars[B_SREADY], c & 1, 14);
         sy.wait(&bars[B_WREADY], c & 1, 15);
         tc_fence_after();
-        trace_mark(P, c, TR_MMA_C1);
+        trace_mark<TRACE>(P, c, TR_MMA_C1);
 #pragma unroll
         for (int ks = 0; ks < DK / 16; ++ks) {
           const uint64_t bd = sdesc_sw128(s_wt + ks * 2048, DK * 128, 1024);
@@ -333,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         umma_commit(&bars[B_VNFULL]);
         sy.wait(&bars[B_VNREADY], c & 1, 17);
         tc_fence_after();
-        trace_mark(P, c, TR_MMA_C2);
+        trace_mark<TRACE>(P, c, TR_MMA_C2);
         const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
         // fast chunks carry V_new*gamma in the Vn^T tile itself; slow chunks in the
         // (then free) W^T tile
@@ -387,21 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         umma_commit(&bars[B_KQFULL]);
       };
       issue_p0(0);
-      int ki = 0;
       for (int c = 0; c < nc; ++c) {
         if (c + 1 < nc) issue_p0(c + 1);   // KQFREE(c) arrives at the end of E(c)
-        // ---- inverse: X = A D, Y = D X, twice -> RW ----
-        for (int r = 0; r < 2; ++r, ++ki) {
-          sy.wait(&bars[B_INVREQ], ki & 1, 12);
-          tc_fence_after();
-          const uint32_t a0 = (ki & 1) ? s_td : s_ta;
-          const uint32_t b0 = (ki & 1) ? s_tpp : s_td;
-#pragma unroll
-          for (int ks = 0; ks < kC / 16; ++ks)
-            umma_ss(t_rw, sdesc_sw128(a0 + ks * 32, 16, 1024),
-                    sdesc_sw128(b0 + ks * 2048, 8192, 1024), ID_INV, ks > 0);
-          umma_commit(&bars[B_INVDONE]);
-        }
         // ---- P1(c): W^T = K^T T'^T -> RW ; U^T = V^T T''^T -> VN[c&1] ----
         sy.wait(&bars[B_TREADY], c & 1, 13);
         sy.wait(&bars[B_VFULL0 + (c & 1)], (c >> 1) & 1, 18);
@@ -436,7 +500,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     const int r = 32 * q + l;
     unsigned char* s_ta = sm + L::OFF_TA;   // A (fp16)
     unsigned char* s_td = sm + L::OFF_TD;   // D: block-diagonal partial inverse (fp16)
-    float* adg = reinterpret_cast<float*>(sm + L::OFF_ADG);  // fp32 diagonal blocks of A
     unsigned char* s_tp = sm + L::OFF_TP;
     unsigned char* s_tpp = sm + L::OFF_TPP;
     const uint32_t lane_off = (32u * q) << 16;
@@ -448,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       float* ms = misc(c);
       const float* gcum = ms + L::M_GCUM / 4;
       sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 20);
-      if (p == 0) trace_mark(P, c, TR_PREP_FULL);
+      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_FULL);
       // ---- per-token coefficients (warp 4: tokens 2l, 2l+1) ----
       if (warp == 4) {
         float g0 = 0.f, g1 = 0.f;
@@ -472,6 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
           mono = (g1 <= g0) && (l == 0 || g0 <= prev);
         }
+        if (p == 0) trace_mark<TRACE>(P, c, TR_X0);
         const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
         const float gl = __shfl_sync(0xffffffffu, g1, 31);
         // exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j): overflow-free when the chunk's
@@ -486,6 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           const float* bf = reinterpret_cast<const float*>(st + L::OFF_MISC + L::M_BRAW);
           b0 = bf[2 * l]; b1 = bf[2 * l + 1];
         }
+        if (p == 0) trace_mark<TRACE>(P, c, TR_X1);
         const float e0 = __expf(g0), e1 = __expf(g1);
         const float rf0 = __expf(g0 - gfirst), rf1 = __expf(g1 - gfirst);
         float2* m2 = reinterpret_cast<float2*>(ms);
@@ -503,77 +568,63 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           reinterpret_cast<int*>(ms)[L::M_FAST / 4] = fast ? 1 : 0;
         }
       }
+      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_COEF);
       named_bar_sync(kPrepBar, kPrepThreads);
       if (p == 0) mbar_arrive(&bars[B_GREADY0 + (c % 3)]);
       const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
       // ---- A = gated strict-lower KK^T (rows 0-63), Aqk = gated causal QK^T (64-127) ----
       // the Aqk buffer of chunk c last fed chunk c-2's output UMMA
       if (c >= 2) sy.wait(&bars[B_OFULL], c & 1, 23);
+      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_OFULL);
       sy.wait(&bars[B_KQFULL], c & 1, 21);
       tc_fence_after();
-      if (p == 0) trace_mark(P, c, TR_PREP_KQ);
-      float v[32];
-      {
-        float a0[16], a1[16];
-        tmem_ld16(t_kq, a0);
-        tmem_ld16(t_kq + 16, a1);
+      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_KQ);
+      // one 16-column half of this warp's 32 columns per iteration (rolled: the prep
+      // loop's code must stay small enough for the SM's instruction cache)
+      const int i = r & 63;
+      const bool is_k = r < 64;
+      const int lim = is_k ? i : i + 1;       // strict lower (A) / causal (Aqk)
+      // fast chunks: A = rowf_i beta_i colf_j KK^T and Aqk = e^{-gl} QK^T (the e^{g_i}
+      // of the score is applied at the output)
+      const float rowm = is_k ? ms[L::M_ROWFB / 4 + i] : ms[L::M_ENGL / 4];
+      unsigned char* dst = is_k ? s_ta : aqk(c);
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        const int j0 = 32 * gh + 16 * hh;
+        float v[16];
+        tmem_ld16(t_kq + 16 * hh, v);
         tmem_wait_ld();
+        if (fast) {
 #pragma unroll
-        for (int m = 0; m < 16; ++m) { v[m] = a0[m]; v[16 + m] = a1[m]; }
+          for (int m = 0; m < 16; ++m) {
+            const float cf = is_k ? rowm * ms[L::M_COLF / 4 + j0 + m] : rowm;
+            v[m] = (j0 + m < lim) ? v[m] * cf : 0.f;
+          }
+        } else {
+          // exact per-element coefficients: K rows beta_i * kkt_coef, Q rows qk_coef
+          // (one exponential each: both are exp(min(x, 0)) up to the x > 0 cut of kkt)
+          const float gi = gcum[i], bi = is_k ? ms[L::M_BV / 4 + i] : 1.f;
+          const float xcut = is_k ? 0.f : 3.0e38f;
+#pragma unroll
+          for (int m = 0; m < 16; ++m) {
+            const float x = gi - gcum[j0 + m];
+            const float cf = (x <= xcut) ? __expf(fminf(x, 0.f)) * bi : 0.f;
+            v[m] = (j0 + m < lim) ? v[m] * cf : 0.f;
+          }
+        }
+        // A in fp16 (operand of the inverse), Aqk in the input type (score UMMA operand)
+        uint32_t pk[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+          pk[m] = is_k ? pack_f16(v[2 * m], v[2 * m + 1]) : pack2<F16>(v[2 * m], v[2 * m + 1]);
+        st_chunk(dst, i, j0 / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+        st_chunk(dst, i, j0 / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
       }
       tc_fence_before();
-      const int i = r & 63, j0 = 32 * gh;
-      const bool is_k = r < 64;
-      const float* colf = ms + L::M_COLF / 4 + j0;
-      if (P.knockout & 2) {
-      } else if (fast && is_k) {
-        const float rf = ms[L::M_ROWFB / 4 + i];
-#pragma unroll
-        for (int m = 0; m < 32; ++m) v[m] = (j0 + m < i) ? v[m] * rf * colf[m] : 0.f;
-      } else if (fast) {
-        // fast chunks: O^T = e^g (S^T Q^T + e^{-gl} (Vn g)^T QK_causal^T), the e^g applied
-        // at the output, so the score only needs the causal mask and one scale
-        const float eng = ms[L::M_ENGL / 4];
-#pragma unroll
-        for (int m = 0; m < 32; ++m) v[m] = (j0 + m <= i) ? v[m] * eng : 0.f;
-      } else {
-        const float gi = gcum[i], bi = ms[L::M_BV / 4 + i];
-#pragma unroll
-        for (int m = 0; m < 32; ++m) {
-          const int j = j0 + m;
-          const float cf = is_k ? bi * kkt_coef(gi, gcum[j]) : qk_coef(gi, gcum[j]);
-          v[m] = (j < (is_k ? i : i + 1)) ? v[m] * cf : 0.f;
-        }
-      }
-      if (is_k) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int m = 0; m < 16; ++m) pk[m] = pack_f16(v[2 * m], v[2 * m + 1]);
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch)
-          st_chunk(s_ta, i, j0 / 8 + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
-        const int bb = i >> 4;                 // this row's diagonal block
-        if ((bb >> 1) == gh) {                 // ... lies in this warp's 32 columns
-          const bool hi = bb & 1;
-          float4* dst = reinterpret_cast<float4*>(adg + (bb * 16 + (i & 15)) * L::ADG_LD);
-#pragma unroll
-          for (int m = 0; m < 4; ++m)
-            dst[m] = hi ? make_float4(v[16 + 4 * m], v[17 + 4 * m], v[18 + 4 * m], v[19 + 4 * m])
-                        : make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
-        }
-      } else {
-        uint32_t pk[16];
-#pragma unroll
-        for (int m = 0; m < 16; ++m) pk[m] = pack2<F16>(v[2 * m], v[2 * m + 1]);
-        unsigned char* aq = aqk(c);
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch)
-          st_chunk(aq, i, j0 / 8 + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
-      }
       named_bar_sync(kPrepBar, kPrepThreads);
       if (p == 0) {
         mbar_arrive(&bars[B_KQFREE]);
-        trace_mark(P, c, TR_PREP_EPI);
+        trace_mark<TRACE>(P, c, TR_PREP_EPI);
       }
     };
 
@@ -581,123 +632,84 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       unsigned char* st = stage(c);
       float* ms = misc(c);
       const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
-      unsigned char* s_tx = s_tpp;  // X operand of the inverse UMMAs (T'' buffer, free here)
-      // ---- level 0 (warps 4, 5: one column of a diagonal block per thread) ||
-      //      zero the off-diagonal 16x16 blocks of D (warps 6-11) ----
-      if (warp < 6) {
-        float x[16];
-        const int b = p >> 4, j = p & 15;
-        diag16_col<L::ADG_LD>(adg + b * 16 * L::ADG_LD, j, x);
-        named_bar_sync(3, 64);  // every column solve has read A's diagonal blocks
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          *tile_elem(s_td, 16 * b + i, 16 * b + j) = __float2half_rn(x[i]);
-          adg[(b * 16 + i) * L::ADG_LD + j] = x[i];   // T_bb, fp32, for the 16 -> 32 merge
+      if (p == 0) trace_mark<TRACE>(P, c, TR_INV_START);
+      if (warp < 8) {
+        // ---- level 0 (warp 4 + b): T_bb = (I + N)^-1 of the diagonal block N = A_bb ----
+        inv16_diag(s_ta, s_td, 16 * (warp - 4), l);
+        if (p == 0) trace_mark<TRACE>(P, c, TR_INV_L0);
+        // ---- level 1 (warps 4, 6): T21 = -(T22 A21) T11 for the block pairs (0,1), (2,3) ----
+        named_bar_sync(4 + ((warp - 4) >> 1), 64);
+        if ((warp & 1) == 0) {
+          const int r1 = 16 * (warp - 4) + 16, c1 = r1 - 16;
+          uint32_t a[4], bf[4], za[4];
+          frag_a(s_td, r1, r1, l, a);
+          frag_b2(s_ta, r1, c1, l, bf);
+          float z0[4] = {0.f, 0.f, 0.f, 0.f}, z1[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_f16_16816(z0, a, bf[0], bf[1]);
+          mma_f16_16816(z1, a, bf[2], bf[3]);
+          c_to_a(z0, z1, za);
+          frag_b2(s_td, c1, c1, l, bf);
+          float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_f16_16816(o0, za, bf[0], bf[1]);
+          mma_f16_16816(o1, za, bf[2], bf[3]);
+          st_c(s_td, r1, c1, l, o0, -1.f);
+          st_c(s_td, r1, c1 + 8, l, o1, -1.f);
         }
-      } else {
-        const int pq = p - 64;  // 0..191: two of the 384 off-diagonal 16-byte chunks each
+        if (p == 0) trace_mark<TRACE>(P, c, TR_INV_L1);
+      } else if (!fast) {
+        // slow chunks: Q' = Q e^g in place (warps 8-11)
+        const float* eg = ms + L::M_EG / 4;
+        constexpr int NCH = DK / 8;
+        for (int idx = p - 128; idx < kC * NCH; idx += 128) {
+          const int i = idx / NCH, ch = idx % NCH;
+          unsigned char* reg = st + L::OFF_KQ + (ch >> 3) * L::KQ_REGION + kC * 128;
+          uint4 u4 = ld_chunk(reg, i, ch & 7);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&u4);
+          const float e = eg[i];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int idx = pq + 192 * u, row = idx / 6, k6 = idx % 6;
-          const int blk = row >> 4, ch = k6 + (k6 >= 2 * blk ? 2 : 0);  // skip chunks 2blk, 2blk+1
-          st_chunk(s_td, row, ch, make_uint4(0u, 0u, 0u, 0u));
+          for (int m = 0; m < 4; ++m) {
+            const float2 f = unpack2<F16>(w[m]);
+            w[m] = pack2<F16>(f.x * e, f.y * e);
+          }
+          st_chunk(reg, i, ch & 7, u4);
         }
-        if (!fast) {  // slow chunks: Q' = Q e^g in place
-          const float* eg = ms + L::M_EG / 4;
-          constexpr int NCH = DK / 8;
-          for (int idx = pq; idx < kC * NCH; idx += 192) {
-            const int i = idx / NCH, ch = idx % NCH;
-            unsigned char* reg = st + L::OFF_KQ + (ch >> 3) * L::KQ_REGION + kC * 128;
-            uint4 u4 = ld_chunk(reg, i, ch & 7);
-            uint32_t* w = reinterpret_cast<uint32_t*>(&u4);
-            const float e = eg[i];
+      }
+      // ---- level 2 (warps 4-7): T[32:64, 0:32] = -(T_BB A_BA) T_AA, warp (rb, ch)
+      //      owns rows 32 + 16 rb .. +15 and columns 16 ch .. +15 ----
+      if (warp < 8) {
+        named_bar_sync(3, 128);
+        const int rb = (warp - 4) >> 1, chh = (warp - 4) & 1, R = 32 + 16 * rb;
+        float z[4][4];
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              const float2 f = unpack2<F16>(w[m]);
-              w[m] = pack2<F16>(f.x * e, f.y * e);
-            }
-            st_chunk(reg, i, ch & 7, u4);
+        for (int n = 0; n < 4; ++n) z[n][0] = z[n][1] = z[n][2] = z[n][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          if (rb == 0 && ks == 1) continue;   // T[32:48, 48:64] = 0
+          uint32_t a[4], bf[4];
+          frag_a(s_td, R, 32 + 16 * ks, l, a);
+#pragma unroll
+          for (int np = 0; np < 2; ++np) {
+            frag_b2(s_ta, 32 + 16 * ks, 16 * np, l, bf);
+            mma_f16_16816(z[2 * np], a, bf[0], bf[1]);
+            mma_f16_16816(z[2 * np + 1], a, bf[2], bf[3]);
           }
         }
+        float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          if (chh == 1 && ks == 0) continue;  // T[0:16, 16:32] = 0
+          uint32_t za[4], bf[4];
+          c_to_a(z[2 * ks], z[2 * ks + 1], za);
+          frag_b2(s_td, 16 * ks, 16 * chh, l, bf);
+          mma_f16_16816(o0, za, bf[0], bf[1]);
+          mma_f16_16816(o1, za, bf[2], bf[3]);
+        }
+        st_c(s_td, R, 16 * chh, l, o0, -1.f);
+        st_c(s_td, R, 16 * chh + 8, l, o1, -1.f);
+        if (p == 0) trace_mark<TRACE>(P, c, TR_INV_L2);
       }
       named_bar_sync(kPrepBar, kPrepThreads);
-      // ---- level 1 (SIMT): T21 = -T22 (A21 T11) for block pairs (1,0), (3,2) ----
-      {
-        float* X = reinterpret_cast<float*>(s_tp);  // T' buffer as fp32 scratch [32][18]
-        const int P2 = p >> 7, e = p & 127, r = e >> 3, c0 = (e & 7) * 2;
-        const int r1 = 32 * P2 + 16, c1 = 32 * P2;
-        const float* T11 = adg + (2 * P2) * 16 * L::ADG_LD;
-        const float* T22 = adg + (2 * P2 + 1) * 16 * L::ADG_LD;
-        float2 xx = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float a = __half2float(*tile_elem(s_ta, r1 + r, c1 + k));
-          const float2 t = *reinterpret_cast<const float2*>(T11 + k * L::ADG_LD + c0);
-          xx = __ffma2_rn(make_float2(a, a), t, xx);
-        }
-        *reinterpret_cast<float2*>(X + (P2 * 16 + r) * 18 + c0) = xx;
-        named_bar_sync(kPrepBar, kPrepThreads);
-        float2 yy = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float a = T22[r * L::ADG_LD + k];
-          const float2 t = *reinterpret_cast<const float2*>(X + (P2 * 16 + k) * 18 + c0);
-          yy = __ffma2_rn(make_float2(a, a), t, yy);
-        }
-        *reinterpret_cast<__half2*>(tile_elem(s_td, r1 + r, c1 + c0)) = __floats2half2_rn(-yy.x, -yy.y);
-      }
-      // ---- level 2 (tensor cores): X = A D32, Y = D32 X, T[32:64, 0:32] = -Y ----
-      const int rowq = (l < 16) ? 16 * q + l : -1;  // M=64 accumulator row of this lane
-      {
-        fence_async_smem();
-        named_bar_sync(kPrepBar, kPrepThreads);
-        if (p == 0) mbar_arrive(&bars[B_INVREQ]);
-        sy.wait(&bars[B_INVDONE], 0, 25);          // phases alternate X, Y: X even
-        tc_fence_after();
-        {
-          float a0[16], a1[16];
-          tmem_ld16(t_rw, a0);
-          tmem_ld16(t_rw + 16, a1);
-          tmem_wait_ld();
-          if (rowq >= 0) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int m = 0; m < 8; ++m) {
-              pk[m] = pack_f16(a0[2 * m], a0[2 * m + 1]);
-              pk[8 + m] = pack_f16(a1[2 * m], a1[2 * m + 1]);
-            }
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch)
-              st_chunk(s_tx, rowq, 4 * gh + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
-          }
-        }
-        tc_fence_before();
-        fence_async_smem();
-        named_bar_sync(kPrepBar, kPrepThreads);
-        if (p == 0) mbar_arrive(&bars[B_INVREQ]);
-        sy.wait(&bars[B_INVDONE], 1, 26);
-        tc_fence_after();
-        if (warp == 6 || warp == 7) {  // rows 32-63 x cols 0-31
-          float a0[16], a1[16];
-          tmem_ld16(t_rw, a0);
-          tmem_ld16(t_rw + 16, a1);
-          tmem_wait_ld();
-          if (rowq >= 0) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int m = 0; m < 8; ++m) {
-              pk[m] = pack_f16(-a0[2 * m], -a0[2 * m + 1]);
-              pk[8 + m] = pack_f16(-a1[2 * m], -a1[2 * m + 1]);
-            }
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch)
-              st_chunk(s_td, rowq, ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
-          }
-        }
-        tc_fence_before();
-      }
-      named_bar_sync(kPrepBar, kPrepThreads);
-      if (p == 0) trace_mark(P, c, TR_PREP_INV);
+      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_INV);
       // ---- T' = T * (beta e^g)_j, T'' = T * beta_j (K-major B operands) ----
       {
         const int i = p >> 2, j0 = (p & 3) * 16;
@@ -737,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       named_bar_sync(kPrepBar, kPrepThreads);
       if (p == 0) {
         mbar_arrive(&bars[B_TREADY]);
-        trace_mark(P, c, TR_PREP_TREADY);
+        trace_mark<TRACE>(P, c, TR_PREP_TREADY);
       }
     };
 
@@ -746,23 +758,21 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       // the single W^T tile: chunk c-1's UMMAs (and its slow-path V_new*gamma) are done
       if (c >= 1) sy.wait(&bars[B_SFULL], (c - 1) & 1, 24);
       tc_fence_after();
-      if (p == 0) trace_mark(P, c, TR_PREP_WU);
+      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_WU);
       const int d = (DK == 128) ? r : (l < 16 ? 16 * q + l : -1);
-      float a0[16], a1[16];
-      tmem_ld16(t_rw, a0);
-      tmem_ld16(t_rw + 16, a1);
-      tmem_wait_ld();
-      if (d >= 0) {
-        unsigned char* wt = sm + L::OFF_WT;
-        uint32_t pk[16];
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        float a0[16];
+        tmem_ld16(t_rw + 16 * hh, a0);
+        tmem_wait_ld();
+        if (d >= 0) {
+          uint32_t pk[8];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
-          pk[8 + m] = pack2<F16>(a1[2 * m], a1[2 * m + 1]);
+          for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
+          const int ch = 4 * gh + 2 * hh;
+          st_chunk(sm + L::OFF_WT, d, ch, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+          st_chunk(sm + L::OFF_WT, d, ch + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
         }
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch)
-          st_chunk(wt, d, 4 * gh + ch, make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]));
       }
       tc_fence_before();
       fence_async_smem();
@@ -770,15 +780,19 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       if (p == 0) {
         mbar_arrive(&bars[B_WREADY]);
         mbar_arrive(&bars[B_RWFREE]);
-        trace_mark(P, c, TR_PREP_END);
+        trace_mark<TRACE>(P, c, TR_PREP_END);
       }
     };
 
-    stage_E(0);
-    for (int c = 0; c < nc; ++c) {
-      stage_I(c);
-      if (c + 1 < nc) stage_E(c + 1);
-      stage_R(c);
+    // the strictly upper blocks of the inverse tile stay zero for the whole sequence
+    reinterpret_cast<uint4*>(s_td)[p] = make_uint4(0u, 0u, 0u, 0u);
+    reinterpret_cast<uint4*>(s_td)[p + kPrepThreads] = make_uint4(0u, 0u, 0u, 0u);
+    // E(0), then [I(c), E(c+1), R(c)]; each stage is expanded once (code size: all
+    // sixteen warps run different code, and the kernel's loops must stay cache-resident)
+    for (int c = 0; c <= nc; ++c) {
+      if (c >= 1) stage_I(c - 1);
+      if (c < nc) stage_E(c);
+      if (c >= 1) stage_R(c - 1);
     }
   }
   // =============================================================== SCAN ====
@@ -866,13 +880,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       // ---- (a) V_new^T row v -> bf16 A operands Vn^T and Vn^T*gamma ----
       sy.wait(&bars[B_VNFULL], c & 1, 31);
       tc_fence_after();
-      if (s == 0) trace_mark(P, c, TR_SCAN_VNFULL);
+      if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_VNFULL);
       const bool fastc = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
       if (s < kC) osc[s] = fastc ? P.scale * ms[L::M_EG / 4 + s] : P.scale;
       {
         const uint32_t t_vn = tmem + ((c & 1) ? L::T_VN1 : L::T_VN0) + lane_off;
         const float* gam = ms + L::M_GAM / 4;
-#pragma unroll
+#pragma unroll 1
         for (int c0 = 0; c0 < kC; c0 += 16) {
           float x[16];
           tmem_ld16(t_vn + c0, x);
@@ -899,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       named_bar_sync(kScanBar, 128);
       if (s == 0) {
         mbar_arrive(&bars[B_VNREADY]);
-        trace_mark(P, c, TR_SCAN_VNREADY);
+        trace_mark<TRACE>(P, c, TR_SCAN_VNREADY);
         mbar_arrive(&bars[B_VNFREE0 + (c & 1)]);
         mbar_arrive(&bars[B_EMPTY0 + (c % 3)]);
       }
@@ -907,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       sy.wait(&bars[B_SFULL], c & 1, 32);
       sy.wait(&bars[B_O1DONE], c & 1, 35);  // the output UMMA has read the bf16 S^T copy
       tc_fence_after();
-      if (s == 0) trace_mark(P, c, TR_SCAN_SFULL);
+      if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_SFULL);
       if (c + 1 < nc) {
         sy.wait(&bars[B_GREADY0 + ((c + 1) % 3)], in_par(c + 1), 33);
         state_pass(false, misc(c + 1)[L::M_EGL / 4], nullptr);
@@ -916,7 +930,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         named_bar_sync(kScanBar, 128);
         if (s == 0) {
           mbar_arrive(&bars[B_SREADY]);
-          trace_mark(P, c, TR_SCAN_SREADY);
+          trace_mark<TRACE>(P, c, TR_SCAN_SREADY);
         }
       } else if (P.S_final) {
         state_pass(false, 1.f, P.S_final);
@@ -924,18 +938,20 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       // ---- (c) output: O^T row v -> o[t0 + i, v] ----
       sy.wait(&bars[B_OFULL], c & 1, 34);
       tc_fence_after();
-      if (s == 0) trace_mark(P, c, TR_SCAN_OFULL);
+      if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_OFULL);
       {
-        const int t0 = c * kC;
-#pragma unroll
+        TO* op = obase + static_cast<int64_t>(c * kC) * P.os_t + (v >= 0 ? v : 0);
+#pragma unroll 1
         for (int c0 = 0; c0 < kC; c0 += 16) {
           float x[16];
           tmem_ld16(t_o + c0, x);
           tmem_wait_ld();
           if (v >= 0) {
 #pragma unroll
-            for (int m = 0; m < 16; ++m)
-              obase[static_cast<int64_t>(t0 + c0 + m) * P.os_t + v] = from_f32<TO>(x[m] * osc[c0 + m]);
+            for (int m = 0; m < 16; ++m) {
+              *op = from_f32<TO>(x[m] * osc[c0 + m]);
+              op += P.os_t;
+            }
           }
         }
       }
@@ -943,7 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       named_bar_sync(kScanBar, 128);
       if (s == 0) {
         mbar_arrive(&bars[B_OFREE]);
-        trace_mark(P, c, TR_SCAN_END);
+        trace_mark<TRACE>(P, c, TR_SCAN_END);
       }
     }
   }
@@ -958,6 +974,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem, L::T_COLS);
+  if (TRACE && tid == 0) {
+    // per-CTA record after the chunk table: start ns, end ns, SM id
+    unsigned long long* rec = P.trace + P.trace_chunks * kTraceSlots + 4 * blockIdx.x;
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    rec[0] = t_start;
+    rec[1] = globaltimer_ns();
+    rec[2] = smid;
+  }
 }
 
 }  // namespace tcfwd
@@ -1005,10 +1030,6 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.status = w->d_status;
   P.trace = static_cast<unsigned long long*>(w->trace);
   P.trace_chunks = w->trace_chunks;
-  {
-    const char* ko = getenv("PTOF_KNOCKOUT");
-    P.knockout = ko ? atoi(ko) : 0;
-  }
   P.B = p.B; P.H = p.H; P.T = p.T; P.nc = p.T / kChunk;
   P.gate_mode = p.gate_mode;
   P.beta_dtype = p.beta_dtype;
@@ -1018,7 +1039,8 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.gs_b = sg.b; P.gs_h = sg.h; P.gs_t = sg.t;
   P.os_b = so.b; P.os_h = so.h; P.os_t = so.t;
   P.scale = p.scale;
-  auto kern = tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO>;
+  auto kern = P.trace ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, true>
+                      : tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false>;
   cudaError_t e = set_smem_once(kern, L::BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_tc smem attribute");
   kern<<<p.B * p.H, tcfwd::kThreads, L::BYTES, stream>>>(P);

@@ -327,4 +327,34 @@ __device__ __forceinline__ float2 unpack_f16(uint32_t u) {
   return __half22float2(h);
 }
 
+// --------------------------------------------------------------------------
+// Warp-level fp16 MMA (m16n8k16, fp32 accumulate) for the small latency-bound
+// products of the triangular inverse: fragments stay in registers, so a 16x16
+// product costs a few tens of cycles instead of a tcgen05 issue/commit round trip.
+// Fragment ownership (g = lane / 4, t = lane % 4):
+//   A 16x16 : a0 (g, 2t..2t+1)  a1 (g+8, 2t..)  a2 (g, 2t+8..)  a3 (g+8, 2t+8..)
+//   B 16x8  : b0 (k 2t..2t+1, n g)  b1 (k 2t+8..2t+9, n g)
+//   C 16x8  : c0,c1 (g, 2t..2t+1)   c2,c3 (g+8, 2t..2t+1)
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 }  // namespace ptof
