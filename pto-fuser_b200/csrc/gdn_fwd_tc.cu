@@ -132,12 +132,9 @@ __device__ __forceinline__ void trace_mark(const Params& P, int c, int slot) {
 struct Sync {
   volatile int* abort;
   int* status;
+  // one inlined probe, the bounded loop out of line
   __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, int site) const {
-#if PTOF_SPIN_MODE == 3
-    if (mbar_test_wait(bar, parity)) return true;
-#else
     if (mbar_try_wait(bar, parity)) return true;
-#endif
     return mbar_wait(bar, parity, abort, status, site);
   }
 };
@@ -372,11 +369,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     }
   }
   // ================================================================ MMA ====
-  // Two single-thread UMMA issuers, each blocking on its own in-order stream (a
+  // Three single-thread UMMA issuers, each blocking on its own in-order stream (a
   // commit tracks only the issuing thread's UMMAs, so the streams stay independent):
-  //   warp 1, chain:  C1a (Vn^T = U^T - S^T W^T), C1b (O = S^T Q'^T),
-  //                   C2 (S^T += (Vn^T g) K ; O += Vn^T Aqk^T)
-  //   warp 2, prep:   P0 ([K;Q] K^T), INV x4 ((I+A)^-1 merges), P1 (W^T, U^T)
+  //   warp 1, chain:  Vn^T = U^T - S^T W^T ; S^T += (Vn^T g) K
+  //   warp 2, prep:   [K;Q] K^T ; W^T = K^T T'^T, U^T = V^T T''^T
+  //   warp 3, output: O = S^T Q'^T ; O += Vn^T Aqk^T
+  // The UMMA loops are rolled: issue costs ~120 cycles per UMMA anyway, and the
+  // kernel's per-chunk code must fit the SM's instruction cache.
   else if (warp >= 1 && warp <= 3 && lane == 0) {
     constexpr uint32_t ID_KQ = idesc_f16(128, kC, false, false, !F16);
     constexpr uint32_t ID_WT = idesc_f16(DK, kC, true, false, !F16);
@@ -401,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         sy.wait(&bars[B_WREADY], c & 1, 15);
         tc_fence_after();
         trace_mark<TRACE>(P, c, TR_MMA_C1);
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < DK / 16; ++ks) {
           const uint64_t bd = sdesc_sw128(s_wt + ks * 2048, DK * 128, 1024);
           if constexpr (L::SA_TMEM) umma_ts(t_vn(c), t_sa + ks * 8, bd, ID_VN, 1);
@@ -416,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         // (then free) W^T tile
         const bool fastc = reinterpret_cast<const int*>(misc(c))[L::M_FAST / 4] != 0;
         const uint32_t s_vs = fastc ? s_vnt : s_wt;
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < kC / 16; ++ks)
           umma_ss(t_sm, sdesc_sw128(s_vs + ks * 32, 16, 1024),
                   sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
@@ -431,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         if (c >= 1) sy.wait(&bars[B_OFREE], (c - 1) & 1, 16);
         tc_fence_after();
         const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < DK / 16; ++ks) {
           const uint64_t bd =
               sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + kC * 128 + (ks & 3) * 32, 16, 1024);
@@ -442,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         sy.wait(&bars[B_VNREADY], c & 1, 41);
         tc_fence_after();
         const uint32_t aq = smem_u32(aqk(c));
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < kC / 16; ++ks)
           umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024),
                   sdesc_sw128(aq + ks * 32, 16, 1024), ID_O2, 1);
@@ -450,39 +449,41 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         umma_commit(&bars[B_EMPTY0 + (c % 3)]);
       }
     } else {
-      // P0(c): [K;Q] K^T -> KQ
-      auto issue_p0 = [&](int c) {
-        sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 10);
-        if (c >= 1) sy.wait(&bars[B_KQFREE], (c - 1) & 1, 11);
-        tc_fence_after();
-        const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
-#pragma unroll
-        for (int ks = 0; ks < DK / 16; ++ks) {
-          const uint32_t a = kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32;
-          umma_ss(t_kq, sdesc_sw128(a, 16, 1024), sdesc_sw128(a, 16, 1024), ID_KQ, ks > 0);
+      // P0(c) = [K;Q] K^T -> KQ, then P1(c - 1) = (W^T, U^T) of the previous chunk:
+      // P0(c) needs only E(c - 1) to have drained KQ, P1(c - 1) needs T'(c - 1)
+      for (int c = 0; c <= nc; ++c) {
+        if (c < nc) {
+          sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 10);
+          if (c >= 1) sy.wait(&bars[B_KQFREE], (c - 1) & 1, 11);
+          tc_fence_after();
+          const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
+#pragma unroll 1
+          for (int ks = 0; ks < DK / 16; ++ks) {
+            const uint32_t a = kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32;
+            umma_ss(t_kq, sdesc_sw128(a, 16, 1024), sdesc_sw128(a, 16, 1024), ID_KQ, ks > 0);
+          }
+          umma_commit(&bars[B_KQFULL]);
         }
-        umma_commit(&bars[B_KQFULL]);
-      };
-      issue_p0(0);
-      for (int c = 0; c < nc; ++c) {
-        if (c + 1 < nc) issue_p0(c + 1);   // KQFREE(c) arrives at the end of E(c)
-        // ---- P1(c): W^T = K^T T'^T -> RW ; U^T = V^T T''^T -> VN[c&1] ----
-        sy.wait(&bars[B_TREADY], c & 1, 13);
-        sy.wait(&bars[B_VFULL0 + (c & 1)], (c >> 1) & 1, 18);
-        if (c >= 2) sy.wait(&bars[B_VNFREE0 + (c & 1)], ((c >> 1) + 1) & 1, 19);
-        if (c >= 1) sy.wait(&bars[B_RWFREE], (c - 1) & 1, 9);
-        tc_fence_after();
-        const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
-        const uint32_t vt = smem_u32(vstage(c));
-#pragma unroll
-        for (int ks = 0; ks < kC / 16; ++ks) {
-          umma_ss(t_rw, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024),
-                  sdesc_sw128(s_tp + ks * 32, 16, 1024), ID_WT, ks > 0);
-          umma_ss(t_vn(c), sdesc_sw128(vt + ks * 2048, L::V_REGION, 1024),
-                  sdesc_sw128(s_tpp + ks * 32, 16, 1024), ID_UT, ks > 0);
+        if (c >= 1) {
+          const int cp = c - 1;
+          sy.wait(&bars[B_TREADY], cp & 1, 13);
+          sy.wait(&bars[B_VFULL0 + (cp & 1)], (cp >> 1) & 1, 18);
+          if (cp >= 2) sy.wait(&bars[B_VNFREE0 + (cp & 1)], ((cp >> 1) + 1) & 1, 19);
+          if (cp >= 1) sy.wait(&bars[B_RWFREE], (cp - 1) & 1, 9);
+          tc_fence_after();
+          const uint32_t kq = smem_u32(stage(cp) + L::OFF_KQ);
+          const uint32_t vt = smem_u32(vstage(cp));
+          const uint32_t t_u = t_vn(cp);
+#pragma unroll 1
+          for (int ks = 0; ks < kC / 16; ++ks) {
+            umma_ss(t_rw, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024),
+                    sdesc_sw128(s_tp + ks * 32, 16, 1024), ID_WT, ks > 0);
+            umma_ss(t_u, sdesc_sw128(vt + ks * 2048, L::V_REGION, 1024),
+                    sdesc_sw128(s_tpp + ks * 32, 16, 1024), ID_UT, ks > 0);
+          }
+          umma_commit(&bars[B_WUFULL]);
+          umma_commit(&bars[B_VEMPTY0 + (cp & 1)]);
         }
-        umma_commit(&bars[B_WUFULL]);
-        umma_commit(&bars[B_VEMPTY0 + (c & 1)]);
       }
     }
     umma_commit(&bars[B_DONE]);

@@ -78,9 +78,6 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-#ifndef PTOF_SPIN_MODE
-#define PTOF_SPIN_MODE 1
-#endif
 // try_wait with a suspend-time hint: the thread sleeps until the phase completes or
 // `hint_ns` elapses, so waiting warps do not compete for issue slots.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
@@ -100,21 +97,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // another thread of the CTA already aborted.
 static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, int* status, int site) {
+  if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-#if PTOF_SPIN_MODE == 3
-    for (int i = 0; i < 256; ++i)
-      if (mbar_test_wait(bar, parity)) return true;
-#elif PTOF_SPIN_MODE == 0
-    if (mbar_try_wait(bar, parity)) return true;
-#elif PTOF_SPIN_MODE == 1
     if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
-#else
-    for (int i = 0; i < 64; ++i) {
-      if (mbar_try_wait(bar, parity)) return true;
-      __nanosleep(64);
-    }
-#endif
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1;
