@@ -34,66 +34,78 @@ namespace tcfwd {
 
 constexpr int kC = kChunk;  // 64
 constexpr int kThreads = 512;
-constexpr int kPrepThreads = 256;
-constexpr int kPrepBar = 1, kScanBar = 2;  // named barrier ids
+// named barrier ids: P = warps 4-7 (inverse, T', W^T readout), Q = warps 8-11
+// (kkt/qk epilogue), scan = warps 12-15; 4 and 5 pair warps 4-5 and 6-7
+constexpr int kPBar = 1, kScanBar = 2, kQBar = 3;
 
 // ------------------------------------------------------------------ layout ----
 template <int DK, int DV>
 struct Layout {
   static constexpr int NKB = DK / 64;               // 64-wide d blocks
   static constexpr int NVB = DV / 64;
-  static constexpr bool SA_TMEM = (DV == 128);       // bf16 S^T as a TMEM A operand
-  static_assert(DV <= DK, "the W^T tile doubles as the slow-chunk V_new*gamma tile");
+  // bf16 S^T and bf16 V_new^T (+ V_new^T gamma) as TMEM A operands (M = DV = 128);
+  // the DV = 64 variant keeps them in shared memory
+  static constexpr bool SA_TMEM = (DV == 128);
+  static constexpr bool VN_TMEM = SA_TMEM;
   // input ring (3 stages): [K | Q] per 64-wide d block, then the per-token arrays
   static constexpr int NIN = 3;
   static constexpr int KQ_REGION = 2 * kC * 128;     // K rows 0-63 | Q rows 64-127, 16 KB
   static constexpr int OFF_KQ = 0;                   // within an input stage
-  static constexpr int OFF_MISC = NKB * KQ_REGION;
-  static constexpr int IN_STAGE = OFF_MISC + 3072;
-  // misc sub-offsets (bytes within MISC): per-token fp32 arrays of the chunk
+  static constexpr int IN_STAGE = NKB * KQ_REGION;
+  // per-chunk arrays (one set per input stage, in their own region below): fp32
+  // per-token coefficients, then three scalars
   static constexpr int M_GRAW = 0, M_BRAW = 256, M_GCUM = 512, M_EG = 768, M_BK = 1024,
-                       M_BV = 1280, M_GAM = 1536, M_ROWF = 1792, M_ROWFB = 2048,
-                       M_COLF = 2304, M_EGL = 2560, M_FAST = 2564, M_ENGL = 2568;
+                       M_BV = 1280, M_GAM = 1536, M_ROWFB = 1792, M_COLF = 2048,
+                       M_EGL = 2304, M_FAST = 2308, M_ENGL = 2312;
+  static constexpr int MISC_BYTES = 2432;
   // V ring (2 stages)
   static constexpr int V_REGION = kC * 128;          // 8 KB per 64-wide block
   static constexpr int OFF_V = NIN * IN_STAGE;
   static constexpr int V_STAGE = NVB * V_REGION;
-  // Aqk (2 buffers), W^T (1 buffer; slow chunks reuse it for V_new*gamma)
+  // Aqk (3 buffers), W^T (2 buffers)
   static constexpr int OFF_AQK = OFF_V + 2 * V_STAGE;
-  static constexpr int OFF_WT = OFF_AQK + 2 * kC * 128;
-  // prep buffers
-  static constexpr int OFF_TP = OFF_WT + DK * 128;   // T' bf16 [64 x 64] (also inverse scratch)
-  static constexpr int OFF_TPP = OFF_TP + 8192;      // T''
-  // inverse workspace: fp16 tiles (128B-swizzled, 64 rows x 64) of A and of T
+  static constexpr int WT_BYTES = DK * 128;
+  static constexpr int OFF_WT = OFF_AQK + 3 * kC * 128;
+  // prep buffers: T' and T'' (bf16 WY operands), A (fp16, 2 buffers; the inverse
+  // overwrites A with T in place)
+  static constexpr int OFF_TP = OFF_WT + 2 * WT_BYTES;
+  static constexpr int OFF_TPP = OFF_TP + 8192;
   static constexpr int OFF_TA = OFF_TPP + 8192;
-  static constexpr int OFF_TD = OFF_TA + 8192;
-  // chain buffers
-  static constexpr int OFF_VNT = OFF_TD + 8192;      // bf16 Vn^T [DV x 64]
-  static constexpr int OFF_SA = OFF_VNT + DV * 128;  // bf16 S^T [DV x DK] (smem variant)
+  // shared-memory chain operands of the DV = 64 variant: Vn^T, Vn^T gamma, S^T
+  static constexpr int VNT_BYTES = VN_TMEM ? 0 : DV * 128;
+  static constexpr int OFF_VNT = OFF_TA + 2 * 8192;
+  static constexpr int OFF_VNG = OFF_VNT + VNT_BYTES;
+  static constexpr int OFF_SA = OFF_VNG + VNT_BYTES;
   static constexpr int SA_BYTES = SA_TMEM ? 0 : NKB * DV * 128;
-  static constexpr int OFF_OSC = OFF_SA + SA_BYTES;  // fp32 [64] output multipliers (scan)
+  static constexpr int OFF_MISC = OFF_SA + SA_BYTES;  // 3 x MISC_BYTES
+  static constexpr int OFF_OSC = OFF_MISC + NIN * MISC_BYTES;  // fp32 [64] output multipliers
   static constexpr int OFF_BAR = OFF_OSC + 256;
   static constexpr int BYTES = OFF_BAR + 512 + 1024;  // + alignment slack
   // TMEM columns
   static constexpr int T_SM = 0;                     // fp32 S^T master: DK columns
   static constexpr int T_SA = DK;                    // bf16 S^T: DK/2 columns
-  static constexpr int T_VN0 = DK + (SA_TMEM ? DK / 2 : 0);
+  static constexpr int T_VN0 = DK + (SA_TMEM ? DK / 2 : 0);  // U^T -> V_new^T, 2 buffers
   static constexpr int T_VN1 = T_VN0 + kC;
   static constexpr int T_O = T_VN1 + kC;
   static constexpr int T_KQ = T_O + kC;             // [K;Q] K^T of the chunk in prep
   static constexpr int T_RW = T_KQ + kC;             // W^T of the chunk in prep
   static constexpr int T_COLS = 512;
   static_assert(T_RW + kC <= T_COLS, "TMEM budget");
-  static_assert(BYTES <= 227 * 1024, "smem budget");
+  // the kernel's static shared memory (1 KB) counts against the 227 KB opt-in
+  static_assert(BYTES <= 227 * 1024 - 1024, "smem budget");
 };
 
-// barrier slots (uint64 each) inside the BAR area
+// barrier slots (uint64 each) inside the BAR area. Hand-offs between groups that
+// can run two chunks apart use one barrier per buffer, so a phase parity never
+// aliases a later chunk.
 enum Bar {
   B_FULL0 = 0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_GREADY0, B_GREADY1, B_GREADY2,
-  B_VFULL0, B_VFULL1, B_VEMPTY0, B_VEMPTY1, B_WREADY,
+  B_VFULL0, B_VFULL1, B_VEMPTY0, B_VEMPTY1, B_WREADY0, B_WREADY1, B_WTFREE0, B_WTFREE1,
+  B_AREADY0, B_AREADY1, B_TAFREE0, B_TAFREE1,
   B_KQFULL, B_TREADY, B_WUFULL, B_RWFREE, B_VNFREE0, B_VNFREE1, B_SREADY, B_VNFULL,
-  B_VNREADY, B_SFULL, B_OFULL, B_OFREE, B_DONE, B_KQFREE, B_O1DONE, B_COUNT
+  B_VNREADY, B_SFULL, B_OFULL0, B_OFULL1, B_OFULL2, B_OFREE, B_DONE, B_KQFREE, B_O1DONE, B_COUNT
 };
+static_assert(B_COUNT * 8 + 8 <= 512, "barrier area");
 
 struct Params {
   CUtensorMap mapK, mapQ, mapV;   // 3D maps, box = 64 d x 64 tokens
@@ -292,6 +304,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     for (int i = 0; i < B_COUNT; ++i) mbar_init(&bars[i], 1);
     for (int i = 0; i < 3; ++i) mbar_init(&bars[B_EMPTY0 + i], 3);  // 2 issuers + scan
     mbar_init(&bars[B_DONE], 3);  // the three UMMA issuers
+    if (L::VN_TMEM) {             // the chain and output UMMAs read V_new^T from TMEM
+      mbar_init(&bars[B_VNFREE0], 2);
+      mbar_init(&bars[B_VNFREE1], 2);
+    }
     fence_mbar_init();
   }
   if (warp == 2) {
@@ -305,9 +321,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
 
   // chunk c lives in input stage c % 3 (use index c / 3), V stage c & 1, Aqk buffer c & 1
   auto stage = [&](int c) { return sm + (c % 3) * L::IN_STAGE; };
-  auto misc = [&](int c) { return reinterpret_cast<float*>(stage(c) + L::OFF_MISC); };
+  auto misc = [&](int c) { return reinterpret_cast<float*>(sm + L::OFF_MISC + (c % 3) * L::MISC_BYTES); };
   auto vstage = [&](int c) { return sm + L::OFF_V + (c & 1) * L::V_STAGE; };
-  auto aqk = [&](int c) { return sm + L::OFF_AQK + (c & 1) * (kC * 128); };
+  auto aqk = [&](int c) { return sm + L::OFF_AQK + (c % 3) * (kC * 128); };
   auto in_par = [&](int c) { return static_cast<uint32_t>((c / 3) & 1); };
 
   // ================================================================ TMA ====
@@ -333,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         // token-strided g / beta (token-major layout): plain loads, 2 tokens per lane
         for (int i = lane; i < kC; i += 32) {
           ms[L::M_GRAW / 4 + i] = P.g ? P.g[gb + i * P.gs_t] : 0.f;
-          reinterpret_cast<float*>(st + L::OFF_MISC + L::M_BRAW)[i] =
+          reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(ms) + L::M_BRAW)[i] =
               ld_beta(P.beta, P.beta_dtype, gb + i * P.gs_t);
         }
         __threadfence_block();
@@ -350,8 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
                       kb * 64, y, z);
         }
         if (contiguous) {
-          if (P.g) bulk_load(st + L::OFF_MISC + L::M_GRAW, P.g + gb, kC * 4, &bars[B_FULL0 + s]);
-          bulk_load(st + L::OFF_MISC + L::M_BRAW,
+          if (P.g) bulk_load(reinterpret_cast<unsigned char*>(ms) + L::M_GRAW, P.g + gb, kC * 4, &bars[B_FULL0 + s]);
+          bulk_load(reinterpret_cast<unsigned char*>(ms) + L::M_BRAW,
                     static_cast<const unsigned char*>(P.beta) + gb * gelt, kC * gelt,
                     &bars[B_FULL0 + s]);
         }
@@ -387,46 +403,55 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     const uint32_t t_sm = tmem + L::T_SM, t_sa = tmem + L::T_SA, t_o = tmem + L::T_O,
                    t_kq = tmem + L::T_KQ, t_rw = tmem + L::T_RW;
     const uint32_t s_tp = smem_u32(sm + L::OFF_TP), s_tpp = smem_u32(sm + L::OFF_TPP);
-    const uint32_t s_vnt = smem_u32(sm + L::OFF_VNT), s_wt = smem_u32(sm + L::OFF_WT);
-    const uint32_t s_sa = smem_u32(sm + L::OFF_SA);
+    const uint32_t s_vnt = smem_u32(sm + L::OFF_VNT), s_vng = smem_u32(sm + L::OFF_VNG);
+    const uint32_t s_wt = smem_u32(sm + L::OFF_WT), s_sa = smem_u32(sm + L::OFF_SA);
     auto a_desc_sa = [&](int ks) {  // smem S^T (K-major, DV rows x DK)
       return sdesc_sw128(s_sa + (ks >> 2) * (DV * 128) + (ks & 3) * 32, 16, 1024);
     };
     auto t_vn = [&](int c) { return tmem + ((c & 1) ? L::T_VN1 : L::T_VN0); };
     if (warp == 1) {
-      // chain critical path: C1a (Vn^T = U^T - S^T W^T), C2a (S^T += (Vn^T g) K)
       for (int c = 0; c < nc; ++c) {
         sy.wait(&bars[B_SREADY], c & 1, 14);
-        sy.wait(&bars[B_WREADY], c & 1, 15);
+        sy.wait(&bars[B_WREADY0 + (c & 1)], (c >> 1) & 1, 15);
         tc_fence_after();
         trace_mark<TRACE>(P, c, TR_MMA_C1);
+        const uint32_t wt = s_wt + (c & 1) * L::WT_BYTES;
 #pragma unroll 1
         for (int ks = 0; ks < DK / 16; ++ks) {
-          const uint64_t bd = sdesc_sw128(s_wt + ks * 2048, DK * 128, 1024);
+          const uint64_t bd = sdesc_sw128(wt + ks * 2048, DK * 128, 1024);
           if constexpr (L::SA_TMEM) umma_ts(t_vn(c), t_sa + ks * 8, bd, ID_VN, 1);
           else umma_ss(t_vn(c), a_desc_sa(ks), bd, ID_VN, 1);
         }
         umma_commit(&bars[B_VNFULL]);
+        umma_commit(&bars[B_WTFREE0 + (c & 1)]);
         sy.wait(&bars[B_VNREADY], c & 1, 17);
         tc_fence_after();
         trace_mark<TRACE>(P, c, TR_MMA_C2);
         const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
-        // fast chunks carry V_new*gamma in the Vn^T tile itself; slow chunks in the
-        // (then free) W^T tile
+        // fast chunks: gamma is folded into U^T and W^T, so Vn^T itself; slow chunks:
+        // the separate Vn^T gamma operand
         const bool fastc = reinterpret_cast<const int*>(misc(c))[L::M_FAST / 4] != 0;
-        const uint32_t s_vs = fastc ? s_vnt : s_wt;
+        if constexpr (L::VN_TMEM) {
+          const uint32_t a0 = t_vn(c) + (fastc ? 0 : kC / 2);
 #pragma unroll 1
-        for (int ks = 0; ks < kC / 16; ++ks)
-          umma_ss(t_sm, sdesc_sw128(s_vs + ks * 32, 16, 1024),
-                  sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
+          for (int ks = 0; ks < kC / 16; ++ks)
+            umma_ts(t_sm, a0 + ks * 8, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
+        } else {
+          const uint32_t s_vs = fastc ? s_vnt : s_vng;
+#pragma unroll 1
+          for (int ks = 0; ks < kC / 16; ++ks)
+            umma_ss(t_sm, sdesc_sw128(s_vs + ks * 32, 16, 1024),
+                    sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
+        }
         umma_commit(&bars[B_SFULL]);
         umma_commit(&bars[B_EMPTY0 + (c % 3)]);
+        if (L::VN_TMEM) umma_commit(&bars[B_VNFREE0 + (c & 1)]);
       }
     } else if (warp == 3) {
-      // output: C1b (O = S^T Q'^T), C2b (O += Vn^T Aqk^T)
       for (int c = 0; c < nc; ++c) {
         sy.wait(&bars[B_SREADY], c & 1, 40);
-        sy.wait(&bars[B_WREADY], c & 1, 42);   // Q' of slow chunks is written by then
+        // Q' of slow chunks is written before A(c) is handed over, long before W^T(c)
+        sy.wait(&bars[B_WREADY0 + (c & 1)], (c >> 1) & 1, 42);
         if (c >= 1) sy.wait(&bars[B_OFREE], (c - 1) & 1, 16);
         tc_fence_after();
         const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
@@ -442,11 +467,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         tc_fence_after();
         const uint32_t aq = smem_u32(aqk(c));
 #pragma unroll 1
-        for (int ks = 0; ks < kC / 16; ++ks)
-          umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024),
-                  sdesc_sw128(aq + ks * 32, 16, 1024), ID_O2, 1);
-        umma_commit(&bars[B_OFULL]);
+        for (int ks = 0; ks < kC / 16; ++ks) {
+          const uint64_t bd = sdesc_sw128(aq + ks * 32, 16, 1024);
+          if constexpr (L::VN_TMEM) umma_ts(t_o, t_vn(c) + ks * 8, bd, ID_O2, 1);
+          else umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024), bd, ID_O2, 1);
+        }
+        umma_commit(&bars[B_OFULL0 + (c % 3)]);
         umma_commit(&bars[B_EMPTY0 + (c % 3)]);
+        if (L::VN_TMEM) umma_commit(&bars[B_VNFREE0 + (c & 1)]);
       }
     } else {
       // P0(c) = [K;Q] K^T -> KQ, then P1(c - 1) = (W^T, U^T) of the previous chunk:
@@ -489,32 +517,25 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     umma_commit(&bars[B_DONE]);
   }
   // =============================================================== PREP ====
-  // 256 threads: warps 4-11. Warp quadrant q = warp & 3 selects TMEM lanes 32q..32q+31
-  // (row r = 32q + lane); column half gh = (warp - 4) >> 2 selects tile columns
-  // [32 gh, 32 gh + 32). Software-pipelined over chunks:
-  //   E(c): coefficients, [K;Q]K^T epilogue -> A (fp32 workspace) and Aqk (bf16 tile)
-  //   I(c): (I + A)^-1, Q' = Q e^g, T' and T''            -> UMMA W^T, U^T
-  //   R(c): W^T readout                                    -> chain of chunk c
-  // in the order E(0), [I(c), E(c+1), R(c)] so the two UMMA latencies hide behind E.
-  else if (warp >= 4 && warp < 12) {
-    const int p = tid - 128, q = warp & 3, gh = (warp - 4) >> 2, l = lane;
+  // Two warpgroups, each one chunk at a time, handing chunks over through mbarriers:
+  //   Q (warps 8-11)  E(c): coefficients, [K;Q]K^T epilogue -> A (fp16, 2 buffers)
+  //                   and Aqk (2 buffers), slow chunks: Q' = Q e^g
+  //   P (warps 4-7)   I(c): (I + A)^-1, T' and T'' -> UMMA W^T, U^T;
+  //                   R(c - 1): W^T readout (2 buffers) -> chain of chunk c - 1
+  // so E(c + 1) runs beside I(c) and the readout lags one chunk behind its UMMA.
+  // Warp quadrant q = warp & 3 selects TMEM lanes 32q..32q+31 (row r = 32q + lane).
+  else if (warp >= 8 && warp < 12) {
+    const int qp = tid - 256, q = warp & 3, l = lane;
     const int r = 32 * q + l;
-    unsigned char* s_ta = sm + L::OFF_TA;   // A (fp16)
-    unsigned char* s_td = sm + L::OFF_TD;   // D: block-diagonal partial inverse (fp16)
-    unsigned char* s_tp = sm + L::OFF_TP;
-    unsigned char* s_tpp = sm + L::OFF_TPP;
-    const uint32_t lane_off = (32u * q) << 16;
-    const uint32_t t_kq = tmem + L::T_KQ + lane_off + 32 * gh;
-    const uint32_t t_rw = tmem + L::T_RW + lane_off + 32 * gh;
-
-    auto stage_E = [&](int c) {
+    const uint32_t t_kq = tmem + L::T_KQ + ((32u * q) << 16);
+    for (int c = 0; c < nc; ++c) {
       unsigned char* st = stage(c);
       float* ms = misc(c);
       const float* gcum = ms + L::M_GCUM / 4;
       sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 20);
-      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_FULL);
-      // ---- per-token coefficients (warp 4: tokens 2l, 2l+1) ----
-      if (warp == 4) {
+      if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_FULL);
+      // ---- per-token coefficients (warp 8: tokens 2l, 2l+1) ----
+      if (warp == 8) {
         float g0 = 0.f, g1 = 0.f;
         if (P.gate_mode != PTOF_GATE_NONE) {
           g0 = ms[L::M_GRAW / 4 + 2 * l];
@@ -536,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
           mono = (g1 <= g0) && (l == 0 || g0 <= prev);
         }
-        if (p == 0) trace_mark<TRACE>(P, c, TR_X0);
+        if (qp == 0) trace_mark<TRACE>(P, c, TR_X0);
         const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
         const float gl = __shfl_sync(0xffffffffu, g1, 31);
         // exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j): overflow-free when the chunk's
@@ -544,14 +565,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         const bool fast = !F16 && __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
         float b0, b1;
         if (P.gs_t == 1 && P.beta_dtype != PTOF_F32) {
-          const uint32_t u = reinterpret_cast<const uint32_t*>(st + L::OFF_MISC + L::M_BRAW)[l];
+          const uint32_t u = reinterpret_cast<const uint32_t*>(reinterpret_cast<const unsigned char*>(ms) + L::M_BRAW)[l];
           const float2 f = (P.beta_dtype == PTOF_F16) ? unpack_f16(u) : unpack_bf16(u);
           b0 = f.x; b1 = f.y;
         } else {
-          const float* bf = reinterpret_cast<const float*>(st + L::OFF_MISC + L::M_BRAW);
+          const float* bf = reinterpret_cast<const float*>(reinterpret_cast<const unsigned char*>(ms) + L::M_BRAW);
           b0 = bf[2 * l]; b1 = bf[2 * l + 1];
         }
-        if (p == 0) trace_mark<TRACE>(P, c, TR_X1);
+        if (qp == 0) trace_mark<TRACE>(P, c, TR_X1);
         const float e0 = __expf(g0), e1 = __expf(g1);
         const float rf0 = __expf(g0 - gfirst), rf1 = __expf(g1 - gfirst);
         float2* m2 = reinterpret_cast<float2*>(ms);
@@ -560,7 +581,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         m2[L::M_BK / 8 + l] = make_float2(b0 * e0, b1 * e1);
         m2[L::M_BV / 8 + l] = make_float2(b0, b1);
         m2[L::M_GAM / 8 + l] = make_float2(__expf(gl - g0), __expf(gl - g1));
-        m2[L::M_ROWF / 8 + l] = make_float2(rf0, rf1);
         m2[L::M_ROWFB / 8 + l] = make_float2(rf0 * b0, rf1 * b1);
         m2[L::M_COLF / 8 + l] = make_float2(__expf(gfirst - g0), __expf(gfirst - g1));
         if (l == 0) {
@@ -569,31 +589,31 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           reinterpret_cast<int*>(ms)[L::M_FAST / 4] = fast ? 1 : 0;
         }
       }
-      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_COEF);
-      named_bar_sync(kPrepBar, kPrepThreads);
-      if (p == 0) mbar_arrive(&bars[B_GREADY0 + (c % 3)]);
+      if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_COEF);
+      named_bar_sync(kQBar, 128);
+      if (qp == 0) mbar_arrive(&bars[B_GREADY0 + (c % 3)]);
       const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
-      // ---- A = gated strict-lower KK^T (rows 0-63), Aqk = gated causal QK^T (64-127) ----
-      // the Aqk buffer of chunk c last fed chunk c-2's output UMMA
-      if (c >= 2) sy.wait(&bars[B_OFULL], c & 1, 23);
-      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_OFULL);
+      // A buffer c & 1 last held A(c - 2) / T(c - 2); Aqk buffer c % 3 last fed O(c - 3)
+      if (c >= 2) sy.wait(&bars[B_TAFREE0 + (c & 1)], ((c >> 1) + 1) & 1, 23);
+      if (c >= 3) sy.wait(&bars[B_OFULL0 + (c % 3)], in_par(c) ^ 1, 24);
+      if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_OFULL);
       sy.wait(&bars[B_KQFULL], c & 1, 21);
       tc_fence_after();
-      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_KQ);
-      // one 16-column half of this warp's 32 columns per iteration (rolled: the prep
-      // loop's code must stay small enough for the SM's instruction cache)
+      if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_KQ);
+      // ---- A = gated strict-lower KK^T (rows 0-63), Aqk = gated causal QK^T (64-127),
+      //      16 columns per iteration (rolled: the per-chunk code of all warps must
+      //      fit the SM's instruction cache) ----
       const int i = r & 63;
       const bool is_k = r < 64;
       const int lim = is_k ? i : i + 1;       // strict lower (A) / causal (Aqk)
       // fast chunks: A = rowf_i beta_i colf_j KK^T and Aqk = e^{-gl} QK^T (the e^{g_i}
       // of the score is applied at the output)
       const float rowm = is_k ? ms[L::M_ROWFB / 4 + i] : ms[L::M_ENGL / 4];
-      unsigned char* dst = is_k ? s_ta : aqk(c);
+      unsigned char* dst = is_k ? (sm + L::OFF_TA + (c & 1) * 8192) : aqk(c);
 #pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        const int j0 = 32 * gh + 16 * hh;
+      for (int j0 = 0; j0 < kC; j0 += 16) {
         float v[16];
-        tmem_ld16(t_kq + 16 * hh, v);
+        tmem_ld16(t_kq + j0, v);
         tmem_wait_ld();
         if (fast) {
 #pragma unroll
@@ -622,23 +642,51 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         st_chunk(dst, i, j0 / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
       }
       tc_fence_before();
-      named_bar_sync(kPrepBar, kPrepThreads);
-      if (p == 0) {
+      if (!fast) {
+        // slow chunks: Q' = Q e^g in place (P0 has read Q: KQFULL)
+        const float* eg = ms + L::M_EG / 4;
+        constexpr int NCH = DK / 8;
+        for (int idx = qp; idx < kC * NCH; idx += 128) {
+          const int ii = idx / NCH, ch = idx % NCH;
+          unsigned char* reg = st + L::OFF_KQ + (ch >> 3) * L::KQ_REGION + kC * 128;
+          uint4 u4 = ld_chunk(reg, ii, ch & 7);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&u4);
+          const float e = eg[ii];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const float2 f = unpack2<F16>(w[m]);
+            w[m] = pack2<F16>(f.x * e, f.y * e);
+          }
+          st_chunk(reg, ii, ch & 7, u4);
+        }
+      }
+      fence_async_smem();   // Aqk and Q' are read by the UMMA unit
+      named_bar_sync(kQBar, 128);
+      if (qp == 0) {
         mbar_arrive(&bars[B_KQFREE]);
+        mbar_arrive(&bars[B_AREADY0 + (c & 1)]);
         trace_mark<TRACE>(P, c, TR_PREP_EPI);
       }
-    };
-
-    auto stage_I = [&](int c) {
-      unsigned char* st = stage(c);
-      float* ms = misc(c);
-      const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
-      if (p == 0) trace_mark<TRACE>(P, c, TR_INV_START);
-      if (warp < 8) {
-        // ---- level 0 (warp 4 + b): T_bb = (I + N)^-1 of the diagonal block N = A_bb ----
+    }
+  } else if (warp >= 4 && warp < 8) {
+    const int pp = tid - 128, q = warp & 3, l = lane;
+    unsigned char* s_tp = sm + L::OFF_TP;
+    unsigned char* s_tpp = sm + L::OFF_TPP;
+    const uint32_t t_rw = tmem + L::T_RW + ((32u * q) << 16);
+    for (int c = 0; c <= nc; ++c) {
+      if (c < nc) {
+        // ================= I(c): T = (I + A)^-1, T' and T'' =================
+        float* ms = misc(c);
+        sy.wait(&bars[B_AREADY0 + (c & 1)], (c >> 1) & 1, 25);
+        const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
+        // A(c) in, T(c) out, in place (the strictly upper blocks of A are zero)
+        unsigned char* s_ta = sm + L::OFF_TA + (c & 1) * 8192;
+        unsigned char* s_td = s_ta;
+        if (pp == 0) trace_mark<TRACE>(P, c, TR_INV_START);
+        // level 0 (warp 4 + b): T_bb = (I + N)^-1 of the diagonal block N = A_bb
         inv16_diag(s_ta, s_td, 16 * (warp - 4), l);
-        if (p == 0) trace_mark<TRACE>(P, c, TR_INV_L0);
-        // ---- level 1 (warps 4, 6): T21 = -(T22 A21) T11 for the block pairs (0,1), (2,3) ----
+        if (pp == 0) trace_mark<TRACE>(P, c, TR_INV_L0);
+        // level 1 (warps 4, 6): T21 = -(T22 A21) T11 for the block pairs (0,1), (2,3)
         named_bar_sync(4 + ((warp - 4) >> 1), 64);
         if ((warp & 1) == 0) {
           const int r1 = 16 * (warp - 4) + 16, c1 = r1 - 16;
@@ -656,144 +704,117 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           st_c(s_td, r1, c1, l, o0, -1.f);
           st_c(s_td, r1, c1 + 8, l, o1, -1.f);
         }
-        if (p == 0) trace_mark<TRACE>(P, c, TR_INV_L1);
-      } else if (!fast) {
-        // slow chunks: Q' = Q e^g in place (warps 8-11)
-        const float* eg = ms + L::M_EG / 4;
-        constexpr int NCH = DK / 8;
-        for (int idx = p - 128; idx < kC * NCH; idx += 128) {
-          const int i = idx / NCH, ch = idx % NCH;
-          unsigned char* reg = st + L::OFF_KQ + (ch >> 3) * L::KQ_REGION + kC * 128;
-          uint4 u4 = ld_chunk(reg, i, ch & 7);
-          uint32_t* w = reinterpret_cast<uint32_t*>(&u4);
-          const float e = eg[i];
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float2 f = unpack2<F16>(w[m]);
-            w[m] = pack2<F16>(f.x * e, f.y * e);
-          }
-          st_chunk(reg, i, ch & 7, u4);
-        }
-      }
-      // ---- level 2 (warps 4-7): T[32:64, 0:32] = -(T_BB A_BA) T_AA, warp (rb, ch)
-      //      owns rows 32 + 16 rb .. +15 and columns 16 ch .. +15 ----
-      if (warp < 8) {
-        named_bar_sync(3, 128);
-        const int rb = (warp - 4) >> 1, chh = (warp - 4) & 1, R = 32 + 16 * rb;
-        float z[4][4];
-#pragma unroll
-        for (int n = 0; n < 4; ++n) z[n][0] = z[n][1] = z[n][2] = z[n][3] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          if (rb == 0 && ks == 1) continue;   // T[32:48, 48:64] = 0
-          uint32_t a[4], bf[4];
-          frag_a(s_td, R, 32 + 16 * ks, l, a);
-#pragma unroll
-          for (int np = 0; np < 2; ++np) {
-            frag_b2(s_ta, 32 + 16 * ks, 16 * np, l, bf);
-            mma_f16_16816(z[2 * np], a, bf[0], bf[1]);
-            mma_f16_16816(z[2 * np + 1], a, bf[2], bf[3]);
-          }
-        }
-        float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          if (chh == 1 && ks == 0) continue;  // T[0:16, 16:32] = 0
-          uint32_t za[4], bf[4];
-          c_to_a(z[2 * ks], z[2 * ks + 1], za);
-          frag_b2(s_td, 16 * ks, 16 * chh, l, bf);
-          mma_f16_16816(o0, za, bf[0], bf[1]);
-          mma_f16_16816(o1, za, bf[2], bf[3]);
-        }
-        st_c(s_td, R, 16 * chh, l, o0, -1.f);
-        st_c(s_td, R, 16 * chh + 8, l, o1, -1.f);
-        if (p == 0) trace_mark<TRACE>(P, c, TR_INV_L2);
-      }
-      named_bar_sync(kPrepBar, kPrepThreads);
-      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_INV);
-      // ---- T' = T * (beta e^g)_j, T'' = T * beta_j (K-major B operands) ----
-      {
-        const int i = p >> 2, j0 = (p & 3) * 16;
-        float tv[16];
+        if (pp == 0) trace_mark<TRACE>(P, c, TR_INV_L1);
+        // level 2: T[32:64, 0:32] = -(T_BB A_BA) T_AA; warp (rb, ch) owns rows
+        // 32 + 16 rb .. +15 and columns 16 ch .. +15
+        named_bar_sync(kPBar, 128);
         {
-          const uint4 u0 = ld_chunk(s_td, i, j0 / 8), u1 = ld_chunk(s_td, i, j0 / 8 + 1);
-          const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+          const int rb = (warp - 4) >> 1, chh = (warp - 4) & 1, R = 32 + 16 * rb;
+          float z[4][4];
 #pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            const float2 f = unpack_f16(w[m]);
-            tv[2 * m] = f.x;
-            tv[2 * m + 1] = f.y;
+          for (int n = 0; n < 4; ++n) zero4(z[n]);
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            if (rb == 0 && ks == 1) continue;   // T[32:48, 48:64] = 0
+            uint32_t a[4], bf[4];
+            frag_a(s_td, R, 32 + 16 * ks, l, a);
+#pragma unroll
+            for (int np = 0; np < 2; ++np) {
+              frag_b2(s_ta, 32 + 16 * ks, 16 * np, l, bf);
+              mma_f16_16816(z[2 * np], a, bf[0], bf[1]);
+              mma_f16_16816(z[2 * np + 1], a, bf[2], bf[3]);
+            }
+          }
+          float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            if (chh == 1 && ks == 0) continue;  // T[0:16, 16:32] = 0
+            uint32_t za[4], bf[4];
+            c_to_a(z[2 * ks], z[2 * ks + 1], za);
+            frag_b2(s_td, 16 * ks, 16 * chh, l, bf);
+            mma_f16_16816(o0, za, bf[0], bf[1]);
+            mma_f16_16816(o1, za, bf[2], bf[3]);
+          }
+          named_bar_sync(kPBar, 128);   // every warp has read A_BA before T_BA replaces it
+          st_c(s_td, R, 16 * chh, l, o0, -1.f);
+          st_c(s_td, R, 16 * chh + 8, l, o1, -1.f);
+        }
+        named_bar_sync(kPBar, 128);
+        if (pp == 0) trace_mark<TRACE>(P, c, TR_PREP_INV);
+        // ---- T' = T * (beta e^g)_j, T'' = T * beta_j (K-major B operands); fast
+        //      chunks also scale row i by gamma_i so the UMMAs yield W^T g, U^T g.
+        //      T' / T'' of chunk c - 1 must have been consumed (WUFULL(c - 1)). ----
+        if (c >= 1) sy.wait(&bars[B_WUFULL], (c - 1) & 1, 26);
+        {
+          const int i = pp >> 1;
+          const float gi = fast ? ms[L::M_GAM / 4 + i] : 1.f;
+#pragma unroll 1
+          for (int j0 = 32 * (pp & 1); j0 < 32 * (pp & 1) + 32; j0 += 16) {
+            float tv[16];
+            {
+              const uint4 u0 = ld_chunk(s_td, i, j0 / 8), u1 = ld_chunk(s_td, i, j0 / 8 + 1);
+              const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+              for (int m = 0; m < 8; ++m) {
+                const float2 f = unpack_f16(w[m]);
+                tv[2 * m] = f.x * gi;
+                tv[2 * m + 1] = f.y * gi;
+              }
+            }
+            const float* bk = ms + L::M_BK / 4 + j0;
+            const float* bv = ms + L::M_BV / 4 + j0;
+            uint32_t a[8], bb[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+              a[m] = pack2<F16>(tv[2 * m] * bk[2 * m], tv[2 * m + 1] * bk[2 * m + 1]);
+              bb[m] = pack2<F16>(tv[2 * m] * bv[2 * m], tv[2 * m + 1] * bv[2 * m + 1]);
+            }
+            st_chunk(s_tp, i, j0 / 8, make_uint4(a[0], a[1], a[2], a[3]));
+            st_chunk(s_tp, i, j0 / 8 + 1, make_uint4(a[4], a[5], a[6], a[7]));
+            st_chunk(s_tpp, i, j0 / 8, make_uint4(bb[0], bb[1], bb[2], bb[3]));
+            st_chunk(s_tpp, i, j0 / 8 + 1, make_uint4(bb[4], bb[5], bb[6], bb[7]));
           }
         }
-
-        const float4* bk = reinterpret_cast<const float4*>(ms + L::M_BK / 4 + j0);
-        const float4* bv = reinterpret_cast<const float4*>(ms + L::M_BV / 4 + j0);
-        // fast chunks: rows scaled by gamma_i so the UMMAs yield W^T g and U^T g
-        const float gi = fast ? ms[L::M_GAM / 4 + i] : 1.f;
-        uint32_t a[8], bb[8];
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          float4 t = make_float4(tv[4 * m], tv[4 * m + 1], tv[4 * m + 2], tv[4 * m + 3]);
-          t.x *= gi; t.y *= gi; t.z *= gi; t.w *= gi;
-          const float4 k4 = bk[m], v4 = bv[m];
-          a[2 * m] = pack2<F16>(t.x * k4.x, t.y * k4.y);
-          a[2 * m + 1] = pack2<F16>(t.z * k4.z, t.w * k4.w);
-          bb[2 * m] = pack2<F16>(t.x * v4.x, t.y * v4.y);
-          bb[2 * m + 1] = pack2<F16>(t.z * v4.z, t.w * v4.w);
+        fence_async_smem();
+        named_bar_sync(kPBar, 128);
+        if (pp == 0) {
+          mbar_arrive(&bars[B_TAFREE0 + (c & 1)]);   // T(c) fully read
+          mbar_arrive(&bars[B_TREADY]);
+          trace_mark<TRACE>(P, c, TR_PREP_TREADY);
         }
-        st_chunk(s_tp, i, j0 / 8, make_uint4(a[0], a[1], a[2], a[3]));
-        st_chunk(s_tp, i, j0 / 8 + 1, make_uint4(a[4], a[5], a[6], a[7]));
-        st_chunk(s_tpp, i, j0 / 8, make_uint4(bb[0], bb[1], bb[2], bb[3]));
-        st_chunk(s_tpp, i, j0 / 8 + 1, make_uint4(bb[4], bb[5], bb[6], bb[7]));
       }
-      fence_async_smem();
-      named_bar_sync(kPrepBar, kPrepThreads);
-      if (p == 0) {
-        mbar_arrive(&bars[B_TREADY]);
-        trace_mark<TRACE>(P, c, TR_PREP_TREADY);
-      }
-    };
-
-    auto stage_R = [&](int c) {
-      sy.wait(&bars[B_WUFULL], c & 1, 22);
-      // the single W^T tile: chunk c-1's UMMAs (and its slow-path V_new*gamma) are done
-      if (c >= 1) sy.wait(&bars[B_SFULL], (c - 1) & 1, 24);
-      tc_fence_after();
-      if (p == 0) trace_mark<TRACE>(P, c, TR_PREP_WU);
-      const int d = (DK == 128) ? r : (l < 16 ? 16 * q + l : -1);
+      if (c >= 1) {
+        // ================= R(c - 1): W^T readout =================
+        const int cp = c - 1;
+        sy.wait(&bars[B_WUFULL], cp & 1, 27);
+        // W^T buffer cp & 1 was last read by the chain UMMA of chunk cp - 2
+        if (cp >= 2) sy.wait(&bars[B_WTFREE0 + (cp & 1)], ((cp >> 1) + 1) & 1, 28);
+        tc_fence_after();
+        if (pp == 0) trace_mark<TRACE>(P, cp, TR_PREP_WU);
+        unsigned char* wt = sm + L::OFF_WT + (cp & 1) * L::WT_BYTES;
+        const int d = (DK == 128) ? 32 * q + l : (l < 16 ? 16 * q + l : -1);
 #pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        float a0[16];
-        tmem_ld16(t_rw + 16 * hh, a0);
-        tmem_wait_ld();
-        if (d >= 0) {
-          uint32_t pk[8];
+        for (int j0 = 0; j0 < kC; j0 += 16) {
+          float a0[16];
+          tmem_ld16(t_rw + j0, a0);
+          tmem_wait_ld();
+          if (d >= 0) {
+            uint32_t pk[8];
 #pragma unroll
-          for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
-          const int ch = 4 * gh + 2 * hh;
-          st_chunk(sm + L::OFF_WT, d, ch, make_uint4(pk[0], pk[1], pk[2], pk[3]));
-          st_chunk(sm + L::OFF_WT, d, ch + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
+            for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
+            st_chunk(wt, d, j0 / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+            st_chunk(wt, d, j0 / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
+          }
+        }
+        tc_fence_before();
+        fence_async_smem();
+        named_bar_sync(kPBar, 128);
+        if (pp == 0) {
+          mbar_arrive(&bars[B_WREADY0 + (cp & 1)]);
+          mbar_arrive(&bars[B_RWFREE]);
+          trace_mark<TRACE>(P, cp, TR_PREP_END);
         }
       }
-      tc_fence_before();
-      fence_async_smem();
-      named_bar_sync(kPrepBar, kPrepThreads);
-      if (p == 0) {
-        mbar_arrive(&bars[B_WREADY]);
-        mbar_arrive(&bars[B_RWFREE]);
-        trace_mark<TRACE>(P, c, TR_PREP_END);
-      }
-    };
-
-    // the strictly upper blocks of the inverse tile stay zero for the whole sequence
-    reinterpret_cast<uint4*>(s_td)[p] = make_uint4(0u, 0u, 0u, 0u);
-    reinterpret_cast<uint4*>(s_td)[p + kPrepThreads] = make_uint4(0u, 0u, 0u, 0u);
-    // E(0), then [I(c), E(c+1), R(c)]; each stage is expanded once (code size: all
-    // sixteen warps run different code, and the kernel's loops must stay cache-resident)
-    for (int c = 0; c <= nc; ++c) {
-      if (c >= 1) stage_I(c - 1);
-      if (c < nc) stage_E(c);
-      if (c >= 1) stage_R(c - 1);
     }
   }
   // =============================================================== SCAN ====
@@ -804,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     const uint32_t t_sm = tmem + L::T_SM + lane_off, t_sa = tmem + L::T_SA + lane_off;
     const uint32_t t_o = tmem + L::T_O + lane_off;
     unsigned char* s_vnt = sm + L::OFF_VNT;
-    unsigned char* s_vng = sm + L::OFF_WT;   // slow chunks: V_new*gamma in the free W^T tile
+    unsigned char* s_vng = sm + L::OFF_VNG;
     unsigned char* s_sa = sm + L::OFF_SA;
     (void)s_sa;
     float* osc = reinterpret_cast<float*>(sm + L::OFF_OSC);
@@ -884,9 +905,35 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_VNFULL);
       const bool fastc = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
       if (s < kC) osc[s] = fastc ? P.scale * ms[L::M_EG / 4 + s] : P.scale;
-      {
-        const uint32_t t_vn = tmem + ((c & 1) ? L::T_VN1 : L::T_VN0) + lane_off;
-        const float* gam = ms + L::M_GAM / 4;
+      const uint32_t t_vn = tmem + ((c & 1) ? L::T_VN1 : L::T_VN0) + lane_off;
+      const float* gam = ms + L::M_GAM / 4;
+      if constexpr (L::VN_TMEM) {
+        // in place: the fp32 row (64 columns) becomes bf16 Vn^T in columns 0-31 and,
+        // for slow chunks, bf16 Vn^T gamma in columns 32-63 (TMEM A operands)
+        float x[kC];
+#pragma unroll
+        for (int c0 = 0; c0 < kC; c0 += 16) tmem_ld16(t_vn + c0, *reinterpret_cast<float(*)[16]>(x + c0));
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+          for (int m = 0; m < 16; ++m) pk[m] = pack2<F16>(x[32 * hh + 2 * m], x[32 * hh + 2 * m + 1]);
+          tmem_st16(t_vn + 16 * hh, pk);
+        }
+        if (!fastc) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+              const int t = 32 * hh + 2 * m;
+              pk[m] = pack2<F16>(x[t] * gam[t], x[t + 1] * gam[t + 1]);
+            }
+            tmem_st16(t_vn + kC / 2 + 16 * hh, pk);
+          }
+        }
+        tmem_wait_st();
+      } else {
 #pragma unroll 1
         for (int c0 = 0; c0 < kC; c0 += 16) {
           float x[16];
@@ -908,14 +955,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
             }
           }
         }
+        fence_async_smem();
       }
       tc_fence_before();
-      fence_async_smem();
       named_bar_sync(kScanBar, 128);
       if (s == 0) {
         mbar_arrive(&bars[B_VNREADY]);
         trace_mark<TRACE>(P, c, TR_SCAN_VNREADY);
-        mbar_arrive(&bars[B_VNFREE0 + (c & 1)]);
+        if (!L::VN_TMEM) mbar_arrive(&bars[B_VNFREE0 + (c & 1)]);
         mbar_arrive(&bars[B_EMPTY0 + (c % 3)]);
       }
       // ---- (b) state: S^T_{c+1} ready -> bf16 copy, pre-scale by e^{gl_{c+1}} ----
@@ -937,7 +984,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         state_pass(false, 1.f, P.S_final);
       }
       // ---- (c) output: O^T row v -> o[t0 + i, v] ----
-      sy.wait(&bars[B_OFULL], c & 1, 34);
+      sy.wait(&bars[B_OFULL0 + (c % 3)], in_par(c), 34);
       tc_fence_after();
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_OFULL);
       {
