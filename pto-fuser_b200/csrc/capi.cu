@@ -180,7 +180,17 @@ void* ptof_gdn_fwd_setup(const ptof_gdn_params* p) {
     return nullptr;
   }
   if (validate_gdn(*p) != PTOF_OK) return nullptr;
-  return ws_create(kWsGdnFwd, p);
+  Workspace* w = ws_create(kWsGdnFwd, p);
+  if (w && p->in_dtype != PTOF_F32 && gdn_fwd_tc_supports(*p)) {
+    w->scratch_bytes = gdn_fwd_tc_scratch_bytes(*p);
+    const cudaError_t e = cudaMalloc(&w->d_scratch, w->scratch_bytes);
+    if (e != cudaSuccess) {
+      cuda_fail(e, "gdn_fwd coefficient buffer");
+      ws_destroy(w);
+      return nullptr;
+    }
+  }
+  return w;
 }
 
 int ptof_gdn_fwd_exec(void* wsv, const void* q, const void* k, const void* v, const void* beta,

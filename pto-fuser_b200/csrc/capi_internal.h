@@ -52,6 +52,9 @@ cudaError_t launch_gdn_fwd_simt(const ptof_gdn_params& p, const void* q, const v
                                 const float* S0, void* o, float* S_final, cudaStream_t stream);
 bool gdn_fwd_simt_supports(const ptof_gdn_params& p);
 bool gdn_fwd_tc_supports(const ptof_gdn_params& p);
+// bytes of the per-chunk coefficient records the tensor-core forward keeps in the
+// workspace (allocated by ptof_gdn_fwd_setup)
+size_t gdn_fwd_tc_scratch_bytes(const ptof_gdn_params& p);
 int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v,
                       const void* beta, const float* g, const float* S0, void* o,
                       float* S_final, cudaStream_t stream);

@@ -38,6 +38,23 @@ constexpr int kThreads = 512;
 // (kkt/qk epilogue), scan = warps 12-15; 4 and 5 pair warps 4-5 and 6-7
 constexpr int kPBar = 1, kScanBar = 2, kQBar = 3;
 
+// ------------------------------------------------------ coefficient records ----
+// Per chunk (64 tokens), computed once by gdn_coef_kernel from g and beta, byte
+// offsets of fp32 arrays [64] and scalars; g is the chunk-local cumsum, gl = g[63].
+namespace coef {
+constexpr int GCUM = 0;      // g_i
+constexpr int EG = 256;      // e^{g_i}
+constexpr int BK = 512;      // beta_i e^{g_i}
+constexpr int BV = 768;      // beta_i
+constexpr int GAM = 1024;    // gamma_i = e^{gl - g_i}
+constexpr int ROWFB = 1280;  // beta_i e^{g_i - g_0}
+constexpr int COLF = 1536;   // e^{g_0 - g_j}
+constexpr int EGL = 1792;    // e^{gl}
+constexpr int FAST = 1796;   // int: the factorised (fast) path applies to this chunk
+constexpr int ENGL = 1800;   // e^{-gl} (fast chunks)
+constexpr int BYTES = 1808;  // multiple of 16 (bulk copies)
+}  // namespace coef
+
 // ------------------------------------------------------------------ layout ----
 template <int DK, int DV>
 struct Layout {
@@ -52,12 +69,12 @@ struct Layout {
   static constexpr int KQ_REGION = 2 * kC * 128;     // K rows 0-63 | Q rows 64-127, 16 KB
   static constexpr int OFF_KQ = 0;                   // within an input stage
   static constexpr int IN_STAGE = NKB * KQ_REGION;
-  // per-chunk arrays (one set per input stage, in their own region below): fp32
-  // per-token coefficients, then three scalars
-  static constexpr int M_GRAW = 0, M_BRAW = 256, M_GCUM = 512, M_EG = 768, M_BK = 1024,
-                       M_BV = 1280, M_GAM = 1536, M_ROWFB = 1792, M_COLF = 2048,
-                       M_EGL = 2304, M_FAST = 2308, M_ENGL = 2312;
-  static constexpr int MISC_BYTES = 2432;
+  // per-chunk coefficient records written by gdn_coef_kernel (one per input stage,
+  // in their own region below)
+  static constexpr int M_GCUM = coef::GCUM, M_EG = coef::EG, M_BK = coef::BK, M_BV = coef::BV,
+                       M_GAM = coef::GAM, M_ROWFB = coef::ROWFB, M_COLF = coef::COLF,
+                       M_EGL = coef::EGL, M_FAST = coef::FAST, M_ENGL = coef::ENGL;
+  static constexpr int MISC_BYTES = coef::BYTES;
   // V ring (2 stages)
   static constexpr int V_REGION = kC * 128;          // 8 KB per 64-wide block
   static constexpr int OFF_V = NIN * IN_STAGE;
@@ -99,7 +116,7 @@ struct Layout {
 // can run two chunks apart use one barrier per buffer, so a phase parity never
 // aliases a later chunk.
 enum Bar {
-  B_FULL0 = 0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_GREADY0, B_GREADY1, B_GREADY2,
+  B_FULL0 = 0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2,
   B_VFULL0, B_VFULL1, B_VEMPTY0, B_VEMPTY1, B_WREADY0, B_WREADY1, B_WTFREE0, B_WTFREE1,
   B_AREADY0, B_AREADY1, B_TAFREE0, B_TAFREE1,
   B_KQFULL, B_TREADY, B_WUFULL, B_RWFREE, B_VNFREE0, B_VNFREE1, B_SREADY, B_VNFULL,
@@ -109,8 +126,7 @@ static_assert(B_COUNT * 8 + 8 <= 512, "barrier area");
 
 struct Params {
   CUtensorMap mapK, mapQ, mapV;   // 3D maps, box = 64 d x 64 tokens
-  const float* g;                  // [B,H,T] / [B,T,H] fp32 (may be null: ungated)
-  const void* beta;
+  const unsigned char* coef;       // [B*H][nc] coefficient records (gdn_coef_kernel)
   const float* S0;                 // [B,H,DK,DV] or null
   void* o;
   float* S_final;                  // or null
@@ -118,8 +134,7 @@ struct Params {
   unsigned long long* trace;       // optional [chunks x kTraceSlots] timestamps of CTA 0
   int trace_chunks;
   int B, H, T, nc;
-  int gate_mode, beta_dtype, layout;
-  int64_t gs_b, gs_h, gs_t;        // g / beta strides (elements)
+  int layout;
   int64_t os_b, os_h, os_t;        // o strides (elements)
   float scale;
 };
@@ -283,6 +298,75 @@ __device__ __forceinline__ void inv16_diag(const unsigned char* a_tile, unsigned
   st_c(t_tile, r0, r0 + 8, lane, p1, 1.f);
 }
 
+// ------------------------------------------------------ coefficient pre-pass ----
+struct CoefParams {
+  const float* g;        // [B,H,T] / [B,T,H] fp32, raw or chunk-local cumsum (null: ungated)
+  const void* beta;
+  unsigned char* out;    // [B*H*nc][coef::BYTES]
+  int B, H, nc;
+  int gate_mode, beta_dtype, allow_fast;
+  int64_t gs_b, gs_h, gs_t;
+};
+
+// One warp per chunk, lane l owns tokens 2l and 2l+1: chunk-local cumsum of the
+// log decay (warp scan), the exponentials every later stage needs, and the fast-path
+// test: exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j) is overflow-free when the
+// cumsum is monotone and the chunk's total decay is below 80 (fp16 operands always
+// take the exact path). Mirrors gdn_reference's per-chunk gate handling
+// (examples/attention/_gdn_full.py:63-66, 108).
+__global__ void __launch_bounds__(256) gdn_coef_kernel(const __grid_constant__ CoefParams P) {
+  const int l = threadIdx.x & 31;
+  const int64_t chunk = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (chunk >= static_cast<int64_t>(P.B) * P.H * P.nc) return;
+  const int bh = static_cast<int>(chunk / P.nc), c = static_cast<int>(chunk % P.nc);
+  const int b = bh / P.H, h = bh % P.H;
+  const int64_t gb = b * P.gs_b + h * P.gs_h + static_cast<int64_t>(c) * kC * P.gs_t;
+  const int64_t i0 = gb + static_cast<int64_t>(2 * l) * P.gs_t, i1 = i0 + P.gs_t;
+  float g0 = 0.f, g1 = 0.f;
+  if (P.gate_mode != PTOF_GATE_NONE) {
+    g0 = P.g[i0];
+    g1 = P.g[i1];
+  }
+  bool mono = true;  // the chunk-local cumsum never increases
+  if (P.gate_mode == PTOF_GATE_RAW) {
+    mono = (g1 <= 0.f) && (g0 <= 0.f);
+    g1 += g0;
+    float run = g1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, run, o);
+      if (l >= o) run += y;
+    }
+    g0 += run - g1;
+    g1 = run;
+  } else if (P.gate_mode == PTOF_GATE_CUMSUM) {
+    const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
+    mono = (g1 <= g0) && (l == 0 || g0 <= prev);
+  }
+  const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
+  const float gl = __shfl_sync(0xffffffffu, g1, 31);
+  const bool fast = P.allow_fast && __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
+  const float b0 = ld_beta(P.beta, P.beta_dtype, i0), b1 = ld_beta(P.beta, P.beta_dtype, i1);
+  const float e0 = __expf(g0), e1 = __expf(g1);
+  const float rf0 = __expf(g0 - gfirst), rf1 = __expf(g1 - gfirst);
+  unsigned char* rec = P.out + chunk * coef::BYTES;
+  auto put = [&](int off, float x, float y) {
+    reinterpret_cast<float2*>(rec + off)[l] = make_float2(x, y);
+  };
+  put(coef::GCUM, g0, g1);
+  put(coef::EG, e0, e1);
+  put(coef::BK, b0 * e0, b1 * e1);
+  put(coef::BV, b0, b1);
+  put(coef::GAM, __expf(gl - g0), __expf(gl - g1));
+  put(coef::ROWFB, rf0 * b0, rf1 * b1);
+  put(coef::COLF, __expf(gfirst - g0), __expf(gfirst - g1));
+  if (l == 0) {
+    *reinterpret_cast<float*>(rec + coef::EGL) = __expf(gl);
+    *reinterpret_cast<int*>(rec + coef::FAST) = fast ? 1 : 0;
+    *reinterpret_cast<float*>(rec + coef::ENGL) = fast ? __expf(-gl) : 0.f;
+  }
+}
+
 // ------------------------------------------------------------------ kernel ----
 template <int DK, int DV, bool F16, typename TO, bool TRACE>
 __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_constant__ Params P) {
@@ -333,44 +417,25 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       prefetch_tmap(&P.mapQ);
       prefetch_tmap(&P.mapV);
     }
-    const int gelt = P.beta_dtype == PTOF_F32 ? 4 : 2;
-    const bool contiguous = (P.gs_t == 1);
     const bool bhtd = (P.layout == PTOF_LAYOUT_BHTD);
+    const unsigned char* crec = P.coef + static_cast<int64_t>(bh) * nc * L::MISC_BYTES;
     for (int c = 0; c < nc; ++c) {
       const int s = c % 3;
       if (c >= 3) sy.wait(&bars[B_EMPTY0 + s], in_par(c) ^ 1, 1);
       unsigned char* st = stage(c);
-      float* ms = misc(c);
       const int t0 = c * kC;
       const int y = bhtd ? t0 : h;
       const int z = bhtd ? bh : b * P.T + t0;
-      const int64_t gb = b * P.gs_b + h * P.gs_h + static_cast<int64_t>(t0) * P.gs_t;
-      if (!contiguous) {
-        // token-strided g / beta (token-major layout): plain loads, 2 tokens per lane
-        for (int i = lane; i < kC; i += 32) {
-          ms[L::M_GRAW / 4 + i] = P.g ? P.g[gb + i * P.gs_t] : 0.f;
-          reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(ms) + L::M_BRAW)[i] =
-              ld_beta(P.beta, P.beta_dtype, gb + i * P.gs_t);
-        }
-        __threadfence_block();
-      }
-      __syncwarp();
       if (lane == 0) {
-        uint32_t bytes = 2 * DK * kC * 2;
-        if (contiguous) bytes += (P.g ? kC * 4 : 0) + kC * gelt;
-        mbar_arrive_expect_tx(&bars[B_FULL0 + s], bytes);
+        mbar_arrive_expect_tx(&bars[B_FULL0 + s], 2 * DK * kC * 2 + L::MISC_BYTES);
 #pragma unroll
         for (int kb = 0; kb < L::NKB; ++kb) {
           tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION, &P.mapK, &bars[B_FULL0 + s], kb * 64, y, z);
           tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION + kC * 128, &P.mapQ, &bars[B_FULL0 + s],
                       kb * 64, y, z);
         }
-        if (contiguous) {
-          if (P.g) bulk_load(reinterpret_cast<unsigned char*>(ms) + L::M_GRAW, P.g + gb, kC * 4, &bars[B_FULL0 + s]);
-          bulk_load(reinterpret_cast<unsigned char*>(ms) + L::M_BRAW,
-                    static_cast<const unsigned char*>(P.beta) + gb * gelt, kC * gelt,
-                    &bars[B_FULL0 + s]);
-        }
+        bulk_load(misc(c), crec + static_cast<int64_t>(c) * L::MISC_BYTES, L::MISC_BYTES,
+                  &bars[B_FULL0 + s]);
         trace_mark<TRACE>(P, c, TR_TMA_ISSUE);
       }
       // V tile of chunk c (consumed by the U^T UMMA only)
@@ -534,64 +599,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       const float* gcum = ms + L::M_GCUM / 4;
       sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 20);
       if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_FULL);
-      // ---- per-token coefficients (warp 8: tokens 2l, 2l+1) ----
-      if (warp == 8) {
-        float g0 = 0.f, g1 = 0.f;
-        if (P.gate_mode != PTOF_GATE_NONE) {
-          g0 = ms[L::M_GRAW / 4 + 2 * l];
-          g1 = ms[L::M_GRAW / 4 + 2 * l + 1];
-        }
-        bool mono = true;  // the chunk-local cumsum never increases
-        if (P.gate_mode == PTOF_GATE_RAW) {
-          mono = (g1 <= 0.f) && (l == 0 || g0 <= 0.f);
-          g1 += g0;
-          float run = g1;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, run, o);
-            if (l >= o) run += y;
-          }
-          g0 += run - g1;
-          g1 = run;
-        } else if (P.gate_mode == PTOF_GATE_CUMSUM) {
-          const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
-          mono = (g1 <= g0) && (l == 0 || g0 <= prev);
-        }
-        if (qp == 0) trace_mark<TRACE>(P, c, TR_X0);
-        const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
-        const float gl = __shfl_sync(0xffffffffu, g1, 31);
-        // exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j): overflow-free when the chunk's
-        // total decay is below 80 and the cumsum is monotone; otherwise the exact form
-        const bool fast = !F16 && __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
-        float b0, b1;
-        if (P.gs_t == 1 && P.beta_dtype != PTOF_F32) {
-          const uint32_t u = reinterpret_cast<const uint32_t*>(reinterpret_cast<const unsigned char*>(ms) + L::M_BRAW)[l];
-          const float2 f = (P.beta_dtype == PTOF_F16) ? unpack_f16(u) : unpack_bf16(u);
-          b0 = f.x; b1 = f.y;
-        } else {
-          const float* bf = reinterpret_cast<const float*>(reinterpret_cast<const unsigned char*>(ms) + L::M_BRAW);
-          b0 = bf[2 * l]; b1 = bf[2 * l + 1];
-        }
-        if (qp == 0) trace_mark<TRACE>(P, c, TR_X1);
-        const float e0 = __expf(g0), e1 = __expf(g1);
-        const float rf0 = __expf(g0 - gfirst), rf1 = __expf(g1 - gfirst);
-        float2* m2 = reinterpret_cast<float2*>(ms);
-        m2[L::M_GCUM / 8 + l] = make_float2(g0, g1);
-        m2[L::M_EG / 8 + l] = make_float2(e0, e1);
-        m2[L::M_BK / 8 + l] = make_float2(b0 * e0, b1 * e1);
-        m2[L::M_BV / 8 + l] = make_float2(b0, b1);
-        m2[L::M_GAM / 8 + l] = make_float2(__expf(gl - g0), __expf(gl - g1));
-        m2[L::M_ROWFB / 8 + l] = make_float2(rf0 * b0, rf1 * b1);
-        m2[L::M_COLF / 8 + l] = make_float2(__expf(gfirst - g0), __expf(gfirst - g1));
-        if (l == 0) {
-          ms[L::M_EGL / 4] = __expf(gl);
-          ms[L::M_ENGL / 4] = fast ? __expf(-gl) : 0.f;
-          reinterpret_cast<int*>(ms)[L::M_FAST / 4] = fast ? 1 : 0;
-        }
-      }
-      if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_COEF);
-      named_bar_sync(kQBar, 128);
-      if (qp == 0) mbar_arrive(&bars[B_GREADY0 + (c % 3)]);
       const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
       // A buffer c & 1 last held A(c - 2) / T(c - 2); Aqk buffer c % 3 last fed O(c - 3)
       if (c >= 2) sy.wait(&bars[B_TAFREE0 + (c & 1)], ((c >> 1) + 1) & 1, 23);
@@ -894,7 +901,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     };
 
     // initial state: S^T <- S0 (or 0), master pre-scaled by e^{g_last} of chunk 0
-    sy.wait(&bars[B_GREADY0], 0, 30);  // chunk 0
+    sy.wait(&bars[B_FULL0], 0, 30);  // chunk 0
     state_pass(true, misc(0)[L::M_EGL / 4], nullptr);
     tc_fence_before();
     if (!L::SA_TMEM) fence_async_smem();
@@ -975,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       tc_fence_after();
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_SFULL);
       if (c + 1 < nc) {
-        sy.wait(&bars[B_GREADY0 + ((c + 1) % 3)], in_par(c + 1), 33);
+        sy.wait(&bars[B_FULL0 + ((c + 1) % 3)], in_par(c + 1), 33);
         state_pass(false, misc(c + 1)[L::M_EGL / 4], nullptr);
         tc_fence_before();
         if (!L::SA_TMEM) fence_async_smem();
@@ -1074,8 +1081,24 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   if (!rc) rc = make_act_map(&P.mapQ, q, p.in_dtype, p, DK);
   if (!rc) rc = make_act_map(&P.mapV, v, p.in_dtype, p, DV);
   if (rc) return rc;
-  P.g = (p.gate_mode == PTOF_GATE_NONE) ? nullptr : g;
-  P.beta = beta;
+  // per-chunk coefficient records, then the fused forward (same stream)
+  if (!w->d_scratch || w->scratch_bytes < gdn_fwd_tc_scratch_bytes(p))
+    return fail(PTOF_EINVAL, "gdn_fwd workspace has no coefficient buffer");
+  {
+    tcfwd::CoefParams C;
+    C.g = (p.gate_mode == PTOF_GATE_NONE) ? nullptr : g;
+    C.beta = beta;
+    C.out = static_cast<unsigned char*>(w->d_scratch);
+    C.B = p.B; C.H = p.H; C.nc = p.T / kChunk;
+    C.gate_mode = p.gate_mode;
+    C.beta_dtype = p.beta_dtype;
+    C.allow_fast = F16 ? 0 : 1;
+    const Strides3 sg = make_strides3(p.layout, p.H, p.T);
+    C.gs_b = sg.b; C.gs_h = sg.h; C.gs_t = sg.t;
+    const int64_t chunks = static_cast<int64_t>(p.B) * p.H * C.nc;
+    tcfwd::gdn_coef_kernel<<<static_cast<unsigned>((chunks + 7) / 8), 256, 0, stream>>>(C);
+  }
+  P.coef = static_cast<const unsigned char*>(w->d_scratch);
   P.S0 = S0;
   P.o = o;
   P.S_final = S_final;
@@ -1083,12 +1106,8 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.trace = static_cast<unsigned long long*>(w->trace);
   P.trace_chunks = w->trace_chunks;
   P.B = p.B; P.H = p.H; P.T = p.T; P.nc = p.T / kChunk;
-  P.gate_mode = p.gate_mode;
-  P.beta_dtype = p.beta_dtype;
   P.layout = p.layout;
-  const Strides3 sg = make_strides3(p.layout, p.H, p.T);
   const Strides4 so = make_strides4(p.layout, p.H, p.T, DV);
-  P.gs_b = sg.b; P.gs_h = sg.h; P.gs_t = sg.t;
   P.os_b = so.b; P.os_h = so.h; P.os_t = so.t;
   P.scale = p.scale;
   auto kern = P.trace ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, true>
@@ -1118,6 +1137,10 @@ int launch_d(Workspace* w, const void* q, const void* k, const void* v, const vo
 }
 
 }  // namespace
+
+size_t gdn_fwd_tc_scratch_bytes(const ptof_gdn_params& p) {
+  return static_cast<size_t>(p.B) * p.H * (p.T / kChunk) * tcfwd::coef::BYTES;
+}
 
 bool gdn_fwd_tc_supports(const ptof_gdn_params& p) {
   if (p.in_dtype != PTOF_F16 && p.in_dtype != PTOF_BF16) return false;
