@@ -593,7 +593,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     const int qp = tid - 256, q = warp & 3, l = lane;
     const int r = 32 * q + l;
     const uint32_t t_kq = tmem + L::T_KQ + ((32u * q) << 16);
-    for (int c = 0; c < nc; ++c) {
+    const uint32_t t_rw = tmem + L::T_RW + ((32u * q) << 16);
+    // E(c), then R(c - 1): the W^T readout follows its WY UMMAs as closely as the
+    // epilogue allows, so the chain of chunk c - 1 starts early
+    for (int c = 0; c <= nc; ++c) {
+      if (c < nc) {
       unsigned char* st = stage(c);
       float* ms = misc(c);
       const float* gcum = ms + L::M_GCUM / 4;
@@ -674,16 +678,46 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         mbar_arrive(&bars[B_AREADY0 + (c & 1)]);
         trace_mark<TRACE>(P, c, TR_PREP_EPI);
       }
+      }
+      if (c >= 1) {
+        // ================= R(c - 1): W^T readout =================
+        const int cp = c - 1;
+        sy.wait(&bars[B_WUFULL], cp & 1, 27);
+        // W^T buffer cp & 1 was last read by the chain UMMA of chunk cp - 2
+        if (cp >= 2) sy.wait(&bars[B_WTFREE0 + (cp & 1)], ((cp >> 1) + 1) & 1, 28);
+        tc_fence_after();
+        if (qp == 0) trace_mark<TRACE>(P, cp, TR_PREP_WU);
+        unsigned char* wt = sm + L::OFF_WT + (cp & 1) * L::WT_BYTES;
+        const int d = (DK == 128) ? 32 * q + l : (l < 16 ? 16 * q + l : -1);
+#pragma unroll 1
+        for (int j0 = 0; j0 < kC; j0 += 16) {
+          float a0[16];
+          tmem_ld16(t_rw + j0, a0);
+          tmem_wait_ld();
+          if (d >= 0) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
+            st_chunk(wt, d, j0 / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+            st_chunk(wt, d, j0 / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
+          }
+        }
+        tc_fence_before();
+        fence_async_smem();
+        named_bar_sync(kQBar, 128);
+        if (qp == 0) {
+          mbar_arrive(&bars[B_WREADY0 + (cp & 1)]);
+          mbar_arrive(&bars[B_RWFREE]);
+          trace_mark<TRACE>(P, cp, TR_PREP_END);
+        }
+      }
     }
   } else if (warp >= 4 && warp < 8) {
     const int pp = tid - 128, q = warp & 3, l = lane;
     unsigned char* s_tp = sm + L::OFF_TP;
     unsigned char* s_tpp = sm + L::OFF_TPP;
-    const uint32_t t_rw = tmem + L::T_RW + ((32u * q) << 16);
-    for (int c = 0; c <= nc; ++c) {
-      // order: inverse(c), R(c - 1), T'(c): the readout of chunk c - 1 waits only for
-      // its WY UMMAs, issued at the end of the previous iteration
-      float* ms = misc(c < nc ? c : 0);
+    for (int c = 0; c < nc; ++c) {
+      float* ms = misc(c);
       // A(c) in, T(c) out, in place (the strictly upper blocks of A are zero)
       unsigned char* s_td = sm + L::OFF_TA + (c & 1) * 8192;
       if (c < nc) {
@@ -749,38 +783,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         }
         named_bar_sync(kPBar, 128);
         if (pp == 0) trace_mark<TRACE>(P, c, TR_PREP_INV);
-      }
-      if (c >= 1) {
-        // ================= R(c - 1): W^T readout =================
-        const int cp = c - 1;
-        sy.wait(&bars[B_WUFULL], cp & 1, 27);
-        // W^T buffer cp & 1 was last read by the chain UMMA of chunk cp - 2
-        if (cp >= 2) sy.wait(&bars[B_WTFREE0 + (cp & 1)], ((cp >> 1) + 1) & 1, 28);
-        tc_fence_after();
-        if (pp == 0) trace_mark<TRACE>(P, cp, TR_PREP_WU);
-        unsigned char* wt = sm + L::OFF_WT + (cp & 1) * L::WT_BYTES;
-        const int d = (DK == 128) ? 32 * q + l : (l < 16 ? 16 * q + l : -1);
-#pragma unroll 1
-        for (int j0 = 0; j0 < kC; j0 += 16) {
-          float a0[16];
-          tmem_ld16(t_rw + j0, a0);
-          tmem_wait_ld();
-          if (d >= 0) {
-            uint32_t pk[8];
-#pragma unroll
-            for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
-            st_chunk(wt, d, j0 / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
-            st_chunk(wt, d, j0 / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
-          }
-        }
-        tc_fence_before();
-        fence_async_smem();
-        named_bar_sync(kPBar, 128);
-        if (pp == 0) {
-          mbar_arrive(&bars[B_WREADY0 + (cp & 1)]);
-          mbar_arrive(&bars[B_RWFREE]);
-          trace_mark<TRACE>(P, cp, TR_PREP_END);
-        }
       }
       if (c < nc) {
         const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
