@@ -64,8 +64,8 @@ struct Layout {
   // the DV = 64 variant keeps them in shared memory
   static constexpr bool SA_TMEM = (DV == 128);
   static constexpr bool VN_TMEM = SA_TMEM;
-  // input ring (3 stages): [K | Q] per 64-wide d block, then the per-token arrays
-  static constexpr int NIN = 3;
+  // input ring (4 stages): [K | Q] per 64-wide d block, then the per-token arrays
+  static constexpr int NIN = 4;
   static constexpr int KQ_REGION = 2 * kC * 128;     // K rows 0-63 | Q rows 64-127, 16 KB
   static constexpr int OFF_KQ = 0;                   // within an input stage
   static constexpr int IN_STAGE = NKB * KQ_REGION;
@@ -79,13 +79,13 @@ struct Layout {
   static constexpr int V_REGION = kC * 128;          // 8 KB per 64-wide block
   static constexpr int OFF_V = NIN * IN_STAGE;
   static constexpr int V_STAGE = NVB * V_REGION;
-  // Aqk (3 buffers), W^T (2 buffers)
-  static constexpr int OFF_AQK = OFF_V + 2 * V_STAGE;
+  // Aqk (3 buffers), W^T (1 buffer)
+  static constexpr int OFF_AQK = OFF_V + V_STAGE;
   static constexpr int WT_BYTES = DK * 128;
   static constexpr int OFF_WT = OFF_AQK + 3 * kC * 128;
   // prep buffers: T' and T'' (bf16 WY operands), A (fp16, 2 buffers; the inverse
   // overwrites A with T in place)
-  static constexpr int OFF_TP = OFF_WT + 2 * WT_BYTES;
+  static constexpr int OFF_TP = OFF_WT + WT_BYTES;
   static constexpr int OFF_TPP = OFF_TP + 8192;
   static constexpr int OFF_TA = OFF_TPP + 8192;
   // shared-memory chain operands of the DV = 64 variant: Vn^T, Vn^T gamma, S^T
@@ -94,7 +94,7 @@ struct Layout {
   static constexpr int OFF_VNG = OFF_VNT + VNT_BYTES;
   static constexpr int OFF_SA = OFF_VNG + VNT_BYTES;
   static constexpr int SA_BYTES = SA_TMEM ? 0 : NKB * DV * 128;
-  static constexpr int OFF_MISC = OFF_SA + SA_BYTES;  // 3 x MISC_BYTES
+  static constexpr int OFF_MISC = OFF_SA + SA_BYTES;  // NIN x MISC_BYTES
   static constexpr int OFF_OSC = OFF_MISC + NIN * MISC_BYTES;  // fp32 [64] output multipliers
   static constexpr int OFF_BAR = OFF_OSC + 256;
   static constexpr int BYTES = OFF_BAR + 512 + 1024;  // + alignment slack
@@ -116,8 +116,8 @@ struct Layout {
 // can run two chunks apart use one barrier per buffer, so a phase parity never
 // aliases a later chunk.
 enum Bar {
-  B_FULL0 = 0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2,
-  B_VFULL0, B_VFULL1, B_VEMPTY0, B_VEMPTY1, B_WREADY0, B_WREADY1, B_WTFREE0, B_WTFREE1,
+  B_FULL0 = 0, B_FULL1, B_FULL2, B_FULL3, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_EMPTY3,
+  B_VFULL, B_WREADY, B_WTFREE,
   B_AREADY0, B_AREADY1, B_TAFREE0, B_TAFREE1,
   B_KQFULL, B_TREADY, B_WUFULL, B_RWFREE, B_VNFREE0, B_VNFREE1, B_SREADY, B_VNFULL,
   B_VNREADY, B_SFULL, B_OFULL0, B_OFULL1, B_OFULL2, B_OFREE, B_DONE, B_KQFREE, B_O1DONE, B_COUNT
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   if (tid == 0) {
     abort_flag = 0;
     for (int i = 0; i < B_COUNT; ++i) mbar_init(&bars[i], 1);
-    for (int i = 0; i < 3; ++i) mbar_init(&bars[B_EMPTY0 + i], 3);  // 2 issuers + scan
+    for (int i = 0; i < L::NIN; ++i) mbar_init(&bars[B_EMPTY0 + i], 3);  // 2 issuers + scan
     mbar_init(&bars[B_DONE], 3);  // the three UMMA issuers
     if (L::VN_TMEM) {             // the chain and output UMMAs read V_new^T from TMEM
       mbar_init(&bars[B_VNFREE0], 2);
@@ -403,12 +403,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
   const uint64_t t_start = (TRACE && tid == 0) ? globaltimer_ns() : 0;
 
-  // chunk c lives in input stage c % 3 (use index c / 3), V stage c & 1, Aqk buffer c & 1
-  auto stage = [&](int c) { return sm + (c % 3) * L::IN_STAGE; };
-  auto misc = [&](int c) { return reinterpret_cast<float*>(sm + L::OFF_MISC + (c % 3) * L::MISC_BYTES); };
-  auto vstage = [&](int c) { return sm + L::OFF_V + (c & 1) * L::V_STAGE; };
+  // chunk c lives in input stage c % NIN (use index c / NIN) and Aqk buffer c % 3
+  auto stage = [&](int c) { return sm + (c % L::NIN) * L::IN_STAGE; };
+  auto misc = [&](int c) { return reinterpret_cast<float*>(sm + L::OFF_MISC + (c % L::NIN) * L::MISC_BYTES); };
   auto aqk = [&](int c) { return sm + L::OFF_AQK + (c % 3) * (kC * 128); };
-  auto in_par = [&](int c) { return static_cast<uint32_t>((c / 3) & 1); };
+  auto in_par = [&](int c) { return static_cast<uint32_t>((c / L::NIN) & 1); };
+  auto aq_par = [&](int c) { return static_cast<uint32_t>((c / 3) & 1); };
 
   // ================================================================ TMA ====
   if (warp == 0) {
@@ -420,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     const bool bhtd = (P.layout == PTOF_LAYOUT_BHTD);
     const unsigned char* crec = P.coef + static_cast<int64_t>(bh) * nc * L::MISC_BYTES;
     for (int c = 0; c < nc; ++c) {
-      const int s = c % 3;
-      if (c >= 3) sy.wait(&bars[B_EMPTY0 + s], in_par(c) ^ 1, 1);
+      const int s = c % L::NIN;
+      if (c >= L::NIN) sy.wait(&bars[B_EMPTY0 + s], in_par(c) ^ 1, 1);
       unsigned char* st = stage(c);
       const int t0 = c * kC;
       const int y = bhtd ? t0 : h;
@@ -437,14 +437,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         bulk_load(misc(c), crec + static_cast<int64_t>(c) * L::MISC_BYTES, L::MISC_BYTES,
                   &bars[B_FULL0 + s]);
         trace_mark<TRACE>(P, c, TR_TMA_ISSUE);
-      }
-      // V tile of chunk c (consumed by the U^T UMMA only)
-      if (c >= 2) sy.wait(&bars[B_VEMPTY0 + (c & 1)], ((c >> 1) + 1) & 1, 2);
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&bars[B_VFULL0 + (c & 1)], DV * kC * 2);
-#pragma unroll
-        for (int vb = 0; vb < L::NVB; ++vb)
-          tma_load_3d(vstage(c) + vb * L::V_REGION, &P.mapV, &bars[B_VFULL0 + (c & 1)], vb * 64, y, z);
       }
       __syncwarp();
     }
@@ -477,10 +469,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     if (warp == 1) {
       for (int c = 0; c < nc; ++c) {
         sy.wait(&bars[B_SREADY], c & 1, 14);
-        sy.wait(&bars[B_WREADY0 + (c & 1)], (c >> 1) & 1, 15);
+        sy.wait(&bars[B_WREADY], c & 1, 15);
         tc_fence_after();
         trace_mark<TRACE>(P, c, TR_MMA_C1);
-        const uint32_t wt = s_wt + (c & 1) * L::WT_BYTES;
+        const uint32_t wt = s_wt;
 #pragma unroll 1
         for (int ks = 0; ks < DK / 16; ++ks) {
           const uint64_t bd = sdesc_sw128(wt + ks * 2048, DK * 128, 1024);
@@ -488,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           else umma_ss(t_vn(c), a_desc_sa(ks), bd, ID_VN, 1);
         }
         umma_commit(&bars[B_VNFULL]);
-        umma_commit(&bars[B_WTFREE0 + (c & 1)]);
+        umma_commit(&bars[B_WTFREE]);
         sy.wait(&bars[B_VNREADY], c & 1, 17);
         tc_fence_after();
         trace_mark<TRACE>(P, c, TR_MMA_C2);
@@ -509,14 +501,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
                     sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
         }
         umma_commit(&bars[B_SFULL]);
-        umma_commit(&bars[B_EMPTY0 + (c % 3)]);
+        umma_commit(&bars[B_EMPTY0 + (c % L::NIN)]);
         if (L::VN_TMEM) umma_commit(&bars[B_VNFREE0 + (c & 1)]);
       }
     } else if (warp == 3) {
       for (int c = 0; c < nc; ++c) {
         sy.wait(&bars[B_SREADY], c & 1, 40);
         // Q' of slow chunks is written before A(c) is handed over, long before W^T(c)
-        sy.wait(&bars[B_WREADY0 + (c & 1)], (c >> 1) & 1, 42);
+        sy.wait(&bars[B_WREADY], c & 1, 42);
         if (c >= 1) sy.wait(&bars[B_OFREE], (c - 1) & 1, 16);
         tc_fence_after();
         const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
@@ -538,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           else umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024), bd, ID_O2, 1);
         }
         umma_commit(&bars[B_OFULL0 + (c % 3)]);
-        umma_commit(&bars[B_EMPTY0 + (c % 3)]);
+        umma_commit(&bars[B_EMPTY0 + (c % L::NIN)]);
         if (L::VN_TMEM) umma_commit(&bars[B_VNFREE0 + (c & 1)]);
       }
     } else {
@@ -546,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       // P0(c) needs only E(c - 1) to have drained KQ, P1(c - 1) needs T'(c - 1)
       for (int c = 0; c <= nc; ++c) {
         if (c < nc) {
-          sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 10);
+          sy.wait(&bars[B_FULL0 + (c % L::NIN)], in_par(c), 10);
           if (c >= 1) sy.wait(&bars[B_KQFREE], (c - 1) & 1, 11);
           tc_fence_after();
           const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
@@ -560,12 +552,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         if (c >= 1) {
           const int cp = c - 1;
           sy.wait(&bars[B_TREADY], cp & 1, 13);
-          sy.wait(&bars[B_VFULL0 + (cp & 1)], (cp >> 1) & 1, 18);
+          sy.wait(&bars[B_VFULL], cp & 1, 18);
           if (cp >= 2) sy.wait(&bars[B_VNFREE0 + (cp & 1)], ((cp >> 1) + 1) & 1, 19);
           if (cp >= 1) sy.wait(&bars[B_RWFREE], (cp - 1) & 1, 9);
           tc_fence_after();
           const uint32_t kq = smem_u32(stage(cp) + L::OFF_KQ);
-          const uint32_t vt = smem_u32(vstage(cp));
+          const uint32_t vt = smem_u32(sm + L::OFF_V);
           const uint32_t t_u = t_vn(cp);
 #pragma unroll 1
           for (int ks = 0; ks < kC / 16; ++ks) {
@@ -575,7 +567,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
                     sdesc_sw128(s_tpp + ks * 32, 16, 1024), ID_UT, ks > 0);
           }
           umma_commit(&bars[B_WUFULL]);
-          umma_commit(&bars[B_VEMPTY0 + (cp & 1)]);
         }
       }
     }
@@ -594,6 +585,21 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     const int r = 32 * q + l;
     const uint32_t t_kq = tmem + L::T_KQ + ((32u * q) << 16);
     const uint32_t t_rw = tmem + L::T_RW + ((32u * q) << 16);
+    // V tile of chunk cv (read by the U^T UMMA only; single buffer, loaded once the
+    // previous chunk's WY UMMAs have completed)
+    auto issue_v = [&](int cv) {
+      const int t0 = cv * kC;
+      const bool bhtd = (P.layout == PTOF_LAYOUT_BHTD);
+      const int y = bhtd ? t0 : h, z = bhtd ? bh : b * P.T + t0;
+      mbar_arrive_expect_tx(&bars[B_VFULL], DV * kC * 2);
+#pragma unroll
+      for (int vb = 0; vb < L::NVB; ++vb)
+        tma_load_3d(sm + L::OFF_V + vb * L::V_REGION, &P.mapV, &bars[B_VFULL], vb * 64, y, z);
+    };
+    if (qp == 0) {
+      prefetch_tmap(&P.mapV);
+      issue_v(0);
+    }
     // E(c), then R(c - 1): the W^T readout follows its WY UMMAs as closely as the
     // epilogue allows, so the chain of chunk c - 1 starts early
     for (int c = 0; c <= nc; ++c) {
@@ -601,12 +607,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       unsigned char* st = stage(c);
       float* ms = misc(c);
       const float* gcum = ms + L::M_GCUM / 4;
-      sy.wait(&bars[B_FULL0 + (c % 3)], in_par(c), 20);
+      sy.wait(&bars[B_FULL0 + (c % L::NIN)], in_par(c), 20);
       if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_FULL);
       const bool fast = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
       // A buffer c & 1 last held A(c - 2) / T(c - 2); Aqk buffer c % 3 last fed O(c - 3)
       if (c >= 2) sy.wait(&bars[B_TAFREE0 + (c & 1)], ((c >> 1) + 1) & 1, 23);
-      if (c >= 3) sy.wait(&bars[B_OFULL0 + (c % 3)], in_par(c) ^ 1, 24);
+      if (c >= 3) sy.wait(&bars[B_OFULL0 + (c % 3)], aq_par(c) ^ 1, 24);
       if (qp == 0) trace_mark<TRACE>(P, c, TR_PREP_OFULL);
       sy.wait(&bars[B_KQFULL], c & 1, 21);
       tc_fence_after();
@@ -684,10 +690,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         const int cp = c - 1;
         sy.wait(&bars[B_WUFULL], cp & 1, 27);
         // W^T buffer cp & 1 was last read by the chain UMMA of chunk cp - 2
-        if (cp >= 2) sy.wait(&bars[B_WTFREE0 + (cp & 1)], ((cp >> 1) + 1) & 1, 28);
+        if (cp + 1 < nc && qp == 0) issue_v(cp + 1);   // P1(cp) has read V(cp)
+        // the W^T tile was last read by the chain UMMA of chunk cp - 1
+        if (cp >= 1) sy.wait(&bars[B_WTFREE], (cp - 1) & 1, 28);
         tc_fence_after();
         if (qp == 0) trace_mark<TRACE>(P, cp, TR_PREP_WU);
-        unsigned char* wt = sm + L::OFF_WT + (cp & 1) * L::WT_BYTES;
+        unsigned char* wt = sm + L::OFF_WT;
         const int d = (DK == 128) ? 32 * q + l : (l < 16 ? 16 * q + l : -1);
 #pragma unroll 1
         for (int j0 = 0; j0 < kC; j0 += 16) {
@@ -706,7 +714,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         fence_async_smem();
         named_bar_sync(kQBar, 128);
         if (qp == 0) {
-          mbar_arrive(&bars[B_WREADY0 + (cp & 1)]);
+          mbar_arrive(&bars[B_WREADY]);
           mbar_arrive(&bars[B_RWFREE]);
           trace_mark<TRACE>(P, cp, TR_PREP_END);
         }
@@ -976,7 +984,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         mbar_arrive(&bars[B_VNREADY]);
         trace_mark<TRACE>(P, c, TR_SCAN_VNREADY);
         if (!L::VN_TMEM) mbar_arrive(&bars[B_VNFREE0 + (c & 1)]);
-        mbar_arrive(&bars[B_EMPTY0 + (c % 3)]);
+        mbar_arrive(&bars[B_EMPTY0 + (c % L::NIN)]);
       }
       // ---- (b) state: S^T_{c+1} ready -> bf16 copy, pre-scale by e^{gl_{c+1}} ----
       sy.wait(&bars[B_SFULL], c & 1, 32);
@@ -984,7 +992,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       tc_fence_after();
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_SFULL);
       if (c + 1 < nc) {
-        sy.wait(&bars[B_FULL0 + ((c + 1) % 3)], in_par(c + 1), 33);
+        sy.wait(&bars[B_FULL0 + ((c + 1) % L::NIN)], in_par(c + 1), 33);
         state_pass(false, misc(c + 1)[L::M_EGL / 4], nullptr);
         tc_fence_before();
         if (!L::SA_TMEM) fence_async_smem();
@@ -997,7 +1005,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         state_pass(false, 1.f, P.S_final);
       }
       // ---- (c) output: O^T row v -> o[t0 + i, v] ----
-      sy.wait(&bars[B_OFULL0 + (c % 3)], in_par(c), 34);
+      sy.wait(&bars[B_OFULL0 + (c % 3)], aq_par(c), 34);
       tc_fence_after();
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_OFULL);
       {
