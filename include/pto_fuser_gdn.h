@@ -92,6 +92,27 @@ PTOF_API int ptof_gdn_fwd_exec(void* ws, const void* q, const void* k, const voi
                       const float* g, const float* S0, void* o, float* S_final, void* stream);
 PTOF_API void ptof_gdn_fwd_teardown(void* ws);
 
+/* The same f16/bf16 tensor-core forward without a workspace and without any device
+ * allocation. It has no counterpart in the reference. It is for callers that cannot
+ * call cudaMalloc, e.g. code inside a device-memory allocator or arena that owns all
+ * device memory, or code replaying a fixed memory plan. Its per-chunk scratch (the gate
+ * coefficient records) lives in a fixed array in the library's device memory, reserved
+ * on every GPU that loads the library until the process exits:
+ *   - B*H*T/64 must not exceed 4096 chunks (7.4 MB of records); larger problems
+ *     are rejected with PTOF_EINVAL, and unsupported shapes or dtypes
+ *     (fp32, Dk = Dv other than 64 or 128) with PTOF_EUNSUPPORTED;
+ *   - the first call on a device looks up the array's device address with that
+ *     device current (cudaGetSymbolAddress); make it before any stream capture;
+ *   - every call shares the one array, so calls whose kernels overlap on the GPU
+ *     (other streams, other host threads) race and corrupt each other's results;
+ *   - there is no status word: a device-side wait that gives up ends the kernel
+ *     early without a report (ptof_check_status does not apply).
+ * Inputs and outputs are as for ptof_gdn_fwd_exec; the call launches on `stream`
+ * and does not synchronise. */
+PTOF_API int ptof_gdn_fwd_exec_noalloc(const ptof_gdn_params* p, const void* q, const void* k,
+                                       const void* v, const void* beta, const float* g,
+                                       const float* S0, void* o, float* S_final, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Kernels behind the reference's finer-grained fused-node keys. They share one
  * library-owned workspace (status word) from ptof_ws_setup / ptof_ws_teardown,

@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <mutex>
 
 #include "capi_internal.h"
 #include "common.cuh"
@@ -1166,4 +1167,72 @@ int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v,
   return launch_d<64, 64>(w, q, k, v, beta, g, S0, o, S_final, stream);
 }
 
+// ----------------------------------------------- allocation-free entry point ----
+// For callers that cannot allocate device memory: code running where cudaMalloc is
+// off limits (inside a host allocator or an arena that owns all device memory, or
+// between the set-up and replay of a fixed memory plan) cannot create a workspace.
+// ptof_gdn_fwd_exec_noalloc runs the same tensor-core forward with its coefficient
+// records in this file-scope array instead of a workspace buffer. Its size is fixed:
+// every GPU that loads the library reserves it until the process exits.
+namespace {
+constexpr int64_t kNoAllocMaxChunks = 4096;   // B * H * T / 64, i.e. 262,144 head-tokens
+static __device__ __align__(256) unsigned char
+    g_noalloc_coef[kNoAllocMaxChunks * tcfwd::coef::BYTES];   // 7.4 MB
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
 }  // namespace ptof
+
+extern "C" int ptof_gdn_fwd_exec_noalloc(const ptof_gdn_params* p, const void* q, const void* k,
+                                         const void* v, const void* beta, const float* g,
+                                         const float* S0, void* o, float* S_final, void* stream) {
+  using namespace ptof;
+  if (!p) return fail(PTOF_EINVAL, "null params");
+  int rc = validate_gdn(*p);
+  if (rc) return rc;
+  if (p->in_dtype == PTOF_F32 || !gdn_fwd_tc_supports(*p))
+    return fail(PTOF_EUNSUPPORTED,
+                "ptof_gdn_fwd_exec_noalloc covers the f16/bf16 tensor-core forward only "
+                "(C = 64, Dk = Dv = 64 or 128)");
+  const int64_t chunks = static_cast<int64_t>(p->B) * p->H * (p->T / kChunk);
+  if (chunks > kNoAllocMaxChunks)
+    return fail(PTOF_EINVAL,
+                "ptof_gdn_fwd_exec_noalloc: B*H*T/64 = %lld chunks exceeds its fixed maximum of "
+                "%lld (use ptof_gdn_fwd_setup / ptof_gdn_fwd_exec)",
+                static_cast<long long>(chunks), static_cast<long long>(kNoAllocMaxChunks));
+  rc = check_ptrs({q, k, v, beta, o}, {S0, S_final});
+  if (rc) return rc;
+  if (p->gate_mode != PTOF_GATE_NONE && !g) return fail(PTOF_EINVAL, "g is NULL for a gated forward");
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PTOF_EUNSUPPORTED, "device index %d", dev);
+  void* base = nullptr;
+  {
+    // the array's device address, looked up once per device with that device
+    // current (in host code the symbol itself is only a host-side stand-in)
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_coef);
+      if (e != cudaSuccess) {
+        g_noalloc_ptr[dev] = nullptr;
+        return cuda_fail(e, "cudaGetSymbolAddress(coefficient array)");
+      }
+    }
+    base = g_noalloc_ptr[dev];
+  }
+  // A workspace on the stack pointing at the array: no status word (a device-side
+  // wait that gives up ends the kernel early without a report), no trace. The
+  // coefficient pre-pass rewrites every record the forward reads, so nothing in the
+  // array has to start at zero.
+  Workspace w;
+  w.kind = kWsGdnFwd;
+  w.device = dev;
+  w.p = *p;
+  w.d_status = nullptr;
+  w.d_scratch = base;
+  w.scratch_bytes = static_cast<size_t>(kNoAllocMaxChunks) * tcfwd::coef::BYTES;
+  return launch_gdn_fwd_tc(&w, q, k, v, beta, g, S0, o, S_final, static_cast<cudaStream_t>(stream));
+}

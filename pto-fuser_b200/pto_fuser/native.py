@@ -48,6 +48,7 @@ _SIGNATURES = {
     "ptof_gdn_fwd_setup": (_vp, [ctypes.POINTER(GdnParams)]),
     "ptof_gdn_fwd_exec": (_i32, [_vp] * 10),
     "ptof_gdn_fwd_teardown": (None, [_vp]),
+    "ptof_gdn_fwd_exec_noalloc": (_i32, [ctypes.POINTER(GdnParams)] + [_vp] * 9),
     "ptof_check_status": (_i32, [_vp, _vp]),
     "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),
     "ptof_last_error": (ctypes.c_char_p, []),
