@@ -60,7 +60,7 @@ class ClockSampler:
     """SM clock and throttle-reason sampling (NVML, ~5 ms period) in a background
     thread during the timed region. Reads only; changes no GPU setting."""
 
-    def __init__(self, gpu_index: int, period_s: float = 0.005):
+    def __init__(self, gpu_index: int, period_s: float = 0.001):
         self.idx = gpu_index
         self.period = period_s
         self.rows = []
@@ -68,28 +68,38 @@ class ClockSampler:
         self._t = None
         self._nv = None
 
-    def _run(self):
+    def _sample(self, h, mx):
         nv = self._nv
-        h = nv.nvmlDeviceGetHandleByIndex(self.idx)
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        try:
+            rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        except Exception:
+            rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+        self.rows.append((sm, mx, rs))
+
+    def _run(self, h, mx):
         while not self._stop.is_set():
             try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.rows.append((sm, mx, rs))
-            except Exception:
-                pass
+                self._sample(h, mx)
+            except Exception as e:  # keep sampling; report the first failure
+                self.error = self.error or repr(e)
             self._stop.wait(self.period)
 
     def __enter__(self):
+        self.error = None
         try:
             import pynvml as nv
             nv.nvmlInit()
             self._nv = nv
-            self._t = threading.Thread(target=self._run, daemon=True)
+            h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._sample(h, mx)          # the calls work before the timed region starts
+            self.rows.clear()
+            self._t = threading.Thread(target=self._run, args=(h, mx), daemon=True)
             self._t.start()
-        except Exception:
+        except Exception as e:
             self._nv = None
+            self.error = repr(e)
         return self
 
     def __exit__(self, *a):
@@ -99,7 +109,8 @@ class ClockSampler:
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "error": self.error}
         import statistics
         nv = self._nv
         bits = {"hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
@@ -278,11 +289,12 @@ def run_ours(args):
                        "d2h_bytes_per_step": d2h},
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak, "traffic": traffic,
-                            "peak_kind": peak_kind, "kernel": "gdn_fwd_tc_kernel",
+                            "peak_kind": peak_kind,
+                            "kernel": "gdn_coef_kernel + gdn_fwd_tc_kernel (one forward call)",
                             "algo_bytes_per_launch": algo, "avg_launch_ms": kern_ms,
                             "tflops": _algo_flops(B, H, T, D) / (kern_ms / 1e3) / 1e12},
                "cpu_baseline": cpu,
-               "gpu_launches": args.steps,
+               "gpu_launches": 2 * args.steps,   # coefficient pre-pass + fused forward
                "clocks": clk.summary()}
         print(json.dumps(out), flush=True)
     if world > 1:
