@@ -280,11 +280,14 @@ def run_ours(args):
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                "data": "synthetic",
-               "config": {"workload": "cfg2: GDN chunk forward B4 H32 T16384 Dk=Dv=128 C64 bf16 "
-                                      "per GPU (weak scaling, 128 (b,h) pairs per GPU)",
+               "config": {"workload": ("cfg2: GDN chunk forward B4 H32 T16384 Dk=Dv=128 C64 bf16 "
+                                       "per GPU (weak scaling, 128 (b,h) pairs per GPU)"
+                                       if not args.shape else
+                                       f"custom shape B{B} H{H} T{T} D{D} (profiling case)"),
                           "B_per_gpu": B, "H": H, "T": T, "D": D, "C": CFG["C"],
                           "global_batch": B * world, "parallelism": f"(b,h) shards x{world}",
-                          "l2": "inputs 2.2 GB per GPU >> 126 MB L2 (no flush needed)"},
+                          "l2": f"inputs+outputs {algo / 1e9:.2f} GB per GPU vs 126 MB L2"
+                                + (" (no flush needed)" if algo > 126e6 * 4 else "")},
                "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                        "d2h_bytes_per_step": d2h},
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -323,7 +326,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--shape", type=int, nargs=4, metavar=("B", "H", "T", "D"),
+                    help="per-GPU problem other than config 2 (small cases for profiling; "
+                         "not a bench line of the headline metric)")
     args = ap.parse_args()
+    if args.shape:
+        CFG.update(B=args.shape[0], H=args.shape[1], T=args.shape[2], D=args.shape[3])
     if args.impl == "reference":
         run_reference(args)
     else:
