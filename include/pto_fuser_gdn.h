@@ -132,6 +132,18 @@ PTOF_API int ptof_gated_qk_exec(void* ws, const void* a, const void* b, const fl
                                 const void* beta, void* L, int M, int C, int D, int in_dtype,
                                 int beta_dtype, int causal, void* stream);
 
+/* The kkt + triangular-inverse stage alone, fused: per chunk of
+ * 64 tokens A = tril(beta_i k_i.k_j exp(g_i - g_j), -1) and T = (I + A)^-1, written
+ * as fp32 T_out [B, H, T/64, 64, 64] (chunk order b, h, c). k [B,H,T,D] or [B,T,H,D]
+ * (layout) in f16/bf16, D = 64 or 128; beta like g; g fp32 raw / chunk-local cumsum /
+ * ignored (gate_mode). Replaces the reference's kkt_exec (kernels/kkt_fused_lib.cpp:
+ * 401-443) followed by the external tri_inv (registry.py:96-140); matches
+ * _gdn_full.py:73-78. ws: a workspace from ptof_ws_setup (its status word records
+ * device wait timeouts) or NULL. */
+PTOF_API int ptof_kkt_inv_exec(void* ws, const void* k, const void* beta, const float* g,
+                               float* T_out, int B, int H, int T, int D, int in_dtype,
+                               int beta_dtype, int gate_mode, int layout, void* stream);
+
 /* (I + A)^-1 for strictly-lower A [M,C,C] (a_dtype), fp32 out [M,C,C]; replaces the
  * opaque tri_inv_rec_unroll kernel (registry.py:96-140). Unlike the reference it takes
  * A lower-triangular directly (no transpose round trip). ws may be NULL. */

@@ -257,6 +257,29 @@ int ptof_gated_qk_exec(void* ws, const void* a, const void* b, const float* g, c
                          static_cast<cudaStream_t>(stream));
 }
 
+int ptof_kkt_inv_exec(void* ws, const void* k, const void* beta, const float* g, float* T_out,
+                      int B, int H, int T, int D, int in_dtype, int beta_dtype, int gate_mode,
+                      int layout, void* stream) {
+  Workspace* w = static_cast<Workspace*>(ws);
+  if (B < 1 || H < 1 || T < kChunk || T % kChunk || (D != 64 && D != 128))
+    return fail(PTOF_EINVAL, "kkt_inv shape B=%d H=%d T=%d D=%d (T a multiple of 64, D 64 or 128)",
+                B, H, T, D);
+  if ((in_dtype != PTOF_F16 && in_dtype != PTOF_BF16) || !dtype_ok(beta_dtype))
+    return fail(PTOF_EINVAL, "kkt_inv dtype");
+  if (gate_mode < PTOF_GATE_RAW || gate_mode > PTOF_GATE_NONE || (layout != PTOF_LAYOUT_BHTD &&
+                                                                  layout != PTOF_LAYOUT_BTHD))
+    return fail(PTOF_EINVAL, "kkt_inv gate/layout");
+  int rc = check_ptrs({k, beta, T_out}, {g});
+  if (rc) return rc;
+  if (gate_mode != PTOF_GATE_NONE && !g) return fail(PTOF_EINVAL, "g is NULL for a gated kkt_inv");
+  ptof_gdn_params p{};
+  p.B = B; p.H = H; p.T = T; p.C = kChunk; p.Dk = D; p.Dv = D;
+  p.in_dtype = in_dtype; p.beta_dtype = beta_dtype; p.out_dtype = PTOF_F32;
+  p.gate_mode = gate_mode; p.layout = layout; p.scale = 1.f;
+  return launch_kkt_inv(p, w ? w->d_status : nullptr, k, beta, g, T_out,
+                        static_cast<cudaStream_t>(stream));
+}
+
 int ptof_tri_inv_exec(void* ws, const void* A, int a_dtype, float* T, int M, int C, void* stream) {
   (void)ws;
   if (M < 1 || C < 1 || C > 128) return fail(PTOF_EINVAL, "tri_inv shape M=%d C=%d", M, C);

@@ -59,6 +59,8 @@ int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v,
                       const void* beta, const float* g, const float* S0, void* o,
                       float* S_final, cudaStream_t stream);
 
+int launch_kkt_inv(const ptof_gdn_params& p, int* status, const void* k, const void* beta,
+                   const float* g, float* Tout, cudaStream_t st);
 int launch_gated_qk(int in_dtype, int beta_dtype, const void* a, const void* b, const float* g,
                     const void* beta, void* L, int M, int C, int D, int causal, cudaStream_t st);
 int launch_tri_inv(int a_dtype, const void* A, float* T, int M, int C, cudaStream_t st);

@@ -69,6 +69,13 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16_rn(x);
 }
 
+// Element i of a beta array of element type dt (PTOF_F32 / F16 / BF16) as fp32.
+__device__ __forceinline__ float ld_beta_any(const void* p, int dt, int64_t i) {
+  if (dt == PTOF_F32) return static_cast<const float*>(p)[i];
+  if (dt == PTOF_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
 // Decay coefficients, written exactly as the reference forward writes them
 // (examples/attention/_gdn_full.py:53-54 `_safe_exp`, :90-91 `exp(min(.,0))`).
 __device__ __forceinline__ float kkt_coef(float gi, float gj) {  // where(x<=0, exp(x), 0)

@@ -1,0 +1,191 @@
+// Warp-level building blocks on 128B-swizzled 64-column fp16 shared-memory tiles and
+// the 64x64 unit-lower-triangular inverse built from them, shared by the fused GDN
+// forward and the standalone kkt + inverse kernel.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace ptof {
+
+// Write 8 consecutive 16-bit values (one 16-byte chunk) of a 128B-swizzled row.
+__device__ __forceinline__ void st_chunk(unsigned char* region, int row, int chunk, uint4 v) {
+  *reinterpret_cast<uint4*>(region + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
+}
+__device__ __forceinline__ uint4 ld_chunk(const unsigned char* region, int row, int chunk) {
+  return *reinterpret_cast<const uint4*>(region + row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// ------------------------------------------------------- (I + A)^-1, 64 x 64 ----
+// T = (I + A)^-1 (A strictly lower), blocked over 16x16 blocks:
+//  level 0: the four diagonal blocks T_bb = (I + N)^-1, N = A_bb nilpotent, by
+//    the product form (I - N)(I + N^2)(I + N^4)(I + N^8) on warp MMAs (inv16_diag);
+//  level 1 (16 -> 32) and level 2 (32 -> 64): the block below the diagonal of a
+//    lower-triangular [[T11, 0], [A21, T22]]-pair is T21 = -(T22 A21) T11, two
+//    chained products done with warp-level fp16 MMAs (fp32 accumulate) whose first
+//    result is fed to the second straight from registers. A tcgen05 round trip
+//    (issue, commit, mbarrier, TMEM readout) costs ~0.5 us for these 16x16 / 32x32
+//    products, the warp-level form a few tens of cycles each.
+// All operands are fp16 (A and T entries are bounded by small multiples of 1 for
+// beta <= 1, decays <= 1 and unit-norm keys), accumulation fp32.
+
+// 16-bit element (row, col) of a 64-column 128B-swizzled tile
+__device__ __forceinline__ __half* tile_elem(unsigned char* tile, int row, int col) {
+  return reinterpret_cast<__half*>(tile + row * 128 + ((((col >> 3) ^ (row & 7)) << 4) |
+                                                       ((col & 7) << 1)));
+}
+
+// Warp-level MMA fragments (layouts in ptx.cuh) of 64-column 128B-swizzled fp16 tiles.
+// A fragment of the 16x16 block at (r0, c0).
+__device__ __forceinline__ void frag_a(const unsigned char* tile, int r0, int c0, int lane,
+                                       uint32_t (&a)[4]) {
+  const int mi = lane >> 3, row = r0 + (lane & 7) + ((mi & 1) << 3), ch = (c0 >> 3) + (mi >> 1);
+  ldsm_x4(smem_u32(tile + row * 128 + ((ch ^ (row & 7)) << 4)), a);
+}
+// B fragments of the two 8-column n-tiles (n0, n0 + 8) over the k rows k0..k0+15 of a
+// row-major [k][n] tile: b[0], b[1] for n-tile n0 and b[2], b[3] for n0 + 8.
+__device__ __forceinline__ void frag_b2(const unsigned char* tile, int k0, int n0, int lane,
+                                        uint32_t (&b)[4]) {
+  const int mi = lane >> 3, row = k0 + (lane & 7) + ((mi & 1) << 3), ch = (n0 >> 3) + (mi >> 1);
+  ldsm_x4_t(smem_u32(tile + row * 128 + ((ch ^ (row & 7)) << 4)), b);
+}
+// The fp32 accumulators of a 16x16 product (two n-tiles) as the fp16 A fragment of
+// the next product (the C layout of m16n8 equals the A layout of m16k16).
+__device__ __forceinline__ void c_to_a(const float (&d0)[4], const float (&d1)[4], uint32_t (&a)[4]) {
+  a[0] = pack_f16(d0[0], d0[1]);
+  a[1] = pack_f16(d0[2], d0[3]);
+  a[2] = pack_f16(d1[0], d1[1]);
+  a[3] = pack_f16(d1[2], d1[3]);
+}
+// Store s * C (one 16x8 n-tile at (r0, n0)) into a 64-column swizzled fp16 tile.
+__device__ __forceinline__ void st_c(unsigned char* tile, int r0, int n0, int lane,
+                                     const float (&d)[4], float sgn) {
+  const int g = lane >> 2, t = lane & 3;
+  *reinterpret_cast<__half2*>(tile_elem(tile, r0 + g, n0 + 2 * t)) =
+      __floats2half2_rn(sgn * d[0], sgn * d[1]);
+  *reinterpret_cast<__half2*>(tile_elem(tile, r0 + g + 8, n0 + 2 * t)) =
+      __floats2half2_rn(sgn * d[2], sgn * d[3]);
+}
+// A fragment of the transpose of the 16x16 block at (r0, c0).
+__device__ __forceinline__ void frag_at(const unsigned char* tile, int r0, int c0, int lane,
+                                        uint32_t (&a)[4]) {
+  const int mi = lane >> 3, row = r0 + (lane & 7) + ((mi >> 1) << 3), ch = (c0 >> 3) + (mi & 1);
+  ldsm_x4_t(smem_u32(tile + row * 128 + ((ch ^ (row & 7)) << 4)), a);
+}
+// 16x16 products on register pairs (X, X^T), each held as an A fragment: an A
+// fragment of X^T is exactly the pair of B fragments of X, so P X needs no data
+// movement: n-tile 0 uses (xt[0], xt[2]), n-tile 1 (xt[1], xt[3]).
+__device__ __forceinline__ void mma16(float (&d0)[4], float (&d1)[4], const uint32_t (&pa)[4],
+                                      const uint32_t (&xt)[4]) {
+  mma_f16_16816(d0, pa, xt[0], xt[2]);
+  mma_f16_16816(d1, pa, xt[1], xt[3]);
+}
+__device__ __forceinline__ void zero4(float (&d)[4]) { d[0] = d[1] = d[2] = d[3] = 0.f; }
+// T = (I + N)^-1 of the strictly lower 16x16 block N at (r0, r0) of the fp16 tile
+// `a_tile`, written (fp16) to the same block of `t_tile`. N is nilpotent (N^16 = 0),
+// so (I + N)^-1 = (I - N)(I + N^2)(I + N^4)(I + N^8): 16 warp MMAs on a dependency
+// chain five products deep, fp32 accumulate, fp16 intermediates. One warp.
+__device__ __forceinline__ void inv16_diag(const unsigned char* a_tile, unsigned char* t_tile,
+                                           int r0, int lane) {
+  uint32_t na[4], nt[4], x2a[4], x2t[4], x4a[4], x4t[4], x8t[4], pa[4];
+  frag_a(a_tile, r0, r0, lane, na);
+  frag_at(a_tile, r0, r0, lane, nt);
+  float d0[4], d1[4], e0[4], e1[4];
+  zero4(d0); zero4(d1); zero4(e0); zero4(e1);
+  mma16(d0, d1, na, nt);          // N^2
+  mma16(e0, e1, nt, na);          // (N^2)^T = N^T N^T
+  c_to_a(d0, d1, x2a);
+  c_to_a(e0, e1, x2t);
+  // P1 = I - N + N^2 - N N^2 (accumulated on top of N^2 in fp32)
+  const int g = lane >> 2, t = lane & 3;
+  const float2 n00 = unpack_f16(na[0]), n10 = unpack_f16(na[1]);
+  const float2 n01 = unpack_f16(na[2]), n11 = unpack_f16(na[3]);
+  float p0[4] = {d0[0] - n00.x + (g == 2 * t ? 1.f : 0.f), d0[1] - n00.y + (g == 2 * t + 1 ? 1.f : 0.f),
+                 d0[2] - n10.x, d0[3] - n10.y};
+  float p1[4] = {d1[0] - n01.x, d1[1] - n01.y, d1[2] - n11.x + (g == 2 * t ? 1.f : 0.f),
+                 d1[3] - n11.y + (g == 2 * t + 1 ? 1.f : 0.f)};
+  zero4(d0); zero4(d1); zero4(e0); zero4(e1);
+  mma16(d0, d1, x2a, x2t);        // N^4
+  mma16(e0, e1, x2t, x2a);        // (N^4)^T
+  float q0[4], q1[4];
+  zero4(q0); zero4(q1);
+  mma16(q0, q1, na, x2t);         // N^3 = N N^2
+#pragma unroll
+  for (int m = 0; m < 4; ++m) { p0[m] -= q0[m]; p1[m] -= q1[m]; }
+  c_to_a(d0, d1, x4a);
+  c_to_a(e0, e1, x4t);
+  zero4(e0); zero4(e1);
+  mma16(e0, e1, x4t, x4a);        // (N^8)^T
+  c_to_a(e0, e1, x8t);
+  c_to_a(p0, p1, pa);
+  mma16(p0, p1, pa, x4t);         // P2 = P1 + P1 N^4
+  c_to_a(p0, p1, pa);
+  mma16(p0, p1, pa, x8t);         // T  = P2 + P2 N^8
+  st_c(t_tile, r0, r0, lane, p0, 1.f);
+  st_c(t_tile, r0, r0 + 8, lane, p1, 1.f);
+}
+
+// (I + A)^-1 of the strictly lower 64x64 fp16 tile, in place (its strictly upper
+// blocks must hold zeros), by four whole warps w = 0..3 of one CTA. Named barriers:
+// pair_bar and pair_bar + 1 (64 threads: warps 0-1, 2-3) and all_bar (128 threads).
+// On return every warp's stores of T are visible to the four warps.
+__device__ __forceinline__ void tri_inv64_inplace(unsigned char* tile, int w, int l, int pair_bar,
+                                                  int all_bar) {
+  // level 0 (warp w): T_bb = (I + N)^-1 of the diagonal block N = A_bb
+  inv16_diag(tile, tile, 16 * w, l);
+  // level 1 (warps 0, 2): T21 = -(T22 A21) T11 for the block pairs (0,1), (2,3)
+  named_bar_sync(pair_bar + (w >> 1), 64);
+  if ((w & 1) == 0) {
+    const int r1 = 16 * w + 16, c1 = r1 - 16;
+    uint32_t a[4], bf[4], za[4];
+    frag_a(tile, r1, r1, l, a);
+    frag_b2(tile, r1, c1, l, bf);
+    float z0[4] = {0.f, 0.f, 0.f, 0.f}, z1[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_f16_16816(z0, a, bf[0], bf[1]);
+    mma_f16_16816(z1, a, bf[2], bf[3]);
+    c_to_a(z0, z1, za);
+    frag_b2(tile, c1, c1, l, bf);
+    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_f16_16816(o0, za, bf[0], bf[1]);
+    mma_f16_16816(o1, za, bf[2], bf[3]);
+    st_c(tile, r1, c1, l, o0, -1.f);
+    st_c(tile, r1, c1 + 8, l, o1, -1.f);
+  }
+  // level 2: T[32:64, 0:32] = -(T_BB A_BA) T_AA; warp (rb, ch) owns rows
+  // 32 + 16 rb .. +15 and columns 16 ch .. +15
+  named_bar_sync(all_bar, 128);
+  {
+    const int rb = w >> 1, chh = w & 1, R = 32 + 16 * rb;
+    float z[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) zero4(z[n]);
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      if (rb == 0 && ks == 1) continue;   // T[32:48, 48:64] = 0
+      uint32_t a[4], bf[4];
+      frag_a(tile, R, 32 + 16 * ks, l, a);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        frag_b2(tile, 32 + 16 * ks, 16 * np, l, bf);
+        mma_f16_16816(z[2 * np], a, bf[0], bf[1]);
+        mma_f16_16816(z[2 * np + 1], a, bf[2], bf[3]);
+      }
+    }
+    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      if (chh == 1 && ks == 0) continue;  // T[0:16, 16:32] = 0
+      uint32_t za[4], bf[4];
+      c_to_a(z[2 * ks], z[2 * ks + 1], za);
+      frag_b2(tile, 16 * ks, 16 * chh, l, bf);
+      mma_f16_16816(o0, za, bf[0], bf[1]);
+      mma_f16_16816(o1, za, bf[2], bf[3]);
+    }
+    named_bar_sync(all_bar, 128);   // every warp has read A_BA before T_BA replaces it
+    st_c(tile, R, 16 * chh, l, o0, -1.f);
+    st_c(tile, R, 16 * chh + 8, l, o1, -1.f);
+  }
+  named_bar_sync(all_bar, 128);
+}
+
+}  // namespace ptof
