@@ -6,11 +6,14 @@
 // external tri_inv pair (kernels/kkt_fused_lib.cpp:401-443, registry.py:96-140).
 //
 // Persistent CTAs, three per SM, each walking chunks m = blockIdx.x + k * gridDim.x:
-//   warp 4      one thread: TMA producer of K tiles (3-stage ring) and UMMA issuer of
+//   warp 4      one thread: TMA producer of K tiles (2-stage ring) and UMMA issuer of
 //               KK^T (M = N = 64, fp32 accumulators in two TMEM buffers)
-//   warps 0-3   gate cumsum (warp 0, prefetched one chunk ahead), KK^T epilogue from
-//               TMEM with the exact per-element coefficients -> fp16 A tile,
-//               (I + A)^-1 in place on warp-level MMAs, T -> global fp32
+//   warps 0-3   gate cumsum and coefficients (warp 0, g and beta prefetched one chunk
+//               ahead), KK^T epilogue from TMEM -> fp16 A tile: beta_i e^{g_i - g_0}
+//               e^{g_0 - g_j} for monotone chunks with total decay < 80, else the exact
+//               per-element safe_exp,
+//               (I + A)^-1 in place on warp-level MMAs, T -> fp32 staging tile ->
+//               one asynchronous bulk store per chunk
 // HBM-bound: per chunk 16 KB of K in, 16 KB of T out, 384 B of g and beta.
 #include <cuda_runtime.h>
 
@@ -24,7 +27,7 @@ namespace kktinv {
 
 constexpr int kC = kChunk;   // 64
 constexpr int kThreads = 160;
-constexpr int kNS = 3;       // K ring depth
+constexpr int kNS = 2;       // K ring depth (3 CTAs per SM fit with the T staging tile)
 constexpr int kAllBar = 1;   // named barriers: 1 = the four compute warps, 2-3 = pairs
 
 template <int D>
@@ -32,8 +35,12 @@ struct KLayout {
   static constexpr int NKB = D / 64;
   static constexpr int STAGE = NKB * kC * 128;       // K rows x (64 d) per 128B-swizzled region
   static constexpr int OFF_A = kNS * STAGE;          // fp16 A -> T tile, 8 KB
-  static constexpr int OFF_G = OFF_A + kC * 128;     // fp32 gcum[64], beta[64]
-  static constexpr int OFF_BAR = OFF_G + 512;
+  // fp32 T staging tile [64][64] for the chunk's bulk store
+  static constexpr int OFF_TS = OFF_A + kC * 128;
+  // fp32 gcum[64], beta[64], rowfb[64] = beta_i e^{g_i - g_0}, colf[64] = e^{g_0 - g_j},
+  // then the chunk's fast-path flag
+  static constexpr int OFF_G = OFF_TS + kC * kC * 4;
+  static constexpr int OFF_BAR = OFF_G + 1024 + 16;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
   static constexpr int TCOLS = 2 * kC;               // two fp32 64x64 accumulators
 };
@@ -135,6 +142,9 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_c
     unsigned char* at = sm + L::OFF_A;
     float* gcum = reinterpret_cast<float*>(sm + L::OFF_G);
     float* bsm = gcum + kC;
+    float* rowfb = gcum + 2 * kC;
+    float* colf = gcum + 3 * kC;
+    int* fastp = reinterpret_cast<int*>(gcum + 4 * kC);
     // warp 0: g and beta of a chunk, two tokens per lane (prefetched one chunk ahead)
     float pg0 = 0.f, pg1 = 0.f, pb0 = 0.f, pb1 = 0.f;
     auto fetch = [&](int64_t k) {
@@ -157,7 +167,9 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_c
       if (w == 0) {
         float g0 = pg0, g1 = pg1;
         const float b0 = pb0, b1 = pb1;
+        bool mono = true;   // the chunk-local cumsum never increases
         if (P.gate_mode == PTOF_GATE_RAW) {
+          mono = (g0 <= 0.f) && (g1 <= 0.f);
           g1 += g0;
           float run = g1;
 #pragma unroll
@@ -167,9 +179,21 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_c
           }
           g0 += run - g1;
           g1 = run;
+        } else if (P.gate_mode == PTOF_GATE_CUMSUM) {
+          const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
+          mono = (g1 <= g0) && (l == 0 || g0 <= prev);
         }
+        // exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j): overflow-free when the cumsum is
+        // monotone and the chunk's total decay is below 80; otherwise the exact form
+        const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
+        const float gl = __shfl_sync(0xffffffffu, g1, 31);
+        const bool fast = __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
         reinterpret_cast<float2*>(gcum)[l] = make_float2(g0, g1);
         reinterpret_cast<float2*>(bsm)[l] = make_float2(b0, b1);
+        reinterpret_cast<float2*>(rowfb)[l] =
+            make_float2(b0 * __expf(g0 - gfirst), b1 * __expf(g1 - gfirst));
+        reinterpret_cast<float2*>(colf)[l] = make_float2(__expf(gfirst - g0), __expf(gfirst - g1));
+        if (l == 0) *fastp = fast ? 1 : 0;
         if (k + 1 < cnt) fetch(k + 1);
       }
       named_bar_sync(kAllBar, 128);   // gcum / beta of chunk k
@@ -186,7 +210,8 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_c
       __syncwarp();
       if (l == 0) mbar_arrive(&bars[K_TFREE0 + bb]);
       if (l < 16) {
-        const float gi = gcum[i], bi = bsm[i];
+        const bool fast = *fastp != 0;
+        const float gi = gcum[i], bi = bsm[i], rb = rowfb[i];
 #pragma unroll
         for (int j0 = 0; j0 < kC; j0 += 8) {
           uint32_t pk[4];
@@ -196,7 +221,8 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_c
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int j = j0 + 2 * u + e;
-              a2[e] = (j < i) ? v[j] * bi * kkt_coef(gi, gcum[j]) : 0.f;
+              const float cf = fast ? rb * colf[j] : bi * kkt_coef(gi, gcum[j]);
+              a2[e] = (j < i) ? v[j] * cf : 0.f;
             }
             pk[u] = pack_f16(a2[0], a2[1]);
           }
@@ -206,21 +232,28 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_c
       }
       named_bar_sync(kAllBar, 128);   // A complete
       tri_inv64_inplace(at, w, l, 2, kAllBar);
-      // ---- T -> global fp32: thread t owns row t / 2, columns 32 (t & 1) .. +31 ----
-      {
-        const int row = tid >> 1, c0 = 32 * (tid & 1);
-        float4* dst = reinterpret_cast<float4*>(P.Tout + m * (kC * kC) + row * kC + c0);
+      // ---- T -> fp32 staging tile (linear float4 f = tid + 128 it: row f / 16,
+      //      columns 4 (f % 16) ..) -> one asynchronous 16 KB bulk store per chunk ----
+      float* ts = reinterpret_cast<float*>(sm + L::OFF_TS);
+      if (tid == 0) bulk_wait_read0();   // the previous chunk's store has read the tile
+      named_bar_sync(kAllBar, 128);
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const uint4 u = *reinterpret_cast<const uint4*>(at + row * 128 + ((((c0 >> 3) + q8) ^ (row & 7)) << 4));
-          const float2 f0 = unpack_f16(u.x), f1 = unpack_f16(u.y), f2 = unpack_f16(u.z), f3 = unpack_f16(u.w);
-          dst[2 * q8] = make_float4(f0.x, f0.y, f1.x, f1.y);
-          dst[2 * q8 + 1] = make_float4(f2.x, f2.y, f3.x, f3.y);
-        }
+      for (int it = 0; it < 8; ++it) {
+        const int f = tid + 128 * it, row = f >> 4, col = (f & 15) * 4;
+        const uint2 u = *reinterpret_cast<const uint2*>(
+            at + row * 128 + ((((col >> 3) ^ (row & 7)) << 4) | ((col & 7) << 1)));
+        const float2 lo = unpack_f16(u.x), hi = unpack_f16(u.y);
+        reinterpret_cast<float4*>(ts)[f] = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
-      named_bar_sync(kAllBar, 128);   // the tile and gcum are free for the next chunk
+      fence_async_smem();
+      named_bar_sync(kAllBar, 128);   // staging complete; A tile and gcum free again
+      if (tid == 0) {
+        bulk_store(P.Tout + m * (kC * kC), ts, kC * kC * 4);
+        bulk_commit();
+      }
     }
   }
+  if (tid == 0) bulk_wait0();   // the last T store has completed
   __syncthreads();
   tc_fence_after();
   if (warp == 4) tmem_dealloc(tmem, L::TCOLS);
