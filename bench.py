@@ -319,6 +319,83 @@ def _ncu_traffic():
     return None
 
 
+def run_configs(args):
+    """One JSON line per BASELINE configuration on one GPU: device time of the op
+    through its C ABI (CUDA events, inputs resident, 3 warm-up calls), with the
+    algorithmic HBM bytes of the configuration and its roofline fraction. These are
+    supporting numbers; the headline line is the default mode (config 2)."""
+    import torch
+    from pto_fuser import GDNChunkForward, native as nv
+    peaks = _peaks()
+    hbm = peaks[0]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    nrm = torch.nn.functional.normalize
+
+    def inputs(B, H, T, D, dt, mu=2.0, gated=True):
+        q = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).to(dt)
+        k = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).to(dt)
+        v = torch.randn(B, H, T, D, device=dev, generator=gen).to(dt)
+        beta = torch.sigmoid(torch.randn(B, H, T, device=dev, generator=gen)).to(dt)
+        g = torch.nn.functional.logsigmoid(torch.randn(B, H, T, device=dev, generator=gen) + mu)
+        return q, k, v, beta, (g if gated else torch.zeros_like(g))
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    def line(name, desc, ms, tokens, algo, dtype):
+        print(json.dumps({"config": name, "workload": desc, "ms": ms,
+                          "tokens_per_s": tokens / (ms / 1e3), "dtype": dtype,
+                          "algo_bytes": algo, "achieved_gbs": algo / (ms / 1e3) / 1e9,
+                          "roofline_frac_hbm": algo / (ms / 1e3) / 1e9 / hbm,
+                          "peak_gbs": hbm}), flush=True)
+
+    def fwd(name, desc, B, H, T, D, dt, mu=2.0, gate="raw", s0_std=None):
+        q, k, v, beta, g = inputs(B, H, T, D, dt, mu, gate != "none")
+        S0 = (torch.randn(B, H, D, D, device=dev, generator=gen) * s0_std) if s0_std else None
+        r = GDNChunkForward(B, H, T, D, D, in_dtype=dt, gate=gate)
+        o = torch.empty_like(v)
+        S = torch.empty(B, H, D, D, device=dev)
+        ms = timed(lambda: r(q, k, v, beta, g, S0, o=o, final_state=S), args.steps)
+        r.check_status()
+        e = 2 if dt != torch.float32 else 4
+        per_tok = 3 * D * e + e + (4 if gate != "none" else 0) + D * e
+        algo = B * H * T * per_tok + B * H * D * D * 4 * (2 if S0 is not None else 1)
+        line(name, desc, ms, B * T, algo, str(dt).split(".")[-1])
+        r.close()
+
+    fwd("cfg0", "GDN forward fp32 B1 H4 T512 D128 (SIMT fp32 path)", 1, 4, 512, 128, torch.float32)
+    # cfg1: kkt + inverse alone
+    B, H, T, D = 8, 32, 8192, 128
+    _, k, _, beta, g = inputs(B, H, T, D, torch.bfloat16)
+    out = torch.empty(B, H, T // 64, 64, 64, device=dev)
+    ws = nv.lib().ptof_ws_setup()
+    ms = timed(lambda: nv.check(nv.lib().ptof_kkt_inv_exec(
+        ws, k.data_ptr(), beta.data_ptr(), g.data_ptr(), out.data_ptr(), B, H, T, D, nv.BF16,
+        nv.BF16, nv.GATE_RAW, nv.LAYOUT_BHTD, nv.stream_handle())), args.steps)
+    nv.check(nv.lib().ptof_check_status(ws, nv.stream_handle()))
+    nv.lib().ptof_ws_teardown(ws)
+    M = B * H * (T // 64)
+    line("cfg1", "kkt + tri-inv B8 H32 T8192 D128 bf16 -> fp32 T", ms, B * T,
+         M * (64 * D * 2 + 64 * 2 + 64 * 4 + 64 * 64 * 4), "bf16")
+    del k, beta, g, out
+    fwd("cfg2", "GDN forward bf16 B4 H32 T16384 D128", 4, 32, 16384, 128, torch.bfloat16)
+    fwd("cfg3", "DeltaNet (g = 0) bf16 B16 H16 T4096 D64", 16, 16, 4096, 64, torch.bfloat16,
+        gate="none")
+    fwd("cfg4", "long-context GDN bf16 B1 H64 T131072 D128, S0 ~ N(0,0.02^2), mu 3", 1, 64,
+        131072, 128, torch.bfloat16, mu=3.0, s0_std=0.02)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -326,13 +403,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--configs", action="store_true",
+                    help="one supporting JSON line per BASELINE configuration (0-4), 1 GPU")
     ap.add_argument("--shape", type=int, nargs=4, metavar=("B", "H", "T", "D"),
                     help="per-GPU problem other than config 2 (small cases for profiling; "
                          "not a bench line of the headline metric)")
     args = ap.parse_args()
     if args.shape:
         CFG.update(B=args.shape[0], H=args.shape[1], T=args.shape[2], D=args.shape[3])
-    if args.impl == "reference":
+    if args.configs:
+        run_configs(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
