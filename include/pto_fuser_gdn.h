@@ -92,6 +92,28 @@ PTOF_API int ptof_gdn_fwd_exec(void* ws, const void* q, const void* k, const voi
                       const float* g, const float* S0, void* o, float* S_final, void* stream);
 PTOF_API void ptof_gdn_fwd_teardown(void* ws);
 
+/* Variable-length sequences with grouped query/key heads (the production layout the
+ * reference leaves out: registry.py:124 passes cu_seqlens=None; gdn_mega.py:49-50).
+ * N sequences packed token-major: q, k [T_total, Hg, Dk]; v, o [T_total, H, Dv];
+ * beta, g [T_total, H]; sequence n spans tokens [cu_seqlens[n], cu_seqlens[n+1])
+ * (device int32 [N+1], non-decreasing, every length <= max_len; a longer one is cut
+ * at max_len and reported by ptof_check_status). Value head h reads query/key head
+ * h / (H / Hg). Chunks start at each sequence's first token; the last chunk of a
+ * sequence may be partial. S0 / S_final [N, H, Dk, Dv] fp32 (optional). f16/bf16
+ * operands, Dk = Dv = 64 or 128. Empty sequences return S_final = S0 (or 0). */
+typedef struct ptof_gdn_varlen_params {
+  int32_t N, H, Hg;    /* sequences, value heads, query/key heads (H % Hg == 0) */
+  int32_t T_total;     /* packed tokens                                        */
+  int32_t max_len;     /* upper bound of every sequence length                 */
+  int32_t Dk, Dv;
+  int32_t in_dtype, beta_dtype, out_dtype, gate_mode;
+  float scale;
+} ptof_gdn_varlen_params;
+PTOF_API void* ptof_gdn_fwd_varlen_setup(const ptof_gdn_varlen_params* p);
+PTOF_API int ptof_gdn_fwd_varlen_exec(void* ws, const void* q, const void* k, const void* v,
+                                      const void* beta, const float* g, const int* cu_seqlens,
+                                      const float* S0, void* o, float* S_final, void* stream);
+
 /* The same f16/bf16 tensor-core forward without a workspace and without any device
  * allocation. It has no counterpart in the reference. It is for callers that cannot
  * call cudaMalloc, e.g. code inside a device-memory allocator or arena that owns all

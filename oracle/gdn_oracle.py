@@ -217,3 +217,50 @@ def rel_l2(got, ref) -> float:
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+def gdn_forward_varlen(q, k, v, beta, g, cu_seqlens, scale, S0=None, C=C_DEFAULT, gate="raw",
+                       dtype=np.float64):
+    """Variable-length, grouped-query GDN forward: sequences packed token-major.
+
+    q, k [T_total, Hg, Dk]; v [T_total, H, Dv]; beta, g [T_total, H]; sequence n spans
+    tokens [cu_seqlens[n], cu_seqlens[n+1]); value head h reads query/key head
+    h // (H // Hg); S0 [N, H, Dk, Dv] or None. Each sequence is gdn_forward on its own
+    tokens (chunks start at its first token), padded at the end to whole chunks with
+    beta = 0 and a flat gate (raw decay 0, or the last cumsum value repeated), which
+    leaves the recurrence over the real tokens unchanged.
+    Returns (o [T_total, H, Dv], S_final [N, H, Dk, Dv])."""
+    q, k, v = _f(q, dtype), _f(k, dtype), _f(v, dtype)
+    beta, g = _f(beta, dtype), _f(g, dtype) if g is not None else None
+    cu = [int(x) for x in cu_seqlens]
+    N = len(cu) - 1
+    T_total, Hg, Dk = q.shape
+    H, Dv = v.shape[1], v.shape[2]
+    grp = H // Hg
+    o = np.zeros((T_total, H, Dv), dtype=dtype)
+    S_out = np.zeros((N, H, Dk, Dv), dtype=dtype)
+    for n in range(N):
+        a, b = cu[n], cu[n + 1]
+        L = b - a
+        if L == 0:
+            if S0 is not None:
+                S_out[n] = _f(S0, dtype)[n]
+            continue
+        Lp = -(-L // C) * C
+        pad = lambda x: np.concatenate([x, np.zeros((Lp - L,) + x.shape[1:], dtype)], 0)
+        qh = pad(q[a:b])[:, np.arange(H) // grp].transpose(1, 0, 2)[None]
+        kh = pad(k[a:b])[:, np.arange(H) // grp].transpose(1, 0, 2)[None]
+        vh = pad(v[a:b]).transpose(1, 0, 2)[None]
+        bh = pad(beta[a:b]).T[None]
+        if g is None or gate == "none":
+            gh = np.zeros_like(bh)
+        elif gate == "cumsum":
+            gp = np.concatenate([g[a:b], np.repeat(g[b - 1:b], Lp - L, 0)], 0)
+            gh = gp.T[None]
+        else:
+            gh = pad(g[a:b]).T[None]
+        s0 = None if S0 is None else _f(S0, dtype)[n:n + 1]
+        on, Sn = gdn_forward(qh, kh, vh, bh, gh, scale, S0=s0, C=C, gate=gate, dtype=dtype)
+        o[a:b] = on[0].transpose(1, 0, 2)[:L]
+        S_out[n] = Sn[0]
+    return o, S_out

@@ -210,7 +210,59 @@ int ptof_gdn_fwd_exec(void* wsv, const void* q, const void* k, const void* v, co
     if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_simt launch");
     return PTOF_OK;
   }
-  return launch_gdn_fwd_tc(w, q, k, v, beta, g, S0, o, S_final, st);
+  return launch_gdn_fwd_tc(w, q, k, v, beta, g, S0, o, S_final, nullptr, st);
+}
+
+void* ptof_gdn_fwd_varlen_setup(const ptof_gdn_varlen_params* v) {
+  if (!v) {
+    fail(PTOF_EINVAL, "null params");
+    return nullptr;
+  }
+  if (v->N < 1 || v->H < 1 || v->Hg < 1 || v->H % v->Hg || v->T_total < 0 || v->max_len < 1) {
+    fail(PTOF_EINVAL, "varlen shape N=%d H=%d Hg=%d T_total=%d max_len=%d (H a multiple of Hg)",
+         v->N, v->H, v->Hg, v->T_total, v->max_len);
+    return nullptr;
+  }
+  ptof_gdn_params p{};
+  p.B = v->N; p.H = v->H; p.T = v->max_len; p.C = kChunk; p.Dk = v->Dk; p.Dv = v->Dv;
+  p.in_dtype = v->in_dtype; p.beta_dtype = v->beta_dtype; p.out_dtype = v->out_dtype;
+  p.gate_mode = v->gate_mode; p.layout = PTOF_LAYOUT_BTHD; p.scale = v->scale;
+  if (p.in_dtype == PTOF_F32 || !gdn_fwd_tc_supports(p)) {
+    fail(PTOF_EUNSUPPORTED, "varlen forward: f16/bf16 operands, Dk = Dv = 64 or 128");
+    return nullptr;
+  }
+  if (!dtype_ok(p.beta_dtype) || !dtype_ok(p.out_dtype) || p.gate_mode < PTOF_GATE_RAW ||
+      p.gate_mode > PTOF_GATE_NONE) {
+    fail(PTOF_EINVAL, "varlen dtype / gate");
+    return nullptr;
+  }
+  Workspace* w = ws_create(kWsGdnFwd, &p);
+  if (!w) return nullptr;
+  w->ex[0] = 1;
+  w->ex[1] = v->Hg;
+  w->ex[2] = v->T_total;
+  w->scratch_bytes = gdn_fwd_tc_scratch_bytes(p);
+  const cudaError_t e = cudaMalloc(&w->d_scratch, w->scratch_bytes);
+  if (e != cudaSuccess) {
+    cuda_fail(e, "gdn_fwd coefficient buffer");
+    ws_destroy(w);
+    return nullptr;
+  }
+  return w;
+}
+
+int ptof_gdn_fwd_varlen_exec(void* wsv, const void* q, const void* k, const void* v,
+                             const void* beta, const float* g, const int* cu_seqlens,
+                             const float* S0, void* o, float* S_final, void* stream) {
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w || w->kind != kWsGdnFwd || w->ex[0] != 1)
+    return fail(PTOF_EINVAL, "not a varlen gdn_fwd workspace");
+  if (!cu_seqlens) return fail(PTOF_EINVAL, "cu_seqlens is NULL");
+  int rc = check_ptrs({q, k, v, beta, o}, {S0, S_final});
+  if (rc) return rc;
+  if (w->p.gate_mode != PTOF_GATE_NONE && !g) return fail(PTOF_EINVAL, "g is NULL for a gated forward");
+  return launch_gdn_fwd_tc(w, q, k, v, beta, g, S0, o, S_final, cu_seqlens,
+                           static_cast<cudaStream_t>(stream));
 }
 
 void ptof_gdn_fwd_teardown(void* ws) { ws_destroy(static_cast<Workspace*>(ws)); }

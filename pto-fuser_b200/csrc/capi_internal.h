@@ -55,9 +55,10 @@ bool gdn_fwd_tc_supports(const ptof_gdn_params& p);
 // bytes of the per-chunk coefficient records the tensor-core forward keeps in the
 // workspace (allocated by ptof_gdn_fwd_setup)
 size_t gdn_fwd_tc_scratch_bytes(const ptof_gdn_params& p);
+// cu_seqlens: device int32 [p.B + 1] for variable-length workspaces (ex[0] = 1), else null
 int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v,
                       const void* beta, const float* g, const float* S0, void* o,
-                      float* S_final, cudaStream_t stream);
+                      float* S_final, const int* cu_seqlens, cudaStream_t stream);
 
 int launch_kkt_inv(const ptof_gdn_params& p, int* status, const void* k, const void* beta,
                    const float* g, float* Tout, cudaStream_t st);

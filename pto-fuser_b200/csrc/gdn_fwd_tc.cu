@@ -137,6 +137,11 @@ struct Params {
   int trace_chunks;
   int B, H, T, nc;
   int layout;
+  // variable-length sequences: B sequences packed token-major, sequence b spans tokens
+  // [cu_seqlens[b], cu_seqlens[b+1]) of every tensor; null for fixed length T
+  const int* cu_seqlens;
+  int mnc;                         // coefficient records per (b, h) (>= chunks of any sequence)
+  int gqa;                         // value heads per query/key head (q, k have H / gqa heads)
   int64_t os_b, os_h, os_t;        // o strides (elements)
   float scale;
 };
@@ -183,14 +188,34 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
   return F16 ? unpack_f16(u) : unpack_bf16(u);
 }
 
+// Output rows of a partial last chunk: tokens [0, lim) of O^T row v (TMEM, 64 columns,
+// scaled by osc) to o; kept out of line so the full-chunk store loop stays unchanged.
+template <typename TO>
+__device__ __noinline__ void store_tail(uint32_t t_o, TO* op, const float* osc, int64_t os_t,
+                                        int lim, bool active) {
+#pragma unroll 1
+  for (int c0 = 0; c0 < 64; c0 += 16) {
+    float x[16];
+    tmem_ld16(t_o + c0, x);
+    tmem_wait_ld();
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      if (active && c0 + m < lim) *op = from_f32<TO>(x[m] * osc[c0 + m]);
+      op += os_t;
+    }
+  }
+}
+
 // ------------------------------------------------------ coefficient pre-pass ----
 struct CoefParams {
   const float* g;        // [B,H,T] / [B,T,H] fp32, raw or chunk-local cumsum (null: ungated)
   const void* beta;
-  unsigned char* out;    // [B*H*nc][coef::BYTES]
-  int B, H, nc;
+  unsigned char* out;    // [B*H][nc][coef::BYTES]
+  int B, H, nc;          // nc: records per (b, h)
   int gate_mode, beta_dtype, allow_fast;
   int64_t gs_b, gs_h, gs_t;
+  const int* cu_seqlens; // variable-length sequences (token-major), or null
+  int T;                 // fixed sequence length (cu_seqlens null)
 };
 
 // One warp per chunk, lane l owns tokens 2l and 2l+1: chunk-local cumsum of the
@@ -205,12 +230,28 @@ __global__ void __launch_bounds__(256) gdn_coef_kernel(const __grid_constant__ C
   if (chunk >= static_cast<int64_t>(P.B) * P.H * P.nc) return;
   const int bh = static_cast<int>(chunk / P.nc), c = static_cast<int>(chunk % P.nc);
   const int b = bh / P.H, h = bh % P.H;
-  const int64_t gb = b * P.gs_b + h * P.gs_h + static_cast<int64_t>(c) * kC * P.gs_t;
+  int len = P.T;
+  int64_t gb = b * P.gs_b;
+  if (P.cu_seqlens != nullptr) {
+    const int st = P.cu_seqlens[b], en = P.cu_seqlens[b + 1];
+    len = en > st ? en - st : 0;
+    if (c * kC >= len) return;   // beyond this sequence: record unused
+    gb = static_cast<int64_t>(st) * P.gs_t;
+  }
+  gb += h * P.gs_h + static_cast<int64_t>(c) * kC * P.gs_t;
   const int64_t i0 = gb + static_cast<int64_t>(2 * l) * P.gs_t, i1 = i0 + P.gs_t;
+  // tokens past the end of the sequence (the ragged last chunk) get beta = 0 and
+  // g = 0: their rows of A, W, U and V_new vanish and the state is not decayed
+  const bool ok0 = c * kC + 2 * l < len, ok1 = c * kC + 2 * l + 1 < len;
   float g0 = 0.f, g1 = 0.f;
   if (P.gate_mode != PTOF_GATE_NONE) {
-    g0 = P.g[i0];
-    g1 = P.g[i1];
+    // a raw decay of 0 past the end keeps the cumsum flat; a given cumsum repeats the
+    // sequence's last value there
+    float gpad = 0.f;
+    if (P.gate_mode == PTOF_GATE_CUMSUM && !ok1)
+      gpad = P.g[gb + static_cast<int64_t>(len - 1 - c * kC) * P.gs_t];
+    g0 = ok0 ? P.g[i0] : gpad;
+    g1 = ok1 ? P.g[i1] : gpad;
   }
   bool mono = true;  // the chunk-local cumsum never increases
   if (P.gate_mode == PTOF_GATE_RAW) {
@@ -231,7 +272,8 @@ __global__ void __launch_bounds__(256) gdn_coef_kernel(const __grid_constant__ C
   const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
   const float gl = __shfl_sync(0xffffffffu, g1, 31);
   const bool fast = P.allow_fast && __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
-  const float b0 = ld_beta(P.beta, P.beta_dtype, i0), b1 = ld_beta(P.beta, P.beta_dtype, i1);
+  const float b0 = ok0 ? ld_beta(P.beta, P.beta_dtype, i0) : 0.f;
+  const float b1 = ok1 ? ld_beta(P.beta, P.beta_dtype, i1) : 0.f;
   const float e0 = __expf(g0), e1 = __expf(g1);
   const float rf0 = __expf(g0 - gfirst), rf1 = __expf(g1 - gfirst);
   unsigned char* rec = P.out + chunk * coef::BYTES;
@@ -253,7 +295,7 @@ __global__ void __launch_bounds__(256) gdn_coef_kernel(const __grid_constant__ C
 }
 
 // ------------------------------------------------------------------ kernel ----
-template <int DK, int DV, bool F16, typename TO, bool TRACE>
+template <int DK, int DV, bool F16, typename TO, bool TRACE, bool VARLEN>
 __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_constant__ Params P) {
   using L = Layout<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -265,7 +307,35 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x, b = bh / P.H, h = bh % P.H;
-  const int nc = P.nc;
+  // sequence bounds: fixed length, or from cu_seqlens (a sequence longer than the
+  // workspace's maximum is cut at mnc chunks and flagged in the status word). They are
+  // kept in shared memory and read where used, so no warp holds them in registers.
+  __shared__ int s_nc, s_len, s_tok0;
+  int nc0 = P.nc, len0 = P.T, tok00 = b * P.T;
+  if (VARLEN) {
+    const int st = P.cu_seqlens[b], en = P.cu_seqlens[b + 1];
+    tok00 = st;
+    len0 = en > st ? en - st : 0;
+    nc0 = (len0 + kC - 1) / kC;
+    if (nc0 > P.mnc) {
+      nc0 = P.mnc;
+      len0 = nc0 * kC;
+      if (tid == 0 && P.status != nullptr) atomicCAS(P.status, 0, 90);
+    }
+  }
+  if (tid == 0) {
+    s_nc = nc0;
+    s_len = len0;
+    s_tok0 = tok00;
+  }
+  if (nc0 == 0) {  // empty sequence: the final state is the initial one (CTA-uniform exit)
+    if (P.S_final != nullptr) {
+      const int64_t base = static_cast<int64_t>(bh) * DK * DV;
+      for (int i = tid; i < DK * DV; i += kThreads)
+        P.S_final[base + i] = P.S0 != nullptr ? P.S0[base + i] : 0.f;
+    }
+    return;
+  }
   Sync sy{&abort_flag, P.status};
 
   if (tid == 0) {
@@ -286,6 +356,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // fixed length: the kernel parameters themselves (no register held for them)
+  const int nc = VARLEN ? s_nc : P.nc;
+  const int tok0 = VARLEN ? s_tok0 : b * P.T;
   const uint64_t t_start = (TRACE && tid == 0) ? globaltimer_ns() : 0;
 
   // chunk c lives in input stage c % NIN (use index c / NIN) and Aqk buffer c % 3
@@ -303,14 +376,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       prefetch_tmap(&P.mapV);
     }
     const bool bhtd = (P.layout == PTOF_LAYOUT_BHTD);
-    const unsigned char* crec = P.coef + static_cast<int64_t>(bh) * nc * L::MISC_BYTES;
+    const unsigned char* crec = P.coef + static_cast<int64_t>(bh) * P.mnc * L::MISC_BYTES;
+    const int Hg = P.H / P.gqa, hk = h / P.gqa;   // this value head's query/key head
     for (int c = 0; c < nc; ++c) {
       const int s = c % L::NIN;
       if (c >= L::NIN) sy.wait(&bars[B_EMPTY0 + s], in_par(c) ^ 1, 1);
       unsigned char* st = stage(c);
       const int t0 = c * kC;
-      const int y = bhtd ? t0 : h;
-      const int z = bhtd ? bh : b * P.T + t0;
+      // q, k: heads-outer {D, T, B*Hg} or token-major {D, Hg, tokens}
+      const int y = bhtd ? t0 : hk;
+      const int z = bhtd ? b * Hg + hk : static_cast<int>(tok0 + t0);
       if (lane == 0) {
         mbar_arrive_expect_tx(&bars[B_FULL0 + s], 2 * DK * kC * 2 + L::MISC_BYTES);
 #pragma unroll
@@ -475,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     auto issue_v = [&](int cv) {
       const int t0 = cv * kC;
       const bool bhtd = (P.layout == PTOF_LAYOUT_BHTD);
-      const int y = bhtd ? t0 : h, z = bhtd ? bh : b * P.T + t0;
+      const int y = bhtd ? t0 : h, z = bhtd ? bh : static_cast<int>(tok0 + t0);
       mbar_arrive_expect_tx(&bars[B_VFULL], DV * kC * 2);
 #pragma unroll
       for (int vb = 0; vb < L::NVB; ++vb)
@@ -681,7 +756,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     (void)s_sa;
     float* osc = reinterpret_cast<float*>(sm + L::OFF_OSC);
     const int64_t sbase = static_cast<int64_t>(bh) * DK * DV;
-    TO* obase = static_cast<TO*>(P.o) + b * P.os_b + h * P.os_h;
+    TO* obase = static_cast<TO*>(P.o) +
+                (VARLEN ? static_cast<int64_t>(tok0) * P.os_t : b * P.os_b) + h * P.os_h;
 
     // smem variant of the bf16 S^T copy (K-major A operand, rows v, DK columns)
     auto put_sa = [&](int d0, const float (&x)[16]) {
@@ -838,7 +914,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       sy.wait(&bars[B_OFULL0 + (c % 3)], aq_par(c), 34);
       tc_fence_after();
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_OFULL);
-      {
+      if (!VARLEN || c + 1 < nc || s_len == nc * kC) {
         TO* op = obase + static_cast<int64_t>(c * kC) * P.os_t + (v >= 0 ? v : 0);
 #pragma unroll 1
         for (int c0 = 0; c0 < kC; c0 += 16) {
@@ -853,6 +929,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
             }
           }
         }
+      } else {   // the partial last chunk of a variable-length sequence (out of line)
+        store_tail<TO>(t_o, obase + static_cast<int64_t>(c * kC) * P.os_t + (v >= 0 ? v : 0),
+                       osc, P.os_t, s_len - c * kC, v >= 0);
       }
       tc_fence_before();
       named_bar_sync(kScanBar, 128);
@@ -892,20 +971,24 @@ namespace {
 // 3D TMA map over a [.., D]-innermost activation so that one box is 64 tokens x 64
 // features of one (batch, head): heads-outer layout -> dims {D, T, B*H};
 // token-major layout -> dims {D, H, B*T}.
-int make_act_map(CUtensorMap* m, const void* base, int dt, const ptof_gdn_params& p, int D) {
+// 3D TMA map over a [.., D]-innermost activation with `heads` heads so that one box
+// is 64 tokens x 64 features of one head: heads-outer layout -> dims {D, T, B*heads};
+// token-major layout -> dims {D, heads, tokens} with tokens = B*T or the packed total.
+int make_act_map(CUtensorMap* m, const void* base, int dt, const ptof_gdn_params& p, int D,
+                 int heads, int64_t tokens) {
   const CUtensorMapDataType t =
       dt == PTOF_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   uint64_t dims[3], strides[2];
   uint32_t box[3];
   if (p.layout == PTOF_LAYOUT_BHTD) {
-    dims[0] = D; dims[1] = p.T; dims[2] = static_cast<uint64_t>(p.B) * p.H;
+    dims[0] = D; dims[1] = p.T; dims[2] = static_cast<uint64_t>(p.B) * heads;
     strides[0] = static_cast<uint64_t>(D) * 2;
     strides[1] = static_cast<uint64_t>(p.T) * D * 2;
     box[0] = 64; box[1] = 64; box[2] = 1;
   } else {
-    dims[0] = D; dims[1] = p.H; dims[2] = static_cast<uint64_t>(p.B) * p.T;
+    dims[0] = D; dims[1] = heads; dims[2] = static_cast<uint64_t>(tokens);
     strides[0] = static_cast<uint64_t>(D) * 2;
-    strides[1] = static_cast<uint64_t>(p.H) * D * 2;
+    strides[1] = static_cast<uint64_t>(heads) * D * 2;
     box[0] = 64; box[1] = 1; box[2] = 64;
   }
   return make_tmap_3d(m, base, t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -913,13 +996,19 @@ int make_act_map(CUtensorMap* m, const void* base, int dt, const ptof_gdn_params
 
 template <int DK, int DV, bool F16, typename TO>
 int launch_t(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
-             const float* g, const float* S0, void* o, float* S_final, cudaStream_t stream) {
+             const float* g, const float* S0, void* o, float* S_final, const int* cu_seqlens,
+             cudaStream_t stream) {
   using L = tcfwd::Layout<DK, DV>;
   const ptof_gdn_params& p = w->p;
+  // variable-length / grouped-query workspaces: ex[0] = 1, ex[1] = q/k heads,
+  // ex[2] = packed tokens (p.B sequences of at most p.T tokens, token-major)
+  const bool varlen = (w->ex[0] == 1);
+  const int Hg = varlen ? w->ex[1] : p.H;
+  const int64_t tokens = varlen ? w->ex[2] : static_cast<int64_t>(p.B) * p.T;
   tcfwd::Params P;
-  int rc = make_act_map(&P.mapK, k, p.in_dtype, p, DK);
-  if (!rc) rc = make_act_map(&P.mapQ, q, p.in_dtype, p, DK);
-  if (!rc) rc = make_act_map(&P.mapV, v, p.in_dtype, p, DV);
+  int rc = make_act_map(&P.mapK, k, p.in_dtype, p, DK, Hg, tokens);
+  if (!rc) rc = make_act_map(&P.mapQ, q, p.in_dtype, p, DK, Hg, tokens);
+  if (!rc) rc = make_act_map(&P.mapV, v, p.in_dtype, p, DV, p.H, tokens);
   if (rc) return rc;
   // per-chunk coefficient records, then the fused forward (same stream)
   if (!w->d_scratch || w->scratch_bytes < gdn_fwd_tc_scratch_bytes(p))
@@ -929,12 +1018,14 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
     C.g = (p.gate_mode == PTOF_GATE_NONE) ? nullptr : g;
     C.beta = beta;
     C.out = static_cast<unsigned char*>(w->d_scratch);
-    C.B = p.B; C.H = p.H; C.nc = p.T / kChunk;
+    C.B = p.B; C.H = p.H; C.nc = (p.T + kChunk - 1) / kChunk;
     C.gate_mode = p.gate_mode;
     C.beta_dtype = p.beta_dtype;
     C.allow_fast = F16 ? 0 : 1;
     const Strides3 sg = make_strides3(p.layout, p.H, p.T);
     C.gs_b = sg.b; C.gs_h = sg.h; C.gs_t = sg.t;
+    C.cu_seqlens = varlen ? cu_seqlens : nullptr;
+    C.T = p.T;
     const int64_t chunks = static_cast<int64_t>(p.B) * p.H * C.nc;
     tcfwd::gdn_coef_kernel<<<static_cast<unsigned>((chunks + 7) / 8), 256, 0, stream>>>(C);
   }
@@ -949,9 +1040,13 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.layout = p.layout;
   const Strides4 so = make_strides4(p.layout, p.H, p.T, DV);
   P.os_b = so.b; P.os_h = so.h; P.os_t = so.t;
+  P.cu_seqlens = varlen ? cu_seqlens : nullptr;
+  P.mnc = (p.T + kChunk - 1) / kChunk;
+  P.gqa = p.H / Hg;
   P.scale = p.scale;
-  auto kern = P.trace ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, true>
-                      : tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false>;
+  auto kern = varlen    ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false, true>
+              : P.trace ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, true, false>
+                        : tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false, false>;
   cudaError_t e = set_smem_once(kern, L::BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_tc smem attribute");
   kern<<<p.B * p.H, tcfwd::kThreads, L::BYTES, stream>>>(P);
@@ -961,25 +1056,27 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
 
 template <int DK, int DV, bool F16>
 int launch_o(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
-             const float* g, const float* S0, void* o, float* S_final, cudaStream_t st) {
+             const float* g, const float* S0, void* o, float* S_final, const int* cu,
+             cudaStream_t st) {
   switch (w->p.out_dtype) {
-    case PTOF_F32: return launch_t<DK, DV, F16, float>(w, q, k, v, beta, g, S0, o, S_final, st);
-    case PTOF_F16: return launch_t<DK, DV, F16, __half>(w, q, k, v, beta, g, S0, o, S_final, st);
-    default: return launch_t<DK, DV, F16, __nv_bfloat16>(w, q, k, v, beta, g, S0, o, S_final, st);
+    case PTOF_F32: return launch_t<DK, DV, F16, float>(w, q, k, v, beta, g, S0, o, S_final, cu, st);
+    case PTOF_F16: return launch_t<DK, DV, F16, __half>(w, q, k, v, beta, g, S0, o, S_final, cu, st);
+    default: return launch_t<DK, DV, F16, __nv_bfloat16>(w, q, k, v, beta, g, S0, o, S_final, cu, st);
   }
 }
 
 template <int DK, int DV>
 int launch_d(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
-             const float* g, const float* S0, void* o, float* S_final, cudaStream_t st) {
-  if (w->p.in_dtype == PTOF_F16) return launch_o<DK, DV, true>(w, q, k, v, beta, g, S0, o, S_final, st);
-  return launch_o<DK, DV, false>(w, q, k, v, beta, g, S0, o, S_final, st);
+             const float* g, const float* S0, void* o, float* S_final, const int* cu,
+             cudaStream_t st) {
+  if (w->p.in_dtype == PTOF_F16) return launch_o<DK, DV, true>(w, q, k, v, beta, g, S0, o, S_final, cu, st);
+  return launch_o<DK, DV, false>(w, q, k, v, beta, g, S0, o, S_final, cu, st);
 }
 
 }  // namespace
 
 size_t gdn_fwd_tc_scratch_bytes(const ptof_gdn_params& p) {
-  return static_cast<size_t>(p.B) * p.H * (p.T / kChunk) * tcfwd::coef::BYTES;
+  return static_cast<size_t>(p.B) * p.H * ((p.T + kChunk - 1) / kChunk) * tcfwd::coef::BYTES;
 }
 
 bool gdn_fwd_tc_supports(const ptof_gdn_params& p) {
@@ -989,11 +1086,11 @@ bool gdn_fwd_tc_supports(const ptof_gdn_params& p) {
 }
 
 int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
-                      const float* g, const float* S0, void* o, float* S_final,
+                      const float* g, const float* S0, void* o, float* S_final, const int* cu,
                       cudaStream_t stream) {
   const ptof_gdn_params& p = w->p;
-  if (p.Dk == 128) return launch_d<128, 128>(w, q, k, v, beta, g, S0, o, S_final, stream);
-  return launch_d<64, 64>(w, q, k, v, beta, g, S0, o, S_final, stream);
+  if (p.Dk == 128) return launch_d<128, 128>(w, q, k, v, beta, g, S0, o, S_final, cu, stream);
+  return launch_d<64, 64>(w, q, k, v, beta, g, S0, o, S_final, cu, stream);
 }
 
 // ----------------------------------------------- allocation-free entry point ----
@@ -1063,5 +1160,6 @@ extern "C" int ptof_gdn_fwd_exec_noalloc(const ptof_gdn_params* p, const void* q
   w.d_status = nullptr;
   w.d_scratch = base;
   w.scratch_bytes = static_cast<size_t>(kNoAllocMaxChunks) * tcfwd::coef::BYTES;
-  return launch_gdn_fwd_tc(&w, q, k, v, beta, g, S0, o, S_final, static_cast<cudaStream_t>(stream));
+  return launch_gdn_fwd_tc(&w, q, k, v, beta, g, S0, o, S_final, nullptr,
+                           static_cast<cudaStream_t>(stream));
 }

@@ -134,3 +134,74 @@ def chunk_gdn_forward(q, k, v, beta, g, *, scale: Optional[float] = None,
                             device=q.device)
         _RUNNERS[key] = r
     return r(q, k, v, beta, g, initial_state, output_final_state=output_final_state)
+
+
+class GDNChunkForwardVarlen:
+    """Persistent runner of the variable-length, grouped-query GDN forward.
+
+    Sequences are packed token-major: q, k [T_total, Hg, Dk]; v, o [T_total, H, Dv];
+    beta, g [T_total, H]; cu_seqlens int32 [N+1] on the device (every length at most
+    ``max_len``). Value head h reads query/key head h // (H // Hg). The workspace is
+    sized for N sequences of up to ``max_len`` tokens; ``T_total`` is fixed per runner.
+    """
+
+    def __init__(self, N: int, H: int, Hg: int, T_total: int, max_len: int, Dk: int,
+                 Dv: int, *, in_dtype=torch.bfloat16, beta_dtype=None, out_dtype=None,
+                 gate: str = "raw", scale: Optional[float] = None, device=None) -> None:
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        beta_dtype = beta_dtype or in_dtype
+        out_dtype = out_dtype or in_dtype
+        self.dims = (N, H, Hg, T_total, max_len, Dk, Dv)
+        self.in_dtype, self.beta_dtype, self.out_dtype, self.gate = (
+            in_dtype, beta_dtype, out_dtype, gate)
+        self.scale = Dk ** -0.5 if scale is None else float(scale)
+        p = nv.GdnVarlenParams(N, H, Hg, T_total, max_len, Dk, Dv, nv.dtype_code(in_dtype),
+                               nv.dtype_code(beta_dtype), nv.dtype_code(out_dtype),
+                               _GATES[gate], self.scale)
+        with torch.cuda.device(self.device):
+            self._ws = nv.lib().ptof_gdn_fwd_varlen_setup(ctypes.byref(p))
+        if not self._ws:
+            raise nv.NativeError(nv.EINVAL, nv.last_error())
+
+    def __call__(self, q, k, v, beta, g, cu_seqlens, initial_state=None, *, o=None,
+                 final_state=None) -> Tuple[torch.Tensor, torch.Tensor]:
+        N, H, Hg, T_total, _, Dk, Dv = self.dims
+        for name, t, shape, dt in (("q", q, (T_total, Hg, Dk), self.in_dtype),
+                                   ("k", k, (T_total, Hg, Dk), self.in_dtype),
+                                   ("v", v, (T_total, H, Dv), self.in_dtype),
+                                   ("beta", beta, (T_total, H), self.beta_dtype),
+                                   ("cu_seqlens", cu_seqlens, (N + 1,), torch.int32)):
+            if tuple(t.shape) != shape or t.dtype != dt or not t.is_contiguous() \
+                    or t.device != self.device:
+                raise ValueError(f"{name}: expected contiguous {dt} {shape} on {self.device}, "
+                                 f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+        if self.gate != "none":
+            if g is None or tuple(g.shape) != (T_total, H) or g.dtype != torch.float32:
+                raise ValueError("g: expected float32 [T_total, H]")
+        else:
+            g = None
+        if o is None:
+            o = torch.empty(T_total, H, Dv, device=self.device, dtype=self.out_dtype)
+        if final_state is None:
+            final_state = torch.empty(N, H, Dk, Dv, device=self.device, dtype=torch.float32)
+        rc = nv.lib().ptof_gdn_fwd_varlen_exec(
+            self._ws, q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(), nv.ptr(g),
+            cu_seqlens.data_ptr(), nv.ptr(initial_state), o.data_ptr(), final_state.data_ptr(),
+            nv.stream_handle(self.device))
+        nv.check(rc)
+        return o, final_state
+
+    def check_status(self) -> None:
+        nv.check(nv.lib().ptof_check_status(self._ws, nv.stream_handle(self.device)))
+
+    def close(self) -> None:
+        if getattr(self, "_ws", None):
+            nv.lib().ptof_gdn_fwd_teardown(self._ws)
+            self._ws = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -42,12 +42,23 @@ class GdnParams(ctypes.Structure):
                 ("layout", ctypes.c_int32), ("scale", ctypes.c_float)]
 
 
+class GdnVarlenParams(ctypes.Structure):
+    _fields_ = [("N", ctypes.c_int32), ("H", ctypes.c_int32), ("Hg", ctypes.c_int32),
+                ("T_total", ctypes.c_int32), ("max_len", ctypes.c_int32),
+                ("Dk", ctypes.c_int32), ("Dv", ctypes.c_int32),
+                ("in_dtype", ctypes.c_int32), ("beta_dtype", ctypes.c_int32),
+                ("out_dtype", ctypes.c_int32), ("gate_mode", ctypes.c_int32),
+                ("scale", ctypes.c_float)]
+
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int
 _SIGNATURES = {
     "ptof_gdn_fwd_setup": (_vp, [ctypes.POINTER(GdnParams)]),
     "ptof_gdn_fwd_exec": (_i32, [_vp] * 10),
     "ptof_gdn_fwd_teardown": (None, [_vp]),
+    "ptof_gdn_fwd_varlen_setup": (_vp, [ctypes.POINTER(GdnVarlenParams)]),
+    "ptof_gdn_fwd_varlen_exec": (_i32, [_vp] * 11),
     "ptof_gdn_fwd_exec_noalloc": (_i32, [ctypes.POINTER(GdnParams)] + [_vp] * 9),
     "ptof_check_status": (_i32, [_vp, _vp]),
     "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),

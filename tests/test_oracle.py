@@ -101,3 +101,25 @@ def test_qkv_flash_matches_gdn_intra_term():
                                           * np.exp(np.minimum(gs[0, 0, 0][:, None] - gs[0, 0, 0][None, :], 0))),
                     v[0, 0])
     assert orc.rel_l2(intra[0, 0, 0], ref) < 1e-12
+
+
+def test_varlen_oracle_reduces_to_fixed_length():
+    """gdn_forward_varlen on equal-length sequences with Hg = H equals gdn_forward, and
+    padding a sequence to whole chunks leaves its outputs unchanged."""
+    rng = np.random.default_rng(5)
+    N, H, T, D = 2, 2, 128, 16
+    q = rng.standard_normal((N, H, T, D)); k = rng.standard_normal((N, H, T, D))
+    v = rng.standard_normal((N, H, T, D))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((N, H, T))))
+    g = -np.log1p(np.exp(-(rng.standard_normal((N, H, T)) + 2)))
+    o, S = orc.gdn_forward(q, k, v, beta, g, 0.25)
+    pk = lambda x: x.transpose(0, 2, 1, *range(3, x.ndim)).reshape(N * T, H, *x.shape[3:])
+    ov, Sv = orc.gdn_forward_varlen(pk(q), pk(k), pk(v), pk(beta), pk(g), [0, T, 2 * T], 0.25)
+    assert np.allclose(ov, pk(o)) and np.allclose(Sv, S)
+    # a 100-token prefix of the first sequence: padded inside the oracle
+    ov2, _ = orc.gdn_forward_varlen(pk(q)[:100], pk(k)[:100], pk(v)[:100], pk(beta)[:100],
+                                    pk(g)[:100], [0, 100], 0.25)
+    o_pref, _ = orc.gdn_forward(q[:1, :, :128], k[:1, :, :128], v[:1, :, :128],
+                                np.where(np.arange(128) < 100, beta[:1], 0.0),
+                                np.where(np.arange(128) < 100, g[:1], 0.0), 0.25)
+    assert np.allclose(ov2, o_pref[0].transpose(1, 0, 2)[:100])
