@@ -166,6 +166,14 @@ PTOF_API int ptof_kkt_inv_exec(void* ws, const void* k, const void* beta, const 
                                float* T_out, int B, int H, int T, int D, int in_dtype,
                                int beta_dtype, int gate_mode, int layout, void* stream);
 
+/* Per-channel-gate intra-chunk score of the chunked linear-attention family (GLA):
+ * L = tril((q * P) (k * invP)^T, 0) per chunk, q/k/P/invP [M, C, D] (f16/bf16/f32),
+ * L [M, C, C] fp16. Replaces pro_exec / pro_exec_v2 (the qk_prologue[_v2] keys,
+ * src/pto_fuser/fused.py:286-311, 532-553). C <= 128, D <= 256. */
+PTOF_API int ptof_qk_prologue_exec(void* ws, const void* q, const void* k, const void* P,
+                                   const void* invP, void* L, int M, int C, int D, int in_dtype,
+                                   void* stream);
+
 /* (I + A)^-1 for strictly-lower A [M,C,C] (a_dtype), fp32 out [M,C,C]; replaces the
  * opaque tri_inv_rec_unroll kernel (registry.py:96-140). Unlike the reference it takes
  * A lower-triangular directly (no transpose round trip). ws may be NULL. */

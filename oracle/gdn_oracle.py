@@ -264,3 +264,19 @@ def gdn_forward_varlen(q, k, v, beta, g, cu_seqlens, scale, S0=None, C=C_DEFAULT
         o[a:b] = on[0].transpose(1, 0, 2)[:L]
         S_out[n] = Sn[0]
     return o, S_out
+
+
+def linear_attention_recurrent(q, k, v, gates, dtype=np.float64):
+    """Token-recurrent gated linear attention, the definition the chunked linear family
+    (vanilla LA, RetNet, Mamba-2, GLA) computes: S_t = diag(g_t) S_{t-1} + k_t^T v_t,
+    o_t = q_t S_t (examples/attention/_chunked.py:14-17, chunked_linear_reference
+    :194-208). q, k, gates [N, T, d_k] (gates in (0, 1]), v [N, T, d_v] -> o [N, T, d_v]."""
+    q, k, v, g = (_f(x, dtype) for x in (q, k, v, gates))
+    N, T, d_k = q.shape
+    o = np.zeros((N, T, v.shape[-1]), dtype=dtype)
+    for n in range(N):
+        S = np.zeros((d_k, v.shape[-1]), dtype=dtype)
+        for t in range(T):
+            S = g[n, t][:, None] * S + np.outer(k[n, t], v[n, t])
+            o[n, t] = q[n, t] @ S
+    return o

@@ -332,6 +332,16 @@ int ptof_kkt_inv_exec(void* ws, const void* k, const void* beta, const float* g,
                         static_cast<cudaStream_t>(stream));
 }
 
+int ptof_qk_prologue_exec(void* ws, const void* q, const void* k, const void* P,
+                          const void* invP, void* L, int M, int C, int D, int in_dtype,
+                          void* stream) {
+  (void)ws;
+  if (M < 1 || C < 1 || C > 128 || D < 1 || D > 256) return fail(PTOF_EINVAL, "qk_prologue shape");
+  if (!dtype_ok(in_dtype)) return fail(PTOF_EINVAL, "qk_prologue dtype");
+  if (!q || !k || !P || !invP || !L) return fail(PTOF_EINVAL, "qk_prologue: NULL pointer");
+  return launch_qk_prologue(in_dtype, q, k, P, invP, L, M, C, D, static_cast<cudaStream_t>(stream));
+}
+
 int ptof_tri_inv_exec(void* ws, const void* A, int a_dtype, float* T, int M, int C, void* stream) {
   (void)ws;
   if (M < 1 || C < 1 || C > 128) return fail(PTOF_EINVAL, "tri_inv shape M=%d C=%d", M, C);

@@ -14,6 +14,9 @@
 //              (src/pto_fuser/kernels/scan_fused.h:13-17, 217-261)
 //   qkv_flash: o = tril(q k^T * exp(min(g_i - g_j, 0))) v                per chunk
 //              (src/pto_fuser/kernels/qkv_fused.h:5-18)
+//   qk_prologue: L = tril((q * P) (k * invP)^T, 0)                         per chunk
+//              (per-channel-gate intra score of the chunked linear family,
+//               src/pto_fuser/fused.py:286-311, 532-553)
 #include <cuda_runtime.h>
 
 #include "capi_internal.h"
@@ -62,6 +65,35 @@ __global__ void __launch_bounds__(kThreads) gated_qk_kernel(const TI* a, const T
       out = acc * expf(fminf(gv[i] - gs[j], 0.f));
     }
     L[static_cast<int64_t>(m) * C * C + idx] = from_f32<TO>(out);
+  }
+}
+
+// --------------------------------------------------------------- qk_prologue ----
+// One CTA per chunk m: the per-channel decay rides on the operands, prescaled while
+// staging into shared memory. q, k, P, invP: [M, C, D]; L: [M, C, C] fp16, causal
+// (j <= i) incl. the diagonal, zeros above.
+template <typename TI>
+__global__ void __launch_bounds__(kThreads) qk_prologue_kernel(const TI* q, const TI* k,
+                                                               const TI* P, const TI* invP,
+                                                               __half* L, int C, int D) {
+  extern __shared__ float sm[];
+  const int m = blockIdx.x;
+  const int ld = D + 1;
+  float* sq = sm;
+  float* sk = sm + C * ld;
+  const int64_t base = static_cast<int64_t>(m) * C * D;
+  for (int idx = threadIdx.x; idx < C * D; idx += kThreads) {
+    const int i = idx / D, d = idx % D;
+    sq[i * ld + d] = ldf(q, base + idx) * ldf(P, base + idx);
+    sk[i * ld + d] = ldf(k, base + idx) * ldf(invP, base + idx);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < C * C; idx += kThreads) {
+    const int i = idx / C, j = idx % C;
+    float acc = 0.f;
+    if (j <= i)
+      for (int d = 0; d < D; ++d) acc = fmaf(sq[i * ld + d], sk[j * ld + d], acc);
+    L[static_cast<int64_t>(m) * C * C + idx] = __float2half_rn(acc);
   }
 }
 
@@ -308,6 +340,27 @@ int launch_qkv_flash(int in_dtype, const void* q, const void* k, const void* v, 
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "qkv_flash launch");
+}
+
+int launch_qk_prologue(int in_dtype, const void* q, const void* k, const void* P,
+                       const void* invP, void* L, int M, int C, int D, cudaStream_t st) {
+  using namespace compat;
+  const size_t smem = 2 * static_cast<size_t>(C) * (D + 1) * sizeof(float);
+  if (smem > 227 * 1024) return fail(PTOF_EUNSUPPORTED, "qk_prologue: C=%d D=%d too large", C, D);
+  cudaError_t e;
+#define PTOF_QKP(TI)                                                                        \
+  {                                                                                         \
+    auto kern = qk_prologue_kernel<TI>;                                                     \
+    e = prep(kern, smem);                                                                   \
+    if (e == cudaSuccess)                                                                   \
+      kern<<<M, kThreads, smem, st>>>(static_cast<const TI*>(q), static_cast<const TI*>(k),  \
+                                      static_cast<const TI*>(P), static_cast<const TI*>(invP), \
+                                      static_cast<__half*>(L), C, D);                       \
+  }
+  if (in_dtype == PTOF_BF16) PTOF_QKP(__nv_bfloat16) else if (in_dtype == PTOF_F16) PTOF_QKP(__half) else PTOF_QKP(float)
+#undef PTOF_QKP
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "qk_prologue launch");
 }
 
 }  // namespace ptof

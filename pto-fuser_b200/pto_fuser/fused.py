@@ -181,6 +181,21 @@ def _qkv_launch(ws, inputs, params) -> List[torch.Tensor]:
     return [o]
 
 
+def _prologue_launch(ws, inputs, params) -> List[torch.Tensor]:
+    """q, k, P, invP [., C, D] over M = nc * H chunks -> L = tril((q*P)(k*invP)^T) [M,C,C]
+    fp16 (the per-channel-gate intra score; reference fused.py:303-311)."""
+    q, k, P, invP = inputs
+    C, D = params.get("C", q.shape[-2]), params.get("D", q.shape[-1])
+    M = params["nc"] * params["H"]
+    rs = lambda t: _c(t, torch.float16).reshape(M, C, D)
+    q, k, P, invP = rs(q), rs(k), rs(P), rs(invP)
+    L = torch.empty(M, C, C, device=q.device, dtype=torch.float16)
+    nv.check(nv.lib().ptof_qk_prologue_exec(ws, q.data_ptr(), k.data_ptr(), P.data_ptr(),
+                                            invP.data_ptr(), L.data_ptr(), M, C, D, nv.F16,
+                                            nv.stream_handle(q.device)))
+    return [L]
+
+
 _GDN_RUNNERS: Dict[tuple, Any] = {}
 
 
@@ -237,6 +252,12 @@ def default_fused_registry() -> FusedKernelRegistry:
                         notes="o = tril(q k^T * exp(min(g_i-g_j,0))) v in one launch")
     for key in ("qkv_flash_native", "qkv_flash_native_v2"):
         reg.register(key, _Recipe(_qkv_launch, qkv))
+    pro = FusedContract(in_slots=["q", "k", "P", "invP"], in_dtypes=[f16, f16, f16, f16],
+                        out_names=["L"], out_dtype=f16,
+                        notes="per-channel-gate intra score tril((q*P)(k*invP)^T, 0); "
+                              "q/k/P/invP [M,C,D], L [M,C,C]")
+    for key in ("qk_prologue", "qk_prologue_v2"):
+        reg.register(key, _Recipe(_prologue_launch, pro))
     reg.register("gdn_chunk_fwd", _Recipe(_gdn_launch, FusedContract(
         in_slots=["q", "k", "v", "g_native", "beta_native"],
         in_dtypes=[torch.bfloat16, torch.bfloat16, torch.bfloat16, f32, torch.bfloat16],
