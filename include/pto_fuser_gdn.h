@@ -189,6 +189,14 @@ PTOF_API int ptof_chunk_h_scan_exec(void* ws, const void* w, const void* u, cons
                                     int H, int nc, int C, int D, int Dv, int in_dtype,
                                     int out_dtype, void* stream);
 
+/* The same scan with a per-key-dimension decay (the KDA scan: chunk_h_scan built with
+ * perdim_decay=True, transforms/kda.py:19-70; scan_fused.h:136-180): decay is fp32
+ * [B, H, nc, D] and row d of the state decays by decay[b, h, c, d]. */
+PTOF_API int ptof_chunk_h_scan_perdim_exec(void* ws, const void* w, const void* u, const void* k,
+                                           const float* decay, void* h_out, void* final_state,
+                                           int B, int H, int nc, int C, int D, int Dv,
+                                           int in_dtype, int out_dtype, void* stream);
+
 /* chunk_o score -> output in one launch (replaces qkv_exec / qkv_exec_v2,
  * kernels/qkv_fused_lib.cpp:296-344): o = tril(q k^T * exp(min(g_i - g_j, 0))) v.
  * q, k [M,C,D], v [M,C,Dv] in_dtype; g [M,C] fp32; o [M,C,Dv] fp32. */

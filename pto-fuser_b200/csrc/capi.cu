@@ -361,7 +361,21 @@ int ptof_chunk_h_scan_exec(void* ws, const void* w, const void* u, const void* k
   if (!w || !u || !k || !decay || !h_out || !final_state)
     return fail(PTOF_EINVAL, "chunk_h_scan: NULL pointer");
   return launch_scan(in_dtype, out_dtype, w, u, k, decay, h_out, final_state, B, H, nc, C, D,
-                     Dv, static_cast<cudaStream_t>(stream));
+                     Dv, 0, static_cast<cudaStream_t>(stream));
+}
+
+int ptof_chunk_h_scan_perdim_exec(void* ws, const void* w, const void* u, const void* k,
+                                  const float* decay, void* h_out, void* final_state, int B,
+                                  int H, int nc, int C, int D, int Dv, int in_dtype,
+                                  int out_dtype, void* stream) {
+  (void)ws;
+  if (B < 1 || H < 1 || nc < 1 || C < 1 || C > 128 || D < 1 || D > 128 || Dv < 1)
+    return fail(PTOF_EINVAL, "chunk_h_scan shape");
+  if (!dt16(in_dtype) || !dt16(out_dtype)) return fail(PTOF_EINVAL, "chunk_h_scan dtype");
+  if (!w || !u || !k || !decay || !h_out || !final_state)
+    return fail(PTOF_EINVAL, "chunk_h_scan: NULL pointer");
+  return launch_scan(in_dtype, out_dtype, w, u, k, decay, h_out, final_state, B, H, nc, C, D,
+                     Dv, 1, static_cast<cudaStream_t>(stream));
 }
 
 int ptof_qkv_flash_exec(void* ws, const void* q, const void* k, const void* v, const float* g,

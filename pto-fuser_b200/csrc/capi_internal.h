@@ -69,7 +69,7 @@ int launch_qk_prologue(int in_dtype, const void* q, const void* k, const void* P
 int launch_tri_inv(int a_dtype, const void* A, float* T, int M, int C, cudaStream_t st);
 int launch_scan(int in_dtype, int out_dtype, const void* w, const void* u, const void* k,
                 const float* decay, void* h_out, void* final_state, int B, int H, int nc, int C,
-                int D, int Dv, cudaStream_t st);
+                int D, int Dv, int perdim, cudaStream_t st);
 int launch_qkv_flash(int in_dtype, const void* q, const void* k, const void* v, const float* g,
                      float* o, int M, int C, int D, int Dv, cudaStream_t st);
 

@@ -128,12 +128,14 @@ __global__ void __launch_bounds__(128) tri_inv_kernel(const TA* A, float* T, int
 
 // --------------------------------------------------------------------- scan ----
 // One CTA per (b, h, value block of 32). w, k: [B, nc, C, H, D]; u: [B, nc, C, H, Dv];
-// decay: [B, H, nc] fp32; h_out: [B, nc, H, D, Dv]; final: [B, H, D, Dv] (TO).
+// decay: [B, H, nc] fp32, or per key dimension [B, H, nc, D] (perdim: row d of S decays
+// by decay[.., d], the KDA scan, scan_fused.h:136-180); h_out: [B, nc, H, D, Dv];
+// final: [B, H, D, Dv] (TO).
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(kThreads) scan_kernel(const TI* w, const TI* u, const TI* k,
                                                         const float* decay, TO* h_out,
                                                         TO* final_state, int B, int H, int nc,
-                                                        int C, int D, int Dv) {
+                                                        int C, int D, int Dv, int perdim) {
   constexpr int BV = 32;
   extern __shared__ float sm[];
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
@@ -174,9 +176,10 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const TI* w, const TI* u
       su[idx] -= acc;
     }
     __syncthreads();
-    const float dec = decay[(static_cast<int64_t>(b) * H + h) * nc + c];
+    const int64_t dbase = (static_cast<int64_t>(b) * H + h) * nc + c;
     for (int idx = threadIdx.x; idx < D * BV; idx += kThreads) {
       const int d = idx / BV, jv = idx % BV;
+      const float dec = perdim ? decay[dbase * D + d] : decay[dbase];
       float acc = 0.f;
       for (int i = 0; i < C; ++i) acc = fmaf(sk[i * ld + d], su[i * BV + jv], acc);
       S[idx] = dec * S[idx] + acc;
@@ -286,7 +289,7 @@ int launch_tri_inv(int a_dtype, const void* A, float* T, int M, int C, cudaStrea
 
 int launch_scan(int in_dtype, int out_dtype, const void* w, const void* u, const void* k,
                 const float* decay, void* h_out, void* final_state, int B, int H, int nc, int C,
-                int D, int Dv, cudaStream_t st) {
+                int D, int Dv, int perdim, cudaStream_t st) {
   using namespace compat;
   const size_t smem = (static_cast<size_t>(D) * 32 + 2 * static_cast<size_t>(C) * (D + 1) +
                        static_cast<size_t>(C) * 32) * sizeof(float);
@@ -300,7 +303,7 @@ int launch_scan(int in_dtype, int out_dtype, const void* w, const void* u, const
     if (e == cudaSuccess)                                                                   \
       kern<<<grid, kThreads, smem, st>>>(static_cast<const TI*>(w), static_cast<const TI*>(u), \
                                          static_cast<const TI*>(k), decay, static_cast<TO*>(h_out), \
-                                         static_cast<TO*>(final_state), B, H, nc, C, D, Dv);  \
+                                         static_cast<TO*>(final_state), B, H, nc, C, D, Dv, perdim); \
   }
   if (in_dtype == PTOF_F16) {
     if (out_dtype == PTOF_F32) PTOF_SCAN(__half, float) else PTOF_SCAN(__half, __half)

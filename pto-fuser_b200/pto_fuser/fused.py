@@ -108,15 +108,18 @@ def _c(t: torch.Tensor, dtype=None) -> torch.Tensor:
 
 
 def _scan_launch(ws, inputs, params) -> List[torch.Tensor]:
-    """w, u, k [B,nc,C,H,D] (cast fp16 per contract), decay [B,H,nc] fp32."""
+    """w, u, k [B,nc,C,H,D] (cast fp16 per contract), decay [B,H,nc] fp32, or
+    [B,H,nc,D] with params perdim_decay (the KDA scan)."""
     w, u, k, decay = inputs
     B, H, nc = params["B"], params["H"], params["nc"]
     w, u, k = _c(w, torch.float16), _c(u, torch.float16), _c(k, torch.float16)
     C, D, Dv = w.shape[2], w.shape[4], u.shape[4]
-    decay = _c(decay.reshape(B, H, nc), torch.float32)
+    perdim = bool(params.get("perdim_decay", False))
+    decay = _c(decay.reshape((B, H, nc, D) if perdim else (B, H, nc)), torch.float32)
     h_out = torch.empty(B, nc, H, D, Dv, device=w.device, dtype=torch.float16)
     final = torch.empty(B, H, D, Dv, device=w.device, dtype=torch.float16)
-    nv.check(nv.lib().ptof_chunk_h_scan_exec(
+    fn = nv.lib().ptof_chunk_h_scan_perdim_exec if perdim else nv.lib().ptof_chunk_h_scan_exec
+    nv.check(fn(
         ws, w.data_ptr(), u.data_ptr(), k.data_ptr(), decay.data_ptr(), h_out.data_ptr(),
         final.data_ptr(), B, H, nc, C, D, Dv, nv.F16, nv.F16, nv.stream_handle(w.device)))
     return [h_out, final]
@@ -228,7 +231,8 @@ def default_fused_registry() -> FusedKernelRegistry:
     reg.register("chunk_h_scan", _Recipe(_scan_launch, FusedContract(
         in_slots=["w", "u", "k", "decay"], in_dtypes=[f16, f16, f16, f32],
         out_names=["h_out", "final"], out_dtype=f16,
-        notes="resident-state chunk recurrence; w/u/k [B,nc,C,H,D], decay [B,H,nc]")))
+        notes="resident-state chunk recurrence; w/u/k [B,nc,C,H,D], decay [B,H,nc] "
+              "(or [B,H,nc,D] with perdim_decay)")))
     mega = lambda causal: (lambda ws, ins, p: _mega_launch(ws, ins, p, p.get("causal", causal)))
     native = lambda causal: (lambda ws, ins, p: _native_launch(ws, ins, p, p.get("causal", causal)))
     reg.register("kkt_gated", _Recipe(mega(False), FusedContract(

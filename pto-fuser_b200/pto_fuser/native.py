@@ -67,6 +67,7 @@ _SIGNATURES = {
     "ptof_ws_teardown": (None, [_vp]),
     "ptof_gated_qk_exec": (_i32, [_vp] * 6 + [_i32] * 6 + [_vp]),
     "ptof_kkt_inv_exec": (_i32, [_vp] * 5 + [_i32] * 8 + [_vp]),
+    "ptof_chunk_h_scan_perdim_exec": (_i32, [_vp] * 7 + [_i32] * 8 + [_vp]),
     "ptof_qk_prologue_exec": (_i32, [_vp] * 6 + [_i32] * 4 + [_vp]),
     "ptof_tri_inv_exec": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _vp]),
     "ptof_chunk_h_scan_exec": (_i32, [_vp] * 7 + [_i32] * 8 + [_vp]),

@@ -8,6 +8,8 @@ checkout given by --ref) on small seeded inputs and stores inputs + outputs as
   deltanet_d64.npz           src/pto_fuser/forwards/deltanet.py:114-143 deltanet_reference
   kkt_c128.npz               src/pto_fuser/forwards/fused_stages.py:140-156 kkt_reference
   scan_c128.npz              src/pto_fuser/forwards/fused_stages.py:46-62 scan_reference
+  kda_d32.npz                examples/attention/_kda_full.py:38-77 kda_reference
+  linear_gla.npz             examples/attention/_chunked.py:194-208 chunked_linear_reference
 
 Inputs follow the build's benchmark distributions (q,k L2-normalised N(0,1), v N(0,1),
 beta = sigmoid(N(0,1)), g = logsigmoid(N(2,1))) except where the reference helper fixes
@@ -83,6 +85,23 @@ def main() -> None:
                         w=sin["w"].float().numpy(), u=sin["u"].float().numpy(),
                         k=sin["k"].float().numpy(), decay=sin["decay"].numpy(),
                         h_out=sref["h_out"].numpy(), final=sref["final"].numpy())
+    from attention._kda_full import kda_reference, make_kda_inputs  # noqa: E402
+    torch.manual_seed(16)
+    kin = make_kda_inputs(1, 2, 3, 16, 32, device="cpu", dtype=torch.float32)
+    ko = kda_reference(kin["q"], kin["k"], kin["v"], kin["beta"], kin["g_in"], 32 ** -0.5)
+    np.savez_compressed(os.path.join(HERE, "kda_d32.npz"),
+                        **{n: t.numpy() for n, t in kin.items()}, o=ko.numpy())
+
+    from attention._chunked import chunked_linear_reference  # noqa: E402
+    g = torch.Generator().manual_seed(17)
+    N, nc, C, dk, dv = 2, 3, 16, 16, 8
+    q = torch.nn.functional.normalize(torch.randn(N, nc, C, dk, generator=g), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(N, nc, C, dk, generator=g), dim=-1)
+    v = torch.randn(N, nc, C, dv, generator=g)
+    gates = 0.95 + 0.05 * torch.rand(N, nc, C, dk, generator=g)
+    lo = chunked_linear_reference(q, k, v, gates, 1, N, nc, C)["o"]
+    np.savez_compressed(os.path.join(HERE, "linear_gla.npz"), q=q.numpy(), k=k.numpy(),
+                        v=v.numpy(), gates=gates.numpy(), o=lo.numpy())
     print("golden vectors written to", HERE)
 
 

@@ -123,3 +123,19 @@ def test_varlen_oracle_reduces_to_fixed_length():
                                 np.where(np.arange(128) < 100, beta[:1], 0.0),
                                 np.where(np.arange(128) < 100, g[:1], 0.0), 0.25)
     assert np.allclose(ov2, o_pref[0].transpose(1, 0, 2)[:100])
+
+
+def test_kda_oracle_matches_reference_golden():
+    """kda_forward against the reference's own kda_reference (_kda_full.py:38-77)."""
+    z = np.load(os.path.join(GOLD, "kda_d32.npz"))
+    o = orc.kda_forward(z["q"], z["k"], z["v"], z["beta"], z["g_in"], 32 ** -0.5)
+    assert orc.rel_l2(o, z["o"]) < 1e-5
+
+
+def test_linear_attention_oracle_matches_reference_golden():
+    """linear_attention_recurrent against the reference's chunked_linear_reference."""
+    z = np.load(os.path.join(GOLD, "linear_gla.npz"))
+    N, nc, C = z["q"].shape[:3]
+    f = lambda x: x.reshape(N, nc * C, -1)
+    o = orc.linear_attention_recurrent(f(z["q"]), f(z["k"]), f(z["v"]), f(z["gates"]))
+    assert orc.rel_l2(o, f(z["o"])) < 1e-5
