@@ -11,8 +11,8 @@ L2-normalised N(0,1); v N(0,1); beta = sigmoid(N(0,1)); g = logsigmoid(N(2,1))).
 
 Prints one JSON line (rank 0). `value` is whole-job tokens/s with inputs resident
 in HBM (device-timed with CUDA events, max over ranks); `e2e` is the same metric
-through the public API with pinned host buffers and the host<->device copies inside
-the timed region; `roofline` is the fused kernel's achieved HBM bandwidth on its
+through the public API with pinned host buffers and every step's host<->device copies
+inside the timed region (uploads, kernels and downloads pipelined over three streams); `roofline` is the fused kernel's achieved HBM bandwidth on its
 algorithmic bytes against the measured copy peak; `cpu_baseline` is the CPU oracle
 timed on this host on a bounded sample. `--impl reference` times the CPU
 restatement of the reference forward (the reference itself is Ascend/CANN code and
@@ -231,29 +231,53 @@ def run_ours(args):
     value = tokens / (ms_max / 1e3)
 
     # ---- end to end through the public API: pinned host in, host out ----
+    # Every step uploads its own inputs from pinned host memory and downloads its own
+    # result (o and the final state). The two PCIe directions and the kernels are
+    # independent engines, so steps are pipelined over three streams with
+    # double-buffered device operands: upload(i) || forward(i-1) || download(i-2).
     names = ("q", "k", "v", "beta", "g")
     host = {n: inp[n].cpu().pin_memory() for n in names}
-    dev_in = {n: torch.empty_like(inp[n]) for n in names}
-    o_h = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
-    S_h = torch.empty(S.shape, dtype=S.dtype, pin_memory=True)
+    dev_in = [{n: torch.empty_like(inp[n]) for n in names} for _ in range(2)]
+    dev_o = [o, torch.empty_like(o)]
+    dev_S = [S, torch.empty_like(S)]
+    o_h = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for _ in range(2)]
+    S_h = [torch.empty(S.shape, dtype=S.dtype, pin_memory=True) for _ in range(2)]
     h2d = sum(host[n].numel() * host[n].element_size() for n in names)
-    d2h = o_h.numel() * o_h.element_size() + S_h.numel() * S_h.element_size()
-    e2e_steps = max(1, min(args.steps, 5))
+    d2h = o_h[0].numel() * o_h[0].element_size() + S_h[0].numel() * S_h[0].element_size()
+    e2e_steps = max(2, min(args.steps, 6))
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
-    def e2e_step():
-        for n in names:
-            dev_in[n].copy_(host[n], non_blocking=True)
-        runner(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["beta"], dev_in["g"], o=o,
-               final_state=S)
-        o_h.copy_(o, non_blocking=True)
-        S_h.copy_(S, non_blocking=True)
+    def e2e_run(n_steps):
+        ev_in = [torch.cuda.Event() for _ in range(n_steps)]
+        ev_fw = [torch.cuda.Event() for _ in range(n_steps)]
+        ev_out = [torch.cuda.Event() for _ in range(n_steps)]
+        for i in range(n_steps):
+            j = i & 1
+            with torch.cuda.stream(up):            # buffer j last read by forward(i-2)
+                if i >= 2:
+                    up.wait_event(ev_fw[i - 2])
+                for n in names:
+                    dev_in[j][n].copy_(host[n], non_blocking=True)
+                ev_in[i].record(up)
+            stream.wait_event(ev_in[i])            # forward(i) on the compute stream
+            if i >= 2:
+                stream.wait_event(ev_out[i - 2])   # its outputs' last download is done
+            d = dev_in[j]
+            runner(d["q"], d["k"], d["v"], d["beta"], d["g"], o=dev_o[j], final_state=dev_S[j])
+            ev_fw[i].record(stream)
+            with torch.cuda.stream(down):
+                down.wait_event(ev_fw[i])
+                o_h[j].copy_(dev_o[j], non_blocking=True)
+                S_h[j].copy_(dev_S[j], non_blocking=True)
+                ev_out[i].record(down)
+        stream.wait_event(ev_out[n_steps - 1])
 
-    e2e_step()
+    e2e_run(2)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    up.wait_event(e0)
+    e2e_run(e2e_steps)
     e1.record(stream)
     barrier()
     t2 = torch.tensor([e0.elapsed_time(e1)], device=dev)
