@@ -420,6 +420,99 @@ def run_configs(args):
         131072, 128, torch.bfloat16, mu=3.0, s0_std=0.02)
 
 
+def run_long(args):
+    """Config 4 (one long sequence, few heads) with the token axis split over the
+    ranks: the chunk-segment scan (pto_fuser.segment), strong scaling. Each rank holds
+    its token range of all 64 heads (inputs drawn on its device, S0 identical on every
+    rank); the timed step is the whole segment-parallel forward including the NCCL
+    all-gather of the segment maps. N = 1 with one segment is the serial forward."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = _dist()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    from pto_fuser import GDNChunkForward
+    from pto_fuser.segment import GDNSegmentScan, split_tokens
+    B, H, T, D = 1, 64, 131072, 128
+    P = B * H
+    Tl = split_tokens(T, world)[rank]
+    segs = args.segments if args.segments else 1
+    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
+    nrm = torch.nn.functional.normalize
+    bf = torch.bfloat16
+    q = nrm(torch.randn(P, Tl, D, device=dev, generator=gen), dim=-1).to(bf)
+    k = nrm(torch.randn(P, Tl, D, device=dev, generator=gen), dim=-1).to(bf)
+    v = torch.randn(P, Tl, D, device=dev, generator=gen).to(bf)
+    beta = torch.sigmoid(torch.randn(P, Tl, device=dev, generator=gen)).to(bf)
+    g = torch.nn.functional.logsigmoid(torch.randn(P, Tl, device=dev, generator=gen) + 3.0)
+    S0 = torch.randn(P, D, D, device=dev,
+                     generator=torch.Generator(device=dev).manual_seed(99)) * 0.02
+    o = torch.empty(P, Tl, D, device=dev, dtype=bf)
+    if world == 1 and segs == 1:
+        run = GDNChunkForward(B, H, Tl, D, D, device=dev)
+        S = torch.empty(B, H, D, D, device=dev)
+        step = lambda: run(q[None], k[None], v[None], beta[None], g[None], S0[None],
+                           o=o[None], final_state=S)
+        launches = 2
+        check = [run]
+        how = "serial chunk scan (one CTA per head)"
+    else:
+        run = GDNSegmentScan(P, Tl, D, segments=segs,
+                             group=dist.group.WORLD if world > 1 else None, device=dev)
+        step = lambda: run(q, k, v, beta, g, S0, o=o)
+        launches = 2 + 2 + (2 if world > 1 else 0) + (1 if rank > 0 else 0) + 1 + 1
+        check = [run]
+        how = f"chunk-segment scan: {world} rank(s) x {segs} sub-segments, NCCL all-gather"
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    for r in check:
+        r.check_status()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    for r in check:
+        r.check_status()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    hbm = _peaks()[0]
+    algo = B * H * T * 1030 + B * H * D * D * 4 * 2
+    if rank == 0:
+        print(json.dumps({
+            "metric": "GDN chunk-forward tokens/s, long context (config 4), whole box",
+            "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg4: GDN forward B1 H64 T131072 D128 bf16, S0 ~ N(0,0.02^2), "
+                                   "g = logsigmoid(N(3,1))", "parallelism": how,
+                       "tokens_per_rank": Tl, "l2": "8.6 GB of operands vs 126 MB L2"},
+            "roofline": {"bound": "hbm", "algo_bytes": algo,
+                         "achieved": algo / (ms / 1e3) / 1e9, "peak": hbm * world,
+                         "unit": "GB/s", "frac": algo / (ms / 1e3) / 1e9 / (hbm * world),
+                         "peak_kind": "measured, per GPU x n_gpus"},
+            "gpu_launches": launches * args.steps, "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -432,11 +525,19 @@ def main():
     ap.add_argument("--shape", type=int, nargs=4, metavar=("B", "H", "T", "D"),
                     help="per-GPU problem other than config 2 (small cases for profiling; "
                          "not a bench line of the headline metric)")
+    ap.add_argument("--long-context", action="store_true",
+                    help="config 4 (B1 H64 T131072) with the token axis split over the ranks "
+                         "(chunk-segment scan, strong scaling)")
+    ap.add_argument("--segments", type=int, default=0,
+                    help="sub-segments per rank for --long-context (default 1; on one GPU 1 is "
+                         "the serial forward)")
     args = ap.parse_args()
     if args.shape:
         CFG.update(B=args.shape[0], H=args.shape[1], T=args.shape[2], D=args.shape[3])
     if args.configs:
         run_configs(args)
+    elif args.long_context:
+        run_long(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -216,6 +216,44 @@ PTOF_API int ptof_gdn_fwd_set_trace(void* ws, void* dev_buf, int chunks);
  * `stream`: PTOF_OK, or PTOF_ETIMEOUT when a bounded device wait gave up. */
 PTOF_API int ptof_check_status(void* ws, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Segment-state combine for a chunk-segment scan of one long sequence (no
+ * counterpart in the reference: it runs each head's recurrence serially over the
+ * whole sequence, scan_fused.h:198-262, and its own notes place few-head long
+ * contexts outside its winning regime, docs/DESIGN.md:336-340).
+ * Over a chunk-aligned token segment the state map is affine, S_out = A S_in + B:
+ * A [D,D] is the final state of ptof_gdn_fwd_exec started from S0 = I with v = 0,
+ * B [D,Dv] the final state started from S0 = 0. For every head this applies the
+ * maps of segments j = 0..nseg-1 in order:
+ *   X_0 = X0 (NULL: zero),  X_{j+1} = A_j X_j + B_j  (Bv NULL: no offset)
+ * and writes the entry state X_j of each segment to Xout (NULL: not written) and
+ * X_nseg to Xfinal (NULL: not written). All fp32; every matrix is row-major with
+ * rows of D (A) or Dv (B, X) floats; the *_stride arguments give, in floats, the
+ * distance between heads and between segments. D in {64, 128}, Dv a multiple of
+ * 32, nseg >= 0. Launches on `stream`, no host synchronisation. Outputs must not
+ * overlap the inputs.
+ */
+PTOF_API int ptof_seg_scan_exec(const float* A, int64_t a_head_stride, int64_t a_seg_stride,
+                                const float* Bv, int64_t b_head_stride, int64_t b_seg_stride,
+                                const float* X0, int64_t x0_head_stride, float* Xout,
+                                int64_t xout_head_stride, int64_t xout_seg_stride,
+                                float* Xfinal, int64_t xfinal_head_stride, int heads, int nseg,
+                                int D, int Dv, void* stream);
+
+/* Output fix-up of the chunk-segment scan (no counterpart in the reference; see
+ * ptof_seg_scan_exec). A segment's output is affine in its entry state X:
+ * o = o^B + o^A X, with o^B the forward's output from a zero state (held in `o` on
+ * entry) and o^A its output from S0 = I with v = 0. For every unit u (one token
+ * segment of one (b, h) pair) and token t < Tseg:
+ *   o[u][t][:] += oa[u][t][:] @ X[u]      (fp32 accumulate, result rounded to dtype)
+ * o, oa: [units][Tseg][D] in dtype (PTOF_BF16 / PTOF_F16), oa distinct from o;
+ * X: [units][D][D] fp32 (rounded to dtype for the tensor-core product). Tseg a
+ * multiple of 128, D 64 or 128, pointers 16-byte aligned. `ws` (from ptof_ws_setup,
+ * or NULL) receives the status of bounded device waits (ptof_check_status).
+ * Launches on `stream`, no host synchronisation. */
+PTOF_API int ptof_seg_fix_exec(void* ws, void* o, const void* oa, const float* X, int units,
+                               int Tseg, int D, int dtype, void* stream);
+
 /* Human-readable text of the last host-side error on this thread. */
 PTOF_API const char* ptof_last_error(void);
 

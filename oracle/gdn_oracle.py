@@ -16,7 +16,10 @@ package is vloncar/pto-fuser; paths below are relative to that project):
   * ``chunk_h_scan``       src/pto_fuser/forwards/fused_stages.py:46-62;
   * ``tri_inv``            src/pto_fuser/registry.py:107-127 semantics, (I+A)^-1 for a
                            strictly-lower A (solve_triangular in _gdn_full.py:76-78);
-  * ``qkv_flash``          src/pto_fuser/fused.py:368-387 semantics (chunk_o intra term).
+  * ``qkv_flash``          src/pto_fuser/fused.py:368-387 semantics (chunk_o intra term);
+  * ``segment_scan``       affine maps of token segments applied in order (no
+                           counterpart in the reference; checked against gdn_forward
+                           run serially).
 
 Parity is pinned: tests/test_oracle.py checks every function here against golden
 vectors produced by running the reference's own torch code
@@ -311,3 +314,23 @@ def kda_forward(q, k, v, beta, g_in, scale, C=C_DEFAULT, dtype=np.float64):
                 g_tot = gc[-1]
                 S = np.exp(g_tot)[:, None] * S + (kc * np.exp(g_tot[None, :] - gc)).T @ vc
     return o * scale
+
+
+def segment_scan(A, B, X0, dtype=np.float64):
+    """Apply per-segment affine state maps in order (the checker of
+    ptof_seg_scan_exec; the reference has no segment split, its scan walks the
+    whole sequence, kernels/scan_fused.h:198-262):
+    X_0 = X0 (None: 0), X_{j+1} = A_j X_j + B_j (B None: no offset).
+    A [H, n, D, D], B [H, n, D, Dv] or None, X0 [H, D, Dv] or None (then Dv from B).
+    Returns (entry states [H, n, D, Dv], exit state [H, D, Dv])."""
+    A = _f(A, dtype)
+    H, n, D = A.shape[:3]
+    Dv = (X0.shape[-1] if X0 is not None else B.shape[-1])
+    X = np.zeros((H, D, Dv), dtype=dtype) if X0 is None else _f(X0, dtype).copy()
+    entries = np.empty((H, n, D, Dv), dtype=dtype)
+    for j in range(n):
+        entries[:, j] = X
+        X = np.einsum("hde,hev->hdv", A[:, j], X)
+        if B is not None:
+            X = X + _f(B, dtype)[:, j]
+    return entries, X

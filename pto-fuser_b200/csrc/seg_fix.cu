@@ -1,0 +1,264 @@
+// Output fix-up of the chunk-segment scan: o += o^A X per token segment.
+//
+// The GDN output of a segment is affine in its entry state: o = o^B + o^A X, where
+// o^B is the forward's output started from a zero state and o^A [Tseg, Dk] its output
+// started from S0 = I with v = 0 (both written by the fused forward), and X [Dk, Dv]
+// is the segment's true entry state. This kernel applies the linear part in place on
+// o (holding o^B), per 128-token tile on the tensor cores:
+//
+//   D[128, Dv] (TMEM, fp32) = o^A tile [128, Dk] (bf16/f16, K-major, TMA)
+//                             x X [Dk, Dv] (fp32 -> bf16/f16, MN-major, staged once per
+//                               segment a CTA touches)
+//   o tile = o^B tile (TMA) + D, stored back with a TMA tensor store.
+//
+// Persistent CTAs (one per SM) walk contiguous tile ranges, so a CTA restages X only
+// when its range crosses a segment boundary. Roles (192 threads):
+//   warp 4  producer: TMA loads of o^A and o^B tiles (2 stages), X staging
+//   warp 5  TMEM owner and UMMA issuer (one thread; two accumulators)
+//   warps 0-3 epilogue: TMEM -> registers, + o^B from shared memory, TMA store.
+// HBM-bound: per token 2 Dk bytes of o^A read, 2 Dv bytes of o read and written.
+#include <cuda_runtime.h>
+
+#include "capi_internal.h"
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace ptof {
+namespace segfix {
+
+constexpr int kRows = 128;
+constexpr int kThreads = 192;
+
+template <int D>
+struct FLayout {
+  static constexpr int NKB = D / 64;
+  static constexpr int TILE = NKB * kRows * 128;   // [128 tokens x D] 16-bit, SW128 blocks
+  static constexpr int XT = NKB * D * 128;         // X [D k-rows x D n], n-blocks of 64
+  static constexpr int OFF_OA = 0;                 // 2 stages
+  static constexpr int OFF_OB = 2 * TILE;          // 2 stages
+  static constexpr int OFF_X = 4 * TILE;           // 2 buffers
+  static constexpr int OFF_BAR = OFF_X + 2 * XT;
+  static constexpr int BYTES = OFF_BAR + 256 + 1024;
+  static constexpr int TCOLS = 2 * D;
+};
+
+enum FBar { F_FULL0 = 0, F_EMPTY0 = 2, F_TFULL0 = 4, F_TFREE0 = 6, F_XFULL0 = 8, F_XFREE0 = 10,
+            F_COUNT = 12 };
+
+struct FParams {
+  CUtensorMap mapOA, mapO;
+  const float* X;      // [units][D][D] fp32 entry states
+  int* status;
+  int64_t tiles;       // units * tiles_per_unit
+  int tiles_per_unit;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_constant__ FParams P) {
+  using L = FLayout<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t sbase = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((sbase + 1023u) & ~1023u) - sbase);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + F_COUNT);
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t t0 = P.tiles * blockIdx.x / gridDim.x;
+  const int64_t cnt = P.tiles * (blockIdx.x + 1) / gridDim.x - t0;
+
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < F_COUNT; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&bars[F_TFREE0], 4);   // one arrival per epilogue warp
+    mbar_init(&bars[F_TFREE0 + 1], 4);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, L::TCOLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto wait = [&](uint64_t* bar, uint32_t par, int site) {
+    if (mbar_try_wait(bar, par)) return true;
+    return mbar_wait(bar, par, &abort_flag, P.status, site);
+  };
+  auto unit_of = [&](int64_t i) { return static_cast<int>((t0 + i) / P.tiles_per_unit); };
+
+  if (warp == 4) {
+    // ================================ producer ================================
+    if (lane == 0) {
+      prefetch_tmap(&P.mapOA);
+      prefetch_tmap(&P.mapO);
+    }
+    int cur = -1, f = 0;   // segment whose X is staged; X fills so far
+    for (int64_t i = 0; i < cnt; ++i) {
+      const int s = static_cast<int>(i & 1);
+      if (i >= 2) wait(&bars[F_EMPTY0 + s], static_cast<uint32_t>(((i >> 1) + 1) & 1), 1);
+      if (lane == 0) {
+        const int y = static_cast<int>((t0 + i) * kRows);
+        mbar_arrive_expect_tx(&bars[F_FULL0 + s], 2 * L::TILE);
+#pragma unroll
+        for (int kb = 0; kb < L::NKB; ++kb) {
+          tma_load_2d(sm + L::OFF_OA + s * L::TILE + kb * kRows * 128, &P.mapOA,
+                      &bars[F_FULL0 + s], kb * 64, y);
+          tma_load_2d(sm + L::OFF_OB + s * L::TILE + kb * kRows * 128, &P.mapO,
+                      &bars[F_FULL0 + s], kb * 64, y);
+        }
+      }
+      const int u = unit_of(i);
+      if (u != cur) {
+        const int xb = f & 1;
+        if (f >= 2) wait(&bars[F_XFREE0 + xb], static_cast<uint32_t>(((f - 2) >> 1) & 1), 2);
+        // X[k][n] fp32 -> 16-bit, MN-major SW128: n-block n/64, row k, byte 2 (n % 64)
+        unsigned char* xs = sm + L::OFF_X + xb * L::XT;
+        const float4* xg = reinterpret_cast<const float4*>(P.X + static_cast<int64_t>(u) * D * D);
+#pragma unroll 4
+        for (int idx = lane; idx < D * D / 4; idx += 32) {
+          const float4 x = xg[idx];
+          const int k = idx / (D / 4), n = (idx % (D / 4)) * 4;
+          const uint32_t lo = BF16 ? pack_bf16(x.x, x.y) : pack_f16(x.x, x.y);
+          const uint32_t hi = BF16 ? pack_bf16(x.z, x.w) : pack_f16(x.z, x.w);
+          *reinterpret_cast<uint2*>(xs + (n >> 6) * (D * 128) + sw128_off(k, (n & 63) * 2)) =
+              make_uint2(lo, hi);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[F_XFULL0 + xb]);
+        cur = u;
+        ++f;
+      }
+    }
+  } else if (warp == 5) {
+    // ============================== UMMA issuer ===============================
+    if (lane == 0) {
+      constexpr uint32_t ID = idesc_f16(kRows, D, false, true, BF16);
+      int cur = -1, f = -1;
+      for (int64_t i = 0; i < cnt; ++i) {
+        const int s = static_cast<int>(i & 1), b = s;
+        const int u = unit_of(i);
+        if (u != cur) {
+          if (f >= 0) umma_commit(&bars[F_XFREE0 + (f & 1)]);   // old X no longer read
+          ++f;
+          wait(&bars[F_XFULL0 + (f & 1)], static_cast<uint32_t>((f >> 1) & 1), 3);
+          cur = u;
+        }
+        wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 4);
+        if (i >= 2) wait(&bars[F_TFREE0 + b], static_cast<uint32_t>(((i >> 1) + 1) & 1), 5);
+        tc_fence_after();
+        const uint32_t a = smem_u32(sm + L::OFF_OA + s * L::TILE);
+        const uint32_t x = smem_u32(sm + L::OFF_X + (f & 1) * L::XT);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma_ss(tmem + b * D, sdesc_sw128(a + (ks >> 2) * (kRows * 128) + (ks & 3) * 32, 16, 1024),
+                  sdesc_sw128(x + ks * 2048, D * 128, 1024), ID, ks > 0);
+        umma_commit(&bars[F_TFULL0 + b]);
+      }
+      if (f >= 0) umma_commit(&bars[F_XFREE0 + (f & 1)]);
+    }
+  } else {
+    // =============================== epilogue =================================
+    const int r = tid;   // tile row = TMEM lane
+    for (int64_t i = 0; i < cnt; ++i) {
+      const int s = static_cast<int>(i & 1), b = s;
+      wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 6);   // o^B visible
+      wait(&bars[F_TFULL0 + b], static_cast<uint32_t>((i >> 1) & 1), 7);
+      tc_fence_after();
+      unsigned char* ob = sm + L::OFF_OB + s * L::TILE;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 16; ++cc) {
+        float v[16];
+        tmem_ld16(tmem + b * D + cc * 16 + ((32u * warp) << 16), v);
+        tmem_wait_ld();
+        unsigned char* row = ob + (cc >> 2) * (kRows * 128);
+        const uint32_t o0 = sw128_off(r, (cc & 3) * 32), o1 = sw128_off(r, (cc & 3) * 32 + 16);
+        uint4 p0 = *reinterpret_cast<const uint4*>(row + o0);
+        uint4 p1 = *reinterpret_cast<const uint4*>(row + o1);
+        uint32_t* w0 = reinterpret_cast<uint32_t*>(&p0);
+        uint32_t* w1 = reinterpret_cast<uint32_t*>(&p1);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 a0 = BF16 ? unpack_bf16(w0[e]) : unpack_f16(w0[e]);
+          const float2 a1 = BF16 ? unpack_bf16(w1[e]) : unpack_f16(w1[e]);
+          w0[e] = BF16 ? pack_bf16(a0.x + v[2 * e], a0.y + v[2 * e + 1])
+                       : pack_f16(a0.x + v[2 * e], a0.y + v[2 * e + 1]);
+          w1[e] = BF16 ? pack_bf16(a1.x + v[8 + 2 * e], a1.y + v[9 + 2 * e])
+                       : pack_f16(a1.x + v[8 + 2 * e], a1.y + v[9 + 2 * e]);
+        }
+        *reinterpret_cast<uint4*>(row + o0) = p0;
+        *reinterpret_cast<uint4*>(row + o1) = p1;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[F_TFREE0 + b]);
+      fence_async_smem();
+      named_bar_sync(1, 128);   // the tile is complete in shared memory
+      if (tid == 0) {
+        const int y = static_cast<int>((t0 + i) * kRows);
+#pragma unroll
+        for (int kb = 0; kb < L::NKB; ++kb) tma_store_2d(&P.mapO, ob + kb * kRows * 128, kb * 64, y);
+        bulk_commit();
+        bulk_wait_read0();
+        mbar_arrive(&bars[F_EMPTY0 + s]);
+      }
+    }
+    if (tid == 0) bulk_wait0();
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, L::TCOLS);
+}
+
+template <int D, bool BF16>
+int launch_t(int* status, void* o, const void* oa, const float* X, int units, int Tseg,
+             cudaStream_t st) {
+  using L = FLayout<D>;
+  FParams P;
+  const CUtensorMapDataType t = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t rows = static_cast<uint64_t>(units) * Tseg;
+  int rc = make_tmap_2d(&P.mapOA, oa, t, 2, D, rows, static_cast<uint64_t>(D) * 2, 64, kRows,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_tmap_2d(&P.mapO, o, t, 2, D, rows, static_cast<uint64_t>(D) * 2, 64, kRows,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  P.X = X;
+  P.status = status;
+  P.tiles_per_unit = Tseg / kRows;
+  P.tiles = static_cast<int64_t>(units) * P.tiles_per_unit;
+  auto kern = seg_fix_kernel<D, BF16>;
+  cudaError_t e = set_smem_once(kern, L::BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "seg_fix smem attribute");
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t grid = P.tiles < sms ? P.tiles : sms;
+  kern<<<static_cast<unsigned>(grid), kThreads, L::BYTES, st>>>(P);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "seg_fix launch");
+}
+
+}  // namespace segfix
+}  // namespace ptof
+
+using namespace ptof;
+
+int ptof_seg_fix_exec(void* ws, void* o, const void* oa, const float* X, int units, int Tseg,
+                      int D, int dtype, void* stream) {
+  Workspace* w = static_cast<Workspace*>(ws);
+  if (units < 1 || Tseg < segfix::kRows || Tseg % segfix::kRows || (D != 64 && D != 128) ||
+      static_cast<int64_t>(units) * Tseg > (1LL << 31) - segfix::kRows)
+    return fail(PTOF_EINVAL, "seg_fix shape units=%d Tseg=%d D=%d (Tseg a multiple of 128, "
+                "D 64 or 128)", units, Tseg, D);
+  if (dtype != PTOF_BF16 && dtype != PTOF_F16) return fail(PTOF_EINVAL, "seg_fix dtype");
+  int rc = check_ptrs({o, oa, X}, {});
+  if (rc) return rc;
+  int* status = w ? w->d_status : nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == PTOF_BF16;
+  if (D == 128)
+    return bf ? segfix::launch_t<128, true>(status, o, oa, X, units, Tseg, st)
+              : segfix::launch_t<128, false>(status, o, oa, X, units, Tseg, st);
+  return bf ? segfix::launch_t<64, true>(status, o, oa, X, units, Tseg, st)
+            : segfix::launch_t<64, false>(status, o, oa, X, units, Tseg, st);
+}

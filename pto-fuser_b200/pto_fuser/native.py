@@ -53,6 +53,7 @@ class GdnVarlenParams(ctypes.Structure):
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int
+_i64 = ctypes.c_int64
 _SIGNATURES = {
     "ptof_gdn_fwd_setup": (_vp, [ctypes.POINTER(GdnParams)]),
     "ptof_gdn_fwd_exec": (_i32, [_vp] * 10),
@@ -60,6 +61,9 @@ _SIGNATURES = {
     "ptof_gdn_fwd_varlen_setup": (_vp, [ctypes.POINTER(GdnVarlenParams)]),
     "ptof_gdn_fwd_varlen_exec": (_i32, [_vp] * 11),
     "ptof_gdn_fwd_exec_noalloc": (_i32, [ctypes.POINTER(GdnParams)] + [_vp] * 9),
+    "ptof_seg_scan_exec": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64,
+                                  _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
+    "ptof_seg_fix_exec": (_i32, [_vp] * 4 + [_i32] * 4 + [_vp]),
     "ptof_check_status": (_i32, [_vp, _vp]),
     "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),
     "ptof_last_error": (ctypes.c_char_p, []),

@@ -1,0 +1,188 @@
+"""Chunk-segment scan on the GPU: ptof_seg_scan_exec against the oracle's
+segment_scan, ptof_seg_fix_exec against a torch product, and GDNSegmentScan (fused
+forward A / B runs, composition, prefix, output fix-up) against the serial oracle and
+the serial fused forward. The 2-rank NCCL case runs when the box has two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn_oracle as orc
+from pto_fuser import make_gdn_inputs
+from pto_fuser.gdn import GDNChunkForward
+from pto_fuser import native as nv
+from pto_fuser.segment import GDNSegmentScan, seg_fix, seg_scan, split_tokens
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2   # bf16 operands, fp32 accumulation
+
+
+@pytest.mark.parametrize("D,nseg,with_b,with_x0", [(128, 5, True, True), (64, 3, False, True),
+                                                   (128, 0, True, True), (128, 2, True, False)])
+def test_seg_scan_kernel_matches_oracle(D, nseg, with_b, with_x0):
+    H, Dv = 3, 96
+    g = torch.Generator().manual_seed(D + nseg)
+    A = torch.randn(H, nseg, D, D, generator=g) * D ** -0.5
+    B = torch.randn(H, nseg, D, Dv, generator=g) if with_b else None
+    X0 = torch.randn(H, D, Dv, generator=g) if with_x0 else None
+    ent_ref, X_ref = orc.segment_scan(A.numpy(), None if B is None else B.numpy(),
+                                      X0.numpy() if X0 is not None else np.zeros((H, D, Dv)))
+    c = lambda t: None if t is None else t.cuda()
+    Xout = torch.full((H, nseg, D, Dv), float("nan"), device="cuda")
+    Xf = torch.full((H, D, Dv), float("nan"), device="cuda")
+    seg_scan(c(A), c(B), c(X0), Xout, Xf, H, nseg, D, Dv)
+    torch.cuda.synchronize()
+    assert np.allclose(Xout.cpu().numpy(), ent_ref, rtol=1e-4, atol=1e-4)
+    assert np.allclose(Xf.cpu().numpy(), X_ref, rtol=1e-4, atol=1e-4)
+
+
+def test_seg_scan_kernel_strided_operands():
+    """The gathered layout [ranks, 2, heads, D, D] read as per-head segment views."""
+    W, H, D = 4, 5, 128
+    g = torch.Generator().manual_seed(3)
+    gath = torch.randn(W, 2, H, D, D, generator=g)
+    gath[:, 0] *= D ** -0.5
+    X0 = torch.randn(H, D, D, generator=g)
+    v = gath.cuda().permute(2, 0, 1, 3, 4)
+    Xf = torch.empty(H, D, D, device="cuda")
+    seg_scan(v[:, :3, 0], v[:, :3, 1], X0.cuda(), None, Xf, H, 3, D, D)
+    _, X_ref = orc.segment_scan(gath[:3, 0].permute(1, 0, 2, 3).numpy(),
+                                gath[:3, 1].permute(1, 0, 2, 3).numpy(), X0.numpy())
+    torch.cuda.synchronize()
+    assert np.allclose(Xf.cpu().numpy(), X_ref, rtol=1e-4, atol=1e-4)
+
+
+def test_seg_scan_rejects_bad_shapes():
+    x = torch.zeros(2, 64, 40, device="cuda")
+    with pytest.raises(RuntimeError):
+        seg_scan(None, None, x, None, torch.zeros_like(x), 2, 0, 64, 40)   # Dv % 32
+
+
+@pytest.mark.parametrize("units,tiles,D,dt", [(5, 40, 128, torch.bfloat16),
+                                               (3, 100, 64, torch.float16),
+                                               (2, 1, 128, torch.bfloat16)])
+def test_seg_fix_kernel(units, tiles, D, dt):
+    """o += oa @ X per unit; more tiles than SMs, so CTAs cross unit boundaries and
+    restage X."""
+    Tseg = 128 * tiles
+    g = torch.Generator(device="cuda").manual_seed(units * tiles)
+    o = torch.randn(units, Tseg, D, device="cuda", generator=g).to(dt)
+    oa = (torch.randn(units, Tseg, D, device="cuda", generator=g) * 0.3).to(dt)
+    X = torch.randn(units, D, D, device="cuda", generator=g) * D ** -0.5
+    ref_x16 = (o.float() + torch.bmm(oa.float(), X.to(dt).float())).to(dt)
+    ref = o.float() + torch.bmm(oa.float(), X)
+    ws = nv.lib().ptof_ws_setup()
+    try:
+        seg_fix(ws, o, oa, X, units, Tseg, D)
+        nv.check(nv.lib().ptof_check_status(ws, nv.stream_handle()))
+    finally:
+        nv.lib().ptof_ws_teardown(ws)
+    assert orc.rel_l2(o.float().cpu().numpy(), ref_x16.float().cpu().numpy()) < 2e-3
+    assert orc.rel_l2(o.float().cpu().numpy(), ref.cpu().numpy()) < TOL
+
+
+def test_seg_fix_rejects_ragged_segments():
+    o = torch.zeros(2, 192, 128, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        seg_fix(None, o, o.clone(), torch.zeros(2, 128, 128, device="cuda"), 2, 192, 128)
+
+
+@pytest.mark.parametrize("segments,mu", [(4, 3.0), (2, 2.0)])
+def test_segment_scan_one_gpu_matches_serial(segments, mu):
+    P, T, D = 4, 4096, 128
+    inp = make_gdn_inputs(1, P, T, D, mu=mu, s0_std=0.02, seed=segments, device="cuda")
+    flat = {n: t[0] for n, t in inp.items()}
+    run = GDNSegmentScan(P, T, D, segments=segments)
+    o, S = run(flat["q"], flat["k"], flat["v"], flat["beta"], flat["g"], flat["S0"])
+    torch.cuda.synchronize()
+    run.check_status()
+    # serial fused forward
+    ser = GDNChunkForward(1, P, T, D, D)
+    o_s, S_s = ser(inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"], inp["S0"])
+    assert orc.rel_l2(o.float().cpu().numpy(), o_s[0].float().cpu().numpy()) < TOL
+    assert orc.rel_l2(S.cpu().numpy(), S_s[0].cpu().numpy()) < TOL
+    # serial oracle on the first two pairs
+    n = lambda k: inp[k][:, :2].float().cpu().numpy()
+    o_r, S_r = orc.gdn_forward(n("q"), n("k"), n("v"), n("beta"), n("g"), D ** -0.5, S0=n("S0"))
+    assert orc.rel_l2(o[:2].float().cpu().numpy(), o_r[0]) < TOL
+    assert orc.rel_l2(S[:2].cpu().numpy(), S_r[0]) < TOL
+
+
+def test_segment_scan_config4_full_size_equals_serial():
+    """BASELINE config 4 (B1 H64 T131072 D128, S0 ~ N(0, 0.02^2), g = logsigmoid(N(3,1)))
+    split into 4 token segments on one GPU: outputs and final state equal the serial
+    fused forward's (a size-independent property; the oracle covers small sizes)."""
+    P, T, D = 64, 131072, 128
+    g = torch.Generator(device="cuda").manual_seed(4)
+    nrm = torch.nn.functional.normalize
+    bf = torch.bfloat16
+    q = nrm(torch.randn(P, T, D, device="cuda", generator=g), dim=-1).to(bf)
+    k = nrm(torch.randn(P, T, D, device="cuda", generator=g), dim=-1).to(bf)
+    v = torch.randn(P, T, D, device="cuda", generator=g).to(bf)
+    beta = torch.sigmoid(torch.randn(P, T, device="cuda", generator=g)).to(bf)
+    gg = torch.nn.functional.logsigmoid(torch.randn(P, T, device="cuda", generator=g) + 3.0)
+    S0 = torch.randn(P, D, D, device="cuda", generator=g) * 0.02
+    run = GDNSegmentScan(P, T, D, segments=4)
+    o, S = run(q, k, v, beta, gg, S0)
+    run.check_status()
+    ser = GDNChunkForward(1, P, T, D, D)
+    o_s, S_s = ser(q[None], k[None], v[None], beta[None], gg[None], S0[None])
+    ser.check_status()
+    num = torch.linalg.vector_norm((o.float() - o_s[0].float())).item()
+    den = torch.linalg.vector_norm(o_s[0].float()).item()
+    assert num / den < TOL
+    assert (torch.linalg.vector_norm(S - S_s[0]) / torch.linalg.vector_norm(S_s[0])).item() < TOL
+    run.close()
+    ser.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, out_dir):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "pto-fuser_b200")]
+    import torch.distributed as dist
+    from pto_fuser import make_gdn_inputs as mk
+    from pto_fuser.segment import GDNSegmentScan as Seg, split_tokens as split
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        P, T, D = 4, 4096, 128
+        inp = mk(1, P, T, D, mu=3.0, s0_std=0.02, seed=21)
+        sizes = split(T, world)
+        a = sum(sizes[:rank])
+        loc = lambda k: inp[k][0, :, a:a + sizes[rank]].contiguous().cuda()
+        run = Seg(P, sizes[rank], D, segments=2, group=dist.group.WORLD)
+        o, S = run(loc("q"), loc("k"), loc("v"), loc("beta"), loc("g"), inp["S0"][0].cuda())
+        torch.cuda.synchronize()
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), o=o.float().cpu().numpy(),
+                 S=S.cpu().numpy(), a=a)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_segment_scan_two_gpus_nccl(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    P, T, D = 4, 4096, 128
+    inp = make_gdn_inputs(1, P, T, D, mu=3.0, s0_std=0.02, seed=21)
+    n = lambda k: inp[k][:, :2].float().numpy()
+    o_r, S_r = orc.gdn_forward(n("q"), n("k"), n("v"), n("beta"), n("g"), D ** -0.5, S0=n("S0"))
+    sizes = split_tokens(T, world)
+    for r in range(world):
+        res = np.load(tmp_path / f"r{r}.npz")
+        a = int(res["a"])
+        assert orc.rel_l2(res["o"][:2], o_r[0][:, a:a + sizes[r]]) < TOL
+    assert orc.rel_l2(res["S"][:2], S_r[0]) < TOL
