@@ -229,8 +229,8 @@ PTOF_API int ptof_check_status(void* ws, void* stream);
  * and writes the entry state X_j of each segment to Xout (NULL: not written) and
  * X_nseg to Xfinal (NULL: not written). All fp32; every matrix is row-major with
  * rows of D (A) or Dv (B, X) floats; the *_stride arguments give, in floats, the
- * distance between heads and between segments. D in {64, 128}, Dv a multiple of
- * 32, nseg >= 0. Launches on `stream`, no host synchronisation. Outputs must not
+ * distance between heads and between segments (multiples of 4; pointers 16-byte
+ * aligned). D in {64, 128}, Dv a multiple of 32, nseg >= 0. Launches on `stream`, no host synchronisation. Outputs must not
  * overlap the inputs.
  */
 PTOF_API int ptof_seg_scan_exec(const float* A, int64_t a_head_stride, int64_t a_seg_stride,

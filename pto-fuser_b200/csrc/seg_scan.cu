@@ -10,8 +10,8 @@
 //
 // writing the entry state X_j of every segment (Xout) and the exit state X_nseg
 // (Xfinal). One CTA owns 32 state columns of one head: the columns stay in shared
-// memory across segments and A_j is staged into shared memory once per segment, so
-// the work per segment is one [Dk,Dk] x [Dk,32] fp32 product. The same kernel
+// memory across segments and A_j streams into shared memory (double-buffered) once
+// per segment, so the work per segment is one [Dk,Dk] x [Dk,32] fp32 product. The same kernel
 // composes two maps (A1,B1) o (A0,B0) = (A1 A0, A1 B0 + B1) by scanning X0 = A0 with
 // no offset and X0 = B0 with offset B1.
 #include <cstdint>
@@ -33,64 +33,124 @@ struct Params {
 constexpr int kCols = 32;
 constexpr int kThreads = 256;
 
+// 16-byte asynchronous global -> shared copy (completion by cp.async.wait_group)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Thread tile: R = D / 32 rows x 4 columns (thread t: columns 4 (t % 8), rows
+// R (t / 8)). A_j rows are padded to D + 4 floats so the R rows a warp reads at one
+// k fall in different banks; A_{j+1} streams into the second buffer (cp.async) while
+// A_j is applied.
+template <int D>
+struct SLayout {
+  static constexpr int AP = D + 4;                       // padded A row (floats)
+  static constexpr int A_FLOATS = D * AP;
+  static constexpr int BYTES = (2 * A_FLOATS + D * kCols) * 4;
+};
+
+template <int D>
+__device__ __forceinline__ void load_a_async(float* As, const float* a, int t) {
+  constexpr int AP = SLayout<D>::AP;
+#pragma unroll 4
+  for (int e = t; e < D * D / 4; e += kThreads) {
+    const int row = e / (D / 4), c4 = e % (D / 4);
+    cp_async16(As + row * AP + 4 * c4, a + static_cast<int64_t>(row) * D + 4 * c4);
+  }
+  cp_async_commit();
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads) seg_scan_kernel(Params p) {
-  extern __shared__ float smem[];
-  float* As = smem;               // [D][D] transition of the current segment
-  float* cur = smem + D * D;      // [D][kCols] running state columns
-  constexpr int R = D / (kThreads / kCols);   // rows per thread
+  using SL = SLayout<D>;
+  constexpr int AP = SL::AP;
+  constexpr int R = D / 32;
+  extern __shared__ __align__(16) float smem[];
+  float* Abuf = smem;                                    // 2 x [D][AP]
+  float* cur = smem + 2 * SL::A_FLOATS;                  // [D][kCols] running state columns
   const int head = blockIdx.x;
   const int c0 = blockIdx.y * kCols;
   const int t = threadIdx.x;
-  const int c = t % kCols;
-  const int r0 = (t / kCols) * R;
+  const int cq = (t % 8) * 4;                            // this thread's 4 columns
+  const int r0 = (t / 8) * R;                            // and R rows
   const int Dv = p.Dv;
 
+  if (p.nseg > 0) load_a_async<D>(Abuf, p.A + head * p.a_hs, t);
   const float* x0 = p.X0 ? p.X0 + head * p.x0_hs : nullptr;
-#pragma unroll
-  for (int i = 0; i < R; ++i)
-    cur[(r0 + i) * kCols + c] = x0 ? x0[(int64_t)(r0 + i) * Dv + c0 + c] : 0.f;
-  __syncthreads();
+  for (int e = t; e < D * kCols / 4; e += kThreads) {
+    const int row = e / (kCols / 4), c4 = (e % (kCols / 4)) * 4;
+    const float4 x = x0 ? *reinterpret_cast<const float4*>(x0 + static_cast<int64_t>(row) * Dv + c0 + c4)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(cur + row * kCols + c4) = x;
+  }
 
   for (int j = 0; j < p.nseg; ++j) {
+    float* As = Abuf + (j & 1) * SL::A_FLOATS;
+    cp_async_wait_all();
+    __syncthreads();                                     // A_j and cur complete
+    if (j + 1 < p.nseg)
+      load_a_async<D>(Abuf + ((j + 1) & 1) * SL::A_FLOATS, p.A + head * p.a_hs + (j + 1) * p.a_ss, t);
     if (p.Xout) {
       float* xo = p.Xout + head * p.xo_hs + j * p.xo_ss;
 #pragma unroll
-      for (int i = 0; i < R; ++i) xo[(int64_t)(r0 + i) * Dv + c0 + c] = cur[(r0 + i) * kCols + c];
+      for (int i = 0; i < R; ++i)
+        *reinterpret_cast<float4*>(xo + static_cast<int64_t>(r0 + i) * Dv + c0 + cq) =
+            *reinterpret_cast<const float4*>(cur + (r0 + i) * kCols + cq);
     }
-    const float* a = p.A + head * p.a_hs + j * p.a_ss;
-    for (int e = t; e < D * D; e += kThreads) As[e] = a[e];
-    float acc[R];
+    float acc[R][4];
     if (p.Bv) {
       const float* b = p.Bv + head * p.b_hs + j * p.b_ss;
 #pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] = b[(int64_t)(r0 + i) * Dv + c0 + c];
+      for (int i = 0; i < R; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(b + static_cast<int64_t>(r0 + i) * Dv + c0 + cq);
+        acc[i][0] = v.x; acc[i][1] = v.y; acc[i][2] = v.z; acc[i][3] = v.w;
+      }
     } else {
 #pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] = 0.f;
+      for (int i = 0; i < R; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     }
-    __syncthreads();
-#pragma unroll 4
-    for (int k = 0; k < D; ++k) {
-      const float s = cur[k * kCols + c];
+#pragma unroll 2
+    for (int k = 0; k < D; k += 4) {
+      float4 s4[4];
 #pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] = fmaf(As[(r0 + i) * D + k], s, acc[i]);
+      for (int kk = 0; kk < 4; ++kk) s4[kk] = *reinterpret_cast<const float4*>(cur + (k + kk) * kCols + cq);
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const float4 a = *reinterpret_cast<const float4*>(As + (r0 + i) * AP + k);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          acc[i][0] = fmaf(av[kk], s4[kk].x, acc[i][0]);
+          acc[i][1] = fmaf(av[kk], s4[kk].y, acc[i][1]);
+          acc[i][2] = fmaf(av[kk], s4[kk].z, acc[i][2]);
+          acc[i][3] = fmaf(av[kk], s4[kk].w, acc[i][3]);
+        }
+      }
     }
-    __syncthreads();   // every thread has read cur and As
+    __syncthreads();                                     // every thread has read cur
 #pragma unroll
-    for (int i = 0; i < R; ++i) cur[(r0 + i) * kCols + c] = acc[i];
-    __syncthreads();
+    for (int i = 0; i < R; ++i)
+      *reinterpret_cast<float4*>(cur + (r0 + i) * kCols + cq) =
+          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   }
+  __syncthreads();
   if (p.Xf) {
     float* xf = p.Xf + head * p.xf_hs;
 #pragma unroll
-    for (int i = 0; i < R; ++i) xf[(int64_t)(r0 + i) * Dv + c0 + c] = cur[(r0 + i) * kCols + c];
+    for (int i = 0; i < R; ++i)
+      *reinterpret_cast<float4*>(xf + static_cast<int64_t>(r0 + i) * Dv + c0 + cq) =
+          *reinterpret_cast<const float4*>(cur + (r0 + i) * kCols + cq);
   }
 }
 
 template <int D>
 int launch(const Params& p, int heads, cudaStream_t st) {
-  const int smem = (D * D + D * kCols) * static_cast<int>(sizeof(float));
+  const int smem = SLayout<D>::BYTES;
   cudaError_t e = set_smem_once(seg_scan_kernel<D>, smem);
   if (e != cudaSuccess) return cuda_fail(e, "seg_scan smem attribute");
   seg_scan_kernel<D><<<dim3(heads, p.Dv / kCols), kThreads, smem, st>>>(p);
@@ -118,6 +178,13 @@ int ptof_seg_scan_exec(const float* A, int64_t a_head_stride, int64_t a_seg_stri
   if (a_head_stride < 0 || a_seg_stride < 0 || b_head_stride < 0 || b_seg_stride < 0 ||
       x0_head_stride < 0 || xout_head_stride < 0 || xout_seg_stride < 0 || xfinal_head_stride < 0)
     return fail(PTOF_EINVAL, "seg_scan: negative stride");
+  if ((a_head_stride | a_seg_stride | b_head_stride | b_seg_stride | x0_head_stride |
+       xout_head_stride | xout_seg_stride | xfinal_head_stride) & 3)
+    return fail(PTOF_EALIGN, "seg_scan: strides must be multiples of 4 floats");
+  for (const void* q : {static_cast<const void*>(A), static_cast<const void*>(Bv),
+                        static_cast<const void*>(X0), static_cast<const void*>(Xout),
+                        static_cast<const void*>(Xfinal)})
+    if (reinterpret_cast<uintptr_t>(q) & 15) return fail(PTOF_EALIGN, "seg_scan: pointer not 16-byte aligned");
   segscan::Params p{A, a_head_stride, a_seg_stride, Bv, b_head_stride, b_seg_stride,
                     X0, x0_head_stride, Xout, xout_head_stride, xout_seg_stride,
                     Xfinal, xfinal_head_stride, nseg, Dv};
