@@ -1,8 +1,10 @@
 // fp32 SIMT chunk forward of Gated DeltaNet.
 //
 // The full-precision path (fp32 inputs, reference tolerance 1e-4): every
-// contraction accumulates in fp32 FMA on the CUDA cores, the (I+A)^-1 solve is a
-// column-parallel forward substitution, and the state S[Dk, BV] of one
+// contraction accumulates in fp32 FMA on the CUDA cores (value-column products in
+// register tiles of four columns), the (I+A)^-1 solve is a forward substitution
+// row by row with every column (and four partial sums of each) in parallel, the
+// per-token exponentials are computed once per chunk, and the state S[Dk, BV] of one
 // (batch, head, value-block) stays resident in shared memory across all chunks.
 // It restates, step for step, gdn_reference (examples/attention/_gdn_full.py:57-97):
 //   A   = tril((k k^T) * safe_exp(g_i - g_j) * beta_i, -1)          :73-75
@@ -44,10 +46,11 @@ struct Args {
 };
 
 // shared-memory carve-up (floats); padded rows break bank conflicts
-struct Smem {
-  static constexpr int kLdK = kMaxDk + 1;
+struct __align__(16) Smem {
+  // rows padded to a multiple of 4 floats (float4 access) plus 4 (bank spread)
+  static constexpr int kLdK = kMaxDk + 4;
   static constexpr int kLdC = kC + 1;
-  static constexpr int kLdV = kBV + 1;
+  static constexpr int kLdV = kBV + 4;
   float K[kC * kLdK];
   float Q[kC * kLdK];
   float W[kC * kLdK];
@@ -60,6 +63,9 @@ struct Smem {
   float S[kMaxDk * kLdV];
   float g[kC];
   float beta[kC];
+  float eg[kC];    // e^{g_i}
+  float wk[kC];    // beta_j e^{g_j}   (W operand scale)
+  float gam[kC];   // e^{g_last - g_i} (state update scale)
 };
 
 template <typename TI, typename TB, typename TO>
@@ -130,6 +136,13 @@ __global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
       s.beta[2 * tid + 1] = to_f32(bp[static_cast<int64_t>(t0 + 2 * tid + 1) * a.sg.t]);
     }
     __syncthreads();
+    if (tid < kC) {
+      // per-token exponentials, once per chunk (not per product term)
+      const float gi = s.g[tid], e = expf(gi);
+      s.eg[tid] = e;
+      s.wk[tid] = s.beta[tid] * e;
+      s.gam[tid] = expf(s.g[kC - 1] - gi);
+    }
 
     // ---- A (strictly lower, gated) and Aqk (causal, gated) ----------------
     for (int idx = tid; idx < kC * kC; idx += kThreads) {
@@ -151,64 +164,105 @@ __global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
     }
     __syncthreads();
 
-    // ---- T = (I + A)^-1: thread j solves column j by forward substitution --
-    if (tid < kC) {
-      const int j = tid;
-      for (int i = 0; i < kC; ++i) s.Tm[i * ldc + j] = (i == j) ? 1.f : 0.f;
-      for (int i = j + 1; i < kC; ++i) {
+    // ---- T = (I + A)^-1 by forward substitution, one row at a time:
+    //      T[i][j] = -sum_{j <= k < i} A[i][k] T[k][j]  (j < i), T[i][i] = 1.
+    //      Thread (j, part) = (tid / 4, tid % 4) sums every fourth k of column j; the
+    //      four partial sums meet by shuffles (same summation for every row) ----
+    {
+      const int j = tid >> 2, part = tid & 3;
+      for (int i = 0; i < kC; ++i) {
         float acc = 0.f;
-        for (int kk = j; kk < i; ++kk) acc = fmaf(s.A[i * ldc + kk], s.Tm[kk * ldc + j], acc);
-        s.Tm[i * ldc + j] = -acc;
+        for (int kk = j + part; kk < i; kk += 4) acc = fmaf(s.A[i * ldc + kk], s.Tm[kk * ldc + j], acc);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (part == 0) s.Tm[i * ldc + j] = (j < i) ? -acc : (j == i ? 1.f : 0.f);
+        __syncthreads();
       }
     }
-    __syncthreads();
 
     // ---- W = T (k * beta * exp(g)),  U = T (v * beta) ----------------------
-    for (int idx = tid; idx < kC * Dk; idx += kThreads) {
-      const int i = idx / Dk, d = idx % Dk;
-      float acc = 0.f;
-      for (int j = 0; j <= i; ++j)
-        acc = fmaf(s.Tm[i * ldc + j], s.K[j * ldk + d] * (s.beta[j] * expf(s.g[j])), acc);
-      s.W[i * ldk + d] = acc;
+    // (register tiles of 4 consecutive columns: one float4 shared load per 4 FMAs)
+    const int dk4 = (Dk + 3) / 4;
+    for (int idx = tid; idx < kC * dk4; idx += kThreads) {
+      const int i = idx / dk4, d = (idx % dk4) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j <= i; ++j) {
+        const float t = s.Tm[i * ldc + j] * s.wk[j];
+        const float4 kv = *reinterpret_cast<const float4*>(&s.K[j * ldk + d]);
+        acc.x = fmaf(t, kv.x, acc.x); acc.y = fmaf(t, kv.y, acc.y);
+        acc.z = fmaf(t, kv.z, acc.z); acc.w = fmaf(t, kv.w, acc.w);
+      }
+      *reinterpret_cast<float4*>(&s.W[i * ldk + d]) = acc;
     }
-    for (int idx = tid; idx < kC * kBV; idx += kThreads) {
-      const int i = idx / kBV, jv = idx % kBV;
-      float acc = 0.f;
-      for (int j = 0; j <= i; ++j) acc = fmaf(s.Tm[i * ldc + j], s.V[j * ldv + jv] * s.beta[j], acc);
-      s.U[i * ldv + jv] = acc;
+    for (int idx = tid; idx < kC * (kBV / 4); idx += kThreads) {
+      const int i = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j <= i; ++j) {
+        const float t = s.Tm[i * ldc + j] * s.beta[j];
+        const float4 vv = *reinterpret_cast<const float4*>(&s.V[j * ldv + jv]);
+        acc.x = fmaf(t, vv.x, acc.x); acc.y = fmaf(t, vv.y, acc.y);
+        acc.z = fmaf(t, vv.z, acc.z); acc.w = fmaf(t, vv.w, acc.w);
+      }
+      *reinterpret_cast<float4*>(&s.U[i * ldv + jv]) = acc;
     }
     __syncthreads();
 
     // ---- v_new = U - W S --------------------------------------------------
-    for (int idx = tid; idx < kC * kBV; idx += kThreads) {
-      const int i = idx / kBV, jv = idx % kBV;
-      float acc = 0.f;
-      for (int d = 0; d < Dk; ++d) acc = fmaf(s.W[i * ldk + d], s.S[d * ldv + jv], acc);
-      s.Vn[i * ldv + jv] = s.U[i * ldv + jv] - acc;
+    for (int idx = tid; idx < kC * (kBV / 4); idx += kThreads) {
+      const int i = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int d = 0; d < Dk; ++d) {
+        const float w = s.W[i * ldk + d];
+        const float4 sv = *reinterpret_cast<const float4*>(&s.S[d * ldv + jv]);
+        acc.x = fmaf(w, sv.x, acc.x); acc.y = fmaf(w, sv.y, acc.y);
+        acc.z = fmaf(w, sv.z, acc.z); acc.w = fmaf(w, sv.w, acc.w);
+      }
+      const float4 u = *reinterpret_cast<const float4*>(&s.U[i * ldv + jv]);
+      *reinterpret_cast<float4*>(&s.Vn[i * ldv + jv]) =
+          make_float4(u.x - acc.x, u.y - acc.y, u.z - acc.z, u.w - acc.w);
     }
     __syncthreads();
 
     // ---- o = scale * ((q S) * exp(g) + Aqk v_new) -------------------------
-    for (int idx = tid; idx < kC * kBV; idx += kThreads) {
-      const int i = idx / kBV, jv = idx % kBV;
-      float qs = 0.f;
-      for (int d = 0; d < Dk; ++d) qs = fmaf(s.Q[i * ldk + d], s.S[d * ldv + jv], qs);
-      float intra = 0.f;
-      for (int j = 0; j <= i; ++j) intra = fmaf(s.Aqk[i * ldc + j], s.Vn[j * ldv + jv], intra);
-      const float ov = a.scale * (qs * expf(s.g[i]) + intra);
-      if (jv < nv) op[static_cast<int64_t>(t0 + i) * a.sv.t + jv] = from_f32<TO>(ov);
+    for (int idx = tid; idx < kC * (kBV / 4); idx += kThreads) {
+      const int i = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
+      float qs[4] = {0.f, 0.f, 0.f, 0.f}, in[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int d = 0; d < Dk; ++d) {
+        const float qd = s.Q[i * ldk + d];
+        const float4 sv = *reinterpret_cast<const float4*>(&s.S[d * ldv + jv]);
+        qs[0] = fmaf(qd, sv.x, qs[0]); qs[1] = fmaf(qd, sv.y, qs[1]);
+        qs[2] = fmaf(qd, sv.z, qs[2]); qs[3] = fmaf(qd, sv.w, qs[3]);
+      }
+      for (int j = 0; j <= i; ++j) {
+        const float aq = s.Aqk[i * ldc + j];
+        const float4 vn = *reinterpret_cast<const float4*>(&s.Vn[j * ldv + jv]);
+        in[0] = fmaf(aq, vn.x, in[0]); in[1] = fmaf(aq, vn.y, in[1]);
+        in[2] = fmaf(aq, vn.z, in[2]); in[3] = fmaf(aq, vn.w, in[3]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float ov = a.scale * (qs[e] * s.eg[i] + in[e]);
+        if (jv + e < nv) op[static_cast<int64_t>(t0 + i) * a.sv.t + jv + e] = from_f32<TO>(ov);
+      }
     }
     __syncthreads();
 
     // ---- S = exp(g_last) S + k^T (v_new * exp(g_last - g)) ----------------
     const float gl = s.g[kC - 1];
     const float egl = expf(gl);
-    for (int idx = tid; idx < Dk * kBV; idx += kThreads) {
-      const int d = idx / kBV, jv = idx % kBV;
-      float acc = 0.f;
-      for (int i = 0; i < kC; ++i)
-        acc = fmaf(s.K[i * ldk + d], s.Vn[i * ldv + jv] * expf(gl - s.g[i]), acc);
-      s.S[d * ldv + jv] = egl * s.S[d * ldv + jv] + acc;
+    for (int idx = tid; idx < Dk * (kBV / 4); idx += kThreads) {
+      const int d = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < kC; ++i) {
+        const float kg = s.K[i * ldk + d] * s.gam[i];
+        const float4 vn = *reinterpret_cast<const float4*>(&s.Vn[i * ldv + jv]);
+        acc.x = fmaf(kg, vn.x, acc.x); acc.y = fmaf(kg, vn.y, acc.y);
+        acc.z = fmaf(kg, vn.z, acc.z); acc.w = fmaf(kg, vn.w, acc.w);
+      }
+      float4* sp = reinterpret_cast<float4*>(&s.S[d * ldv + jv]);
+      const float4 o = *sp;
+      *sp = make_float4(fmaf(egl, o.x, acc.x), fmaf(egl, o.y, acc.y), fmaf(egl, o.z, acc.z),
+                        fmaf(egl, o.w, acc.w));
     }
   }
   __syncthreads();
