@@ -436,7 +436,7 @@ def run_long(args):
     torch.cuda.set_device(dev)
     from pto_fuser import GDNChunkForward
     from pto_fuser.segment import GDNSegmentScan, split_tokens
-    B, H, T, D = 1, 64, 131072, 128
+    B, H, T, D = 1, 64, args.long_tokens or 131072, 128
     P = B * H
     Tl = split_tokens(T, world)[rank]
     segs = args.segments if args.segments else 1
@@ -501,9 +501,10 @@ def run_long(args):
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg4: GDN forward B1 H64 T131072 D128 bf16, S0 ~ N(0,0.02^2), "
+            "config": {"workload": f"cfg4: GDN forward B1 H64 T{T} D128 bf16, S0 ~ N(0,0.02^2), "
                                    "g = logsigmoid(N(3,1))", "parallelism": how,
-                       "tokens_per_rank": Tl, "l2": "8.6 GB of operands vs 126 MB L2"},
+                       "tokens_per_rank": Tl,
+                       "l2": f"{algo / 1e9:.2f} GB of operands vs 126 MB L2 (no flush needed)"},
             "roofline": {"bound": "hbm", "algo_bytes": algo,
                          "achieved": algo / (ms / 1e3) / 1e9, "peak": hbm * world,
                          "unit": "GB/s", "frac": algo / (ms / 1e3) / 1e9 / (hbm * world),
@@ -528,6 +529,9 @@ def main():
     ap.add_argument("--long-context", action="store_true",
                     help="config 4 (B1 H64 T131072) with the token axis split over the ranks "
                          "(chunk-segment scan, strong scaling)")
+    ap.add_argument("--long-tokens", type=int, default=0,
+                    help="sequence length for --long-context other than config 4's 131072 "
+                         "(small cases for profiling; not a bench line of config 4)")
     ap.add_argument("--segments", type=int, default=0,
                     help="sub-segments per rank for --long-context (default 1; on one GPU 1 is "
                          "the serial forward)")
