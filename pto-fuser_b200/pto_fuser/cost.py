@@ -75,9 +75,13 @@ class CostModel:
             return Prediction(10.0 if ok else 0.0,
                               "one tcgen05 launch for the whole forward (q,k,v,beta,g read once)"
                               if ok else "fused forward supports C=64, D in {64,128}")
-        if n in ("lower-resident-scan",):
+        if n in ("lower-resident-scan", "lower-perdim-scan"):
             return Prediction(1.0 + 0.05 * feat.nc,
                               f"keeps S on chip across {feat.nc} chunks")
+        if n == "batch-chunk-intra-score":
+            return Prediction(0.5 + 0.05 * feat.nc,
+                              f"{feat.nc} per-chunk intra scores -> one batched kernel",
+                              v2=feat.C * feat.D >= 4096)
         if n == "fuse-chunk-o-flash":
             return Prediction(0.4, "masked score never reaches HBM")
         if n == "fuse-contraction-epilogue":
@@ -85,6 +89,6 @@ class CostModel:
                               v2=feat.C * feat.D >= 4096)
         if n in ("enable-direct-reads", "enable-fused-store"):
             return Prediction(0.0, "read-mode levers have no effect on B200 (torch contraction)")
-        if n in ("lower-perdim-scan", "fuse-perdim-chunk-o-flash", "batch-chunk-intra-score"):
-            return Prediction(0.0, "per-dim / linear-attention kernels not built on B200")
+        if n == "fuse-perdim-chunk-o-flash":
+            return Prediction(0.0, "per-dim score -> output flash kernel not built on B200")
         return Prediction(0.0, "unknown transform - no prediction")

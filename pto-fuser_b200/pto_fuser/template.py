@@ -7,8 +7,9 @@ kernel shape; ``FuseContractionEpilogue`` rewrites every unit some template matc
 and leaves the rest staged; ``FuseChunkOFlash`` fuses the chunk_o score -> output
 chain into one ``qkv_flash_native_v2`` node; ``epilogue_report`` explains each
 contraction's fate. Proven-only: a template exists only where a kernel backs it.
-The per-dim (KDA / GLA) prologue kernels are not built for B200, so their template
-and ``FusePerDimChunkOFlash`` never match.
+The per-dim (KDA) chunk_o score is backed by the ``qk_prologue`` kernel
+(``PerDimPrologueTemplate``); the per-dim score -> output flash kernel is not built, so
+``FusePerDimChunkOFlash`` never matches.
 """
 from __future__ import annotations
 
@@ -136,12 +137,39 @@ class GatedChunkOTemplate(Template):
 
 
 class PerDimPrologueTemplate(Template):
-    """Per-dim (KDA / GLA) prologue template: no B200 kernel backs it, never matches."""
+    """KDA chunk_o score with the per-dimension gate on its operands:
+    ``Aqk = tril((qF * coef_ag)(kF * coef_bg)^T, 0)`` -> ``qk_prologue[_v2]``, which
+    applies the two operand scales while loading (the reference's template of the same
+    name, src/pto_fuser/template.py:174-203). The unit is the score einsum whose two
+    operands come from those prescale muls, followed by ``tril -> contiguous``. The
+    q-side product also feeds the inter-chunk output, so it stays; the k-side product
+    is dropped when the score einsum is its only consumer."""
     name = "qk-prologue"
     family = "per-dim-prologue"
 
     def matches(self, program, unit) -> bool:
-        return False
+        pa = unit.prologue.get(unit.anchor.inputs[0])
+        pb = unit.prologue.get(unit.anchor.inputs[1])
+        return (pa is not None and pb is not None
+                and unit.anchor.equation == "nid,njd->nij"
+                and pa[1] == ["qF", "coef_ag"] and pb[1] == ["kF", "coef_bg"]
+                and unit.epilogue_ops == ["tril", "contiguous"])
+
+    def emit(self, program, unit, dims):
+        from .transforms.chunked import select_prologue_kernel
+        if dims.v2 is None:
+            kernel = select_prologue_kernel(dims.C, dims.D)
+        else:
+            kernel = "qk_prologue_v2" if dims.v2 else "qk_prologue"
+        node = FusedNode(kernel=kernel, inputs=["qF", "kF", "coef_ag", "coef_bg"],
+                         outputs=[unit.boundary_out],
+                         params={"nc": dims.nc, "H": dims.N, "C": dims.C, "D": dims.D},
+                         subsumes=["chunk_o k-side gate mul + Aqk einsum + tril + contiguous"])
+        drop = {unit.anchor_idx} | {i for i, _ in unit.epilogue}
+        k_mul = unit.prologue[unit.anchor.inputs[1]][0]
+        if _only_consumer(program, program.nodes[k_mul].output) == unit.anchor_idx:
+            drop.add(k_mul)
+        return node, drop
 
 
 def default_templates() -> List[Template]:

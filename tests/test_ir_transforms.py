@@ -116,3 +116,36 @@ def test_compile_unverified_partial_lowering():
     res = compile_program(prog, Features(B, H, NC, 32, D), verify=False)
     ks = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
     assert ks == {"chunk_h_scan", "qkv_flash_native_v2", "kkt_gated_native_v2"}
+
+
+def test_policy_and_compile_kda():
+    """KDA: the per-dim scan and the epilogue generator (its qk_prologue template)
+    apply, the scalar-decay scan and the whole-forward fusion do not (reference
+    tests/test_compile.py:64-70); the per-dim score -> output flash is not built, so
+    the compiled program keeps the prologue score (the reference's compile consumes it
+    in qkvp_flash_native_v2 instead)."""
+    from pto_fuser.forwards import build_kda_program
+    prog = build_kda_program(1, 16, 8, 128, 128, 128 ** -0.5)
+    f = Features(1, 16, 8, 128, 128)
+    names = [p.name for p in Policy().pipeline(canonicalize(prog), f)]
+    assert "lower-perdim-scan" in names and "fuse-contraction-epilogue" in names
+    assert "lower-resident-scan" not in names and "fuse-gdn-forward" not in names
+    res = compile_program(prog, f, verify=False)
+    ks = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
+    assert ks == {"chunk_h_scan", "qk_prologue_v2"}
+
+
+@pytest.mark.parametrize("per_dim", [False, True])
+def test_policy_and_compile_chunked_linear(per_dim):
+    """Chunked linear attention: batch-chunk-intra-score is proposed and lowers the
+    per-chunk scores to one kernel (gated_qk_native_v2 for a scalar gate, qk_prologue
+    for GLA's per-channel gate; C * d_k = 1024 -> the V1 prologue key)."""
+    from pto_fuser.forwards.chunked import build_chunked_linear_program
+    N, nc, C_, dk = 2, 4, 16, 64
+    prog = build_chunked_linear_program(N, nc, C_, dk, dk)
+    f = Features(1, N, nc, C_, dk, per_dim_gate=per_dim)
+    names = [p.name for p in Policy().pipeline(canonicalize(prog), f)]
+    assert "batch-chunk-intra-score" in names
+    res = compile_program(prog, f, verify=False)
+    ks = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
+    assert ks == ({"qk_prologue"} if per_dim else {"gated_qk_native_v2"})

@@ -8,6 +8,7 @@ import torch
 from oracle import gdn_oracle as orc
 from pto_fuser import FusedNode, OpaqueNode
 from pto_fuser.forwards import build_kda_program, make_kda_inputs, prepare_kda_bindings
+from pto_fuser.template import FuseContractionEpilogue
 from pto_fuser.transforms import LowerPerDimScan, LowerResidentScan
 
 B, H, NC, C, D = 1, 2, 4, 64, 64
@@ -27,6 +28,23 @@ def test_kda_program_and_perdim_scan_rewrite():
     assert not any(getattr(n, "output", "").startswith("WS0") for n in res.program.nodes)
 
 
+def test_kda_chunk_o_prologue_template():
+    """The per-dim chunk_o score becomes one qk_prologue node (k-side mul absorbed,
+    q-side kept for the inter-chunk term); kkt stays a plain einsum, as in the
+    reference (transforms/kda.py:1-8)."""
+    prog = build_kda_program(B, H, NC, C, D, D ** -0.5)
+    t = FuseContractionEpilogue(B, H, NC, C, D)
+    assert t.match(prog) == 1
+    res = t.apply(prog)
+    fused = [n for n in res.program.nodes if isinstance(n, FusedNode)]
+    assert [n.kernel for n in fused] == ["qk_prologue_v2"]    # C * D = 4096: the v2 key
+    assert fused[0].inputs == ["qF", "kF", "coef_ag", "coef_bg"]
+    outs = {o for n in res.program.nodes for o in ([n.output] if hasattr(n, "output") else [])}
+    assert "k_eff" not in outs and "q_eff" in outs and "Aqk" not in outs
+    assert "Araw" in outs                                      # kkt left staged
+    assert t.match(res.program) == 0
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("lower", [False, True])
 def test_kda_programs_on_gpu(lower):
@@ -36,7 +54,31 @@ def test_kda_programs_on_gpu(lower):
     prog = build_kda_program(B, H, NC, C, D, D ** -0.5)
     if lower:
         prog = LowerPerDimScan(B, H, NC, C, D).apply(prog).program
+        prog = FuseContractionEpilogue(B, H, NC, C, D).apply(prog).program
+        assert any(isinstance(n, FusedNode) and n.kernel.startswith("qk_prologue")
+                   for n in prog.nodes)
     o = StagedExecutor().run(prog, binds)["o"]
+    torch.cuda.synchronize()
+    f = lambda t: t.float().cpu().numpy()
+    ref = orc.kda_forward(f(inp["q"]), f(inp["k"]), f(inp["v"]), f(inp["beta"]),
+                          f(inp["g_in"]), D ** -0.5)
+    assert orc.rel_l2(f(o), ref) < 2e-2
+
+
+@pytest.mark.gpu
+def test_kda_compile_verified_on_gpu():
+    """compile_program on CUDA: the verifier times and checks each proposed transform
+    (per-dim scan, qk_prologue template) and the compiled program still matches the
+    oracle, whichever transforms it kept."""
+    from pto_fuser import Features, StagedExecutor, compile_program
+    inp = make_kda_inputs(B, H, NC, C, D, device="cuda")
+    binds = prepare_kda_bindings(**inp)
+    prog = build_kda_program(B, H, NC, C, D, D ** -0.5)
+    res = compile_program(prog, Features(B, H, NC, C, D), bindings=binds, iters=5, warmup=2)
+    assert res.report.verified
+    assert {r.name for r in res.report.records} >= {"lower-perdim-scan",
+                                                      "fuse-contraction-epilogue"}
+    o = StagedExecutor().run(res.program, binds)["o"]
     torch.cuda.synchronize()
     f = lambda t: t.float().cpu().numpy()
     ref = orc.kda_forward(f(inp["q"]), f(inp["k"]), f(inp["v"]), f(inp["beta"]),
