@@ -166,6 +166,14 @@ PTOF_API int ptof_kkt_inv_exec(void* ws, const void* k, const void* beta, const 
                                float* T_out, int B, int H, int T, int D, int in_dtype,
                                int beta_dtype, int gate_mode, int layout, void* stream);
 
+/* Per-channel-gate chunk_o flash (KDA / GLA): o = tril((q * P)(k * invP)^T, 0) v per
+ * chunk, the score kept on chip. q/k/P/invP [M, C, D], v [M, C, Dv] (f16/bf16/f32),
+ * o [M, C, Dv] fp32. Replaces qkvp_exec / qkvp_exec_v2 (the qkvp_flash_native[_v2]
+ * keys, src/pto_fuser/fused.py:396-441, 570-585). C <= 128, D <= 256. */
+PTOF_API int ptof_qkvp_flash_exec(void* ws, const void* q, const void* k, const void* v,
+                                  const void* P, const void* invP, float* o, int M, int C,
+                                  int D, int Dv, int in_dtype, void* stream);
+
 /* Per-channel-gate intra-chunk score of the chunked linear-attention family (GLA):
  * L = tril((q * P) (k * invP)^T, 0) per chunk, q/k/P/invP [M, C, D] (f16/bf16/f32),
  * L [M, C, C] fp16. Replaces pro_exec / pro_exec_v2 (the qk_prologue[_v2] keys,

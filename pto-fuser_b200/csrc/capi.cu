@@ -342,6 +342,18 @@ int ptof_qk_prologue_exec(void* ws, const void* q, const void* k, const void* P,
   return launch_qk_prologue(in_dtype, q, k, P, invP, L, M, C, D, static_cast<cudaStream_t>(stream));
 }
 
+int ptof_qkvp_flash_exec(void* ws, const void* q, const void* k, const void* v, const void* P,
+                         const void* invP, float* o, int M, int C, int D, int Dv, int in_dtype,
+                         void* stream) {
+  (void)ws;
+  if (M < 1 || C < 1 || C > 128 || D < 1 || D > 256 || Dv < 1)
+    return fail(PTOF_EINVAL, "qkvp_flash shape");
+  if (!dtype_ok(in_dtype)) return fail(PTOF_EINVAL, "qkvp_flash dtype");
+  if (!q || !k || !v || !P || !invP || !o) return fail(PTOF_EINVAL, "qkvp_flash: NULL pointer");
+  return launch_qkvp_flash(in_dtype, q, k, v, P, invP, o, M, C, D, Dv,
+                           static_cast<cudaStream_t>(stream));
+}
+
 int ptof_tri_inv_exec(void* ws, const void* A, int a_dtype, float* T, int M, int C, void* stream) {
   (void)ws;
   if (M < 1 || C < 1 || C > 128) return fail(PTOF_EINVAL, "tri_inv shape M=%d C=%d", M, C);

@@ -64,6 +64,8 @@ int launch_kkt_inv(const ptof_gdn_params& p, int* status, const void* k, const v
                    const float* g, float* Tout, cudaStream_t st);
 int launch_gated_qk(int in_dtype, int beta_dtype, const void* a, const void* b, const float* g,
                     const void* beta, void* L, int M, int C, int D, int causal, cudaStream_t st);
+int launch_qkvp_flash(int in_dtype, const void* q, const void* k, const void* v, const void* P,
+                      const void* invP, float* o, int M, int C, int D, int Dv, cudaStream_t st);
 int launch_qk_prologue(int in_dtype, const void* q, const void* k, const void* P,
                        const void* invP, void* L, int M, int C, int D, cudaStream_t st);
 int launch_tri_inv(int a_dtype, const void* A, float* T, int M, int C, cudaStream_t st);

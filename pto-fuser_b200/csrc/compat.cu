@@ -233,6 +233,46 @@ __global__ void __launch_bounds__(kThreads) qkv_flash_kernel(const TI* q, const 
   }
 }
 
+// --------------------------------------------------------------- qkvp_flash ----
+// Per-channel-gate chunk_o flash, one CTA per chunk m: the decay rides on the
+// operands (q P, k invP, prescaled while staging), then the causal score (j <= i)
+// and its product with v, the score staying in shared memory.
+// q, k, P, invP: [M, C, D]; v: [M, C, Dv]; o: [M, C, Dv] fp32.
+template <typename TI>
+__global__ void __launch_bounds__(kThreads) qkvp_flash_kernel(const TI* q, const TI* k,
+                                                              const TI* v, const TI* P,
+                                                              const TI* invP, float* o, int C,
+                                                              int D, int Dv) {
+  extern __shared__ float sm[];
+  const int m = blockIdx.x;
+  const int ld = D + 1, lds = C + 1;
+  float* sq = sm;
+  float* sk = sq + C * ld;
+  float* ss = sk + C * ld;     // [C][C+1] causal score
+  const int64_t b = static_cast<int64_t>(m) * C * D;
+  for (int idx = threadIdx.x; idx < C * D; idx += kThreads) {
+    const int i = idx / D, d = idx % D;
+    sq[i * ld + d] = ldf(q, b + idx) * ldf(P, b + idx);
+    sk[i * ld + d] = ldf(k, b + idx) * ldf(invP, b + idx);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < C * C; idx += kThreads) {
+    const int i = idx / C, j = idx % C;
+    float s = 0.f;
+    if (j <= i)
+      for (int d = 0; d < D; ++d) s = fmaf(sq[i * ld + d], sk[j * ld + d], s);
+    ss[i * lds + j] = s;
+  }
+  __syncthreads();
+  const int64_t bv = static_cast<int64_t>(m) * C * Dv;
+  for (int idx = threadIdx.x; idx < C * Dv; idx += kThreads) {
+    const int i = idx / Dv, e = idx % Dv;
+    float acc = 0.f;
+    for (int j = 0; j <= i; ++j) acc = fmaf(ss[i * lds + j], ldf(v, bv + j * Dv + e), acc);
+    o[bv + idx] = acc;
+  }
+}
+
 template <typename K>
 cudaError_t prep(K kern, size_t smem) {
   return set_smem_once(kern, static_cast<int>(smem));
@@ -343,6 +383,28 @@ int launch_qkv_flash(int in_dtype, const void* q, const void* k, const void* v, 
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "qkv_flash launch");
+}
+
+int launch_qkvp_flash(int in_dtype, const void* q, const void* k, const void* v, const void* P,
+                      const void* invP, float* o, int M, int C, int D, int Dv, cudaStream_t st) {
+  using namespace compat;
+  const size_t smem = (2 * static_cast<size_t>(C) * (D + 1) + static_cast<size_t>(C) * (C + 1)) *
+                      sizeof(float);
+  if (smem > 227 * 1024) return fail(PTOF_EUNSUPPORTED, "qkvp_flash: C=%d D=%d too large", C, D);
+  cudaError_t e;
+#define PTOF_QKVP(TI)                                                                        \
+  {                                                                                          \
+    auto kern = qkvp_flash_kernel<TI>;                                                       \
+    e = prep(kern, smem);                                                                    \
+    if (e == cudaSuccess)                                                                    \
+      kern<<<M, kThreads, smem, st>>>(static_cast<const TI*>(q), static_cast<const TI*>(k),   \
+                                      static_cast<const TI*>(v), static_cast<const TI*>(P),   \
+                                      static_cast<const TI*>(invP), o, C, D, Dv);             \
+  }
+  if (in_dtype == PTOF_BF16) PTOF_QKVP(__nv_bfloat16) else if (in_dtype == PTOF_F16) PTOF_QKVP(__half) else PTOF_QKVP(float)
+#undef PTOF_QKVP
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "qkvp_flash launch");
 }
 
 int launch_qk_prologue(int in_dtype, const void* q, const void* k, const void* P,

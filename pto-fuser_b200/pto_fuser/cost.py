@@ -90,5 +90,5 @@ class CostModel:
         if n in ("enable-direct-reads", "enable-fused-store"):
             return Prediction(0.0, "read-mode levers have no effect on B200 (torch contraction)")
         if n == "fuse-perdim-chunk-o-flash":
-            return Prediction(0.0, "per-dim score -> output flash kernel not built on B200")
+            return Prediction(0.4, "per-dim masked score never reaches HBM")
         return Prediction(0.0, "unknown transform - no prediction")

@@ -199,6 +199,23 @@ def _prologue_launch(ws, inputs, params) -> List[torch.Tensor]:
     return [L]
 
 
+def _qkvp_launch(ws, inputs, params) -> List[torch.Tensor]:
+    """q, k, v, coef_ag, coef_bg over M = nc * H chunks -> o = tril((q*coef_ag)
+    (k*coef_bg)^T) v [M, C, DV] fp32 (the per-dim chunk_o flash; reference
+    fused.py:414-433)."""
+    q, k, v, ag, bg = inputs
+    C, D = params.get("C", q.shape[-2]), params.get("D", q.shape[-1])
+    DV = params.get("DV", v.shape[-1])
+    M = params["nc"] * params["H"]
+    rs = lambda t, d: _c(t, torch.float16).reshape(M, C, d)
+    q, k, ag, bg, v = rs(q, D), rs(k, D), rs(ag, D), rs(bg, D), rs(v, DV)
+    o = torch.empty(M, C, DV, device=q.device, dtype=torch.float32)
+    nv.check(nv.lib().ptof_qkvp_flash_exec(ws, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                           ag.data_ptr(), bg.data_ptr(), o.data_ptr(), M, C, D,
+                                           DV, nv.F16, nv.stream_handle(q.device)))
+    return [o]
+
+
 _GDN_RUNNERS: Dict[tuple, Any] = {}
 
 
@@ -262,6 +279,12 @@ def default_fused_registry() -> FusedKernelRegistry:
                               "q/k/P/invP [M,C,D], L [M,C,C]")
     for key in ("qk_prologue", "qk_prologue_v2"):
         reg.register(key, _Recipe(_prologue_launch, pro))
+    qkvp = FusedContract(in_slots=["q", "k", "v", "coef_ag", "coef_bg"],
+                         in_dtypes=[f16] * 5, out_names=["o"], out_dtype=f32,
+                         notes="per-dim chunk_o flash o = tril((q*coef_ag)(k*coef_bg)^T) v; "
+                               "q/k/coef [M,C,D], v [M,C,DV], o [M,C,DV] f32")
+    for key in ("qkvp_flash_native", "qkvp_flash_native_v2"):
+        reg.register(key, _Recipe(_qkvp_launch, qkvp))
     reg.register("gdn_chunk_fwd", _Recipe(_gdn_launch, FusedContract(
         in_slots=["q", "k", "v", "g_native", "beta_native"],
         in_dtypes=[torch.bfloat16, torch.bfloat16, torch.bfloat16, f32, torch.bfloat16],

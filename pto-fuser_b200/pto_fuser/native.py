@@ -73,6 +73,7 @@ _SIGNATURES = {
     "ptof_kkt_inv_exec": (_i32, [_vp] * 5 + [_i32] * 8 + [_vp]),
     "ptof_chunk_h_scan_perdim_exec": (_i32, [_vp] * 7 + [_i32] * 8 + [_vp]),
     "ptof_qk_prologue_exec": (_i32, [_vp] * 6 + [_i32] * 4 + [_vp]),
+    "ptof_qkvp_flash_exec": (_i32, [_vp] * 7 + [_i32] * 5 + [_vp]),
     "ptof_tri_inv_exec": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _vp]),
     "ptof_chunk_h_scan_exec": (_i32, [_vp] * 7 + [_i32] * 8 + [_vp]),
     "ptof_qkv_flash_exec": (_i32, [_vp] * 6 + [_i32] * 5 + [_vp]),

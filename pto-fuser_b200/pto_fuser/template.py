@@ -8,8 +8,8 @@ and leaves the rest staged; ``FuseChunkOFlash`` fuses the chunk_o score -> outpu
 chain into one ``qkv_flash_native_v2`` node; ``epilogue_report`` explains each
 contraction's fate. Proven-only: a template exists only where a kernel backs it.
 The per-dim (KDA) chunk_o score is backed by the ``qk_prologue`` kernel
-(``PerDimPrologueTemplate``); the per-dim score -> output flash kernel is not built, so
-``FusePerDimChunkOFlash`` never matches.
+(``PerDimPrologueTemplate``) and its score -> output chain by ``qkvp_flash_native_v2``
+(``FusePerDimChunkOFlash``).
 """
 from __future__ import annotations
 
@@ -259,18 +259,59 @@ class FuseChunkOFlash(Transform):
 
 
 class FusePerDimChunkOFlash(Transform):
-    """Per-dim (KDA / GLA) chunk_o flash: no B200 kernel is built, so never matches."""
+    """Per-dim (KDA) chunk_o score -> output in one ``qkvp_flash_native_v2`` launch: the
+    gated score ``tril((qF coef_ag)(kF coef_bg)^T, 0)`` never reaches HBM (the
+    reference's transform of that name, src/pto_fuser/template.py:335-397). The site is
+    the per-dim prologue unit (as ``PerDimPrologueTemplate`` matches it) whose only
+    consumer is the o_intra ``nij,nje->nie`` contraction; the score einsum, its
+    ``tril -> contiguous`` epilogue and that contraction are replaced, the k-side
+    prescale too when nothing else reads it (the q-side one feeds o_inter)."""
     name = "fuse-perdim-chunk-o-flash"
-    summary = "per-dim chunk_o flash (not built on B200)"
+    summary = "per-dim chunk_o prescale, q k^T, tril, A v -> one qkvp_flash_native_v2"
 
     def __init__(self, B, H, nc, C, D) -> None:
         self.dims = Dims(B, H, nc, C, D)
 
+    def _site(self, program: Program):
+        probe = PerDimPrologueTemplate()
+        for i, n in enumerate(program.nodes):
+            if not isinstance(n, EinsumNode):
+                continue
+            unit = extract_epilogue_unit(program, i)
+            if not probe.matches(program, unit):
+                continue
+            c = _only_consumer(program, unit.boundary_out)
+            if c is None:
+                continue
+            cn = program.nodes[c]
+            if (isinstance(cn, EinsumNode) and cn.equation == "nij,nje->nie"
+                    and cn.inputs[0] == unit.boundary_out):
+                return i, unit, c
+        return None
+
     def match(self, program: Program) -> int:
-        return 0
+        return int(self._site(program) is not None)
 
     def apply(self, program: Program) -> TransformResult:
-        return TransformResult(program, False, 0, "per-dim flash kernel not built on B200")
+        site = self._site(program)
+        if site is None:
+            return TransformResult(program, False, 0, "no per-dim chunk_o score -> output chain")
+        i, unit, c = site
+        o_intra = program.nodes[c]
+        d = self.dims
+        node = FusedNode(kernel="qkvp_flash_native_v2",
+                         inputs=["qF", "kF", o_intra.inputs[1], "coef_ag", "coef_bg"],
+                         outputs=[o_intra.output],
+                         params={"nc": d.nc, "H": d.N, "C": d.C, "D": d.D, "DV": d.D,
+                                 "causal": True},
+                         subsumes=["chunk_o k-side gate mul + Aqk einsum + tril + contiguous + "
+                                   "o_intra A v"])
+        drop = {i, c} | {j for j, _ in unit.epilogue}
+        k_mul = unit.prologue[unit.anchor.inputs[1]][0]
+        if _only_consumer(program, program.nodes[k_mul].output) == i:
+            drop.add(k_mul)
+        return TransformResult(splice(program, drop, min(drop), [node]), True, 1,
+                               "emitted qkvp_flash_native_v2")
 
 
 @dataclass

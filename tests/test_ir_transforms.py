@@ -121,9 +121,9 @@ def test_compile_unverified_partial_lowering():
 def test_policy_and_compile_kda():
     """KDA: the per-dim scan and the epilogue generator (its qk_prologue template)
     apply, the scalar-decay scan and the whole-forward fusion do not (reference
-    tests/test_compile.py:64-70); the per-dim score -> output flash is not built, so
-    the compiled program keeps the prologue score (the reference's compile consumes it
-    in qkvp_flash_native_v2 instead)."""
+    tests/test_compile.py:64-70); the per-dim flash runs before the generator and
+    consumes the score, so the compiled kernel set is the reference's
+    (tests/test_compile.py:91-97)."""
     from pto_fuser.forwards import build_kda_program
     prog = build_kda_program(1, 16, 8, 128, 128, 128 ** -0.5)
     f = Features(1, 16, 8, 128, 128)
@@ -132,7 +132,13 @@ def test_policy_and_compile_kda():
     assert "lower-resident-scan" not in names and "fuse-gdn-forward" not in names
     res = compile_program(prog, f, verify=False)
     ks = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
-    assert ks == {"chunk_h_scan", "qk_prologue_v2"}
+    assert ks == {"chunk_h_scan", "qkvp_flash_native_v2"}
+    # perdim scan + perdim flash (the generator then finds no score; the reference's two
+    # read-mode levers are not proposed on B200)
+    assert [r.name for r in res.report.kept] == ["lower-perdim-scan", "fuse-perdim-chunk-o-flash"]
+    # without the flash, the generator's qk_prologue template takes the score
+    from pto_fuser.template import FusePerDimChunkOFlash
+    assert FusePerDimChunkOFlash(1, 16, 8, 128, 128).match(canonicalize(prog)) == 1
 
 
 @pytest.mark.parametrize("per_dim", [False, True])

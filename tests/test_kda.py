@@ -46,17 +46,19 @@ def test_kda_chunk_o_prologue_template():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("lower", [False, True])
+@pytest.mark.parametrize("lower", ["none", "prologue", "flash"])
 def test_kda_programs_on_gpu(lower):
     from pto_fuser import StagedExecutor
+    from pto_fuser.template import FusePerDimChunkOFlash
     inp = make_kda_inputs(B, H, NC, C, D, device="cuda")
     binds = prepare_kda_bindings(**inp)
     prog = build_kda_program(B, H, NC, C, D, D ** -0.5)
-    if lower:
+    if lower != "none":
         prog = LowerPerDimScan(B, H, NC, C, D).apply(prog).program
-        prog = FuseContractionEpilogue(B, H, NC, C, D).apply(prog).program
-        assert any(isinstance(n, FusedNode) and n.kernel.startswith("qk_prologue")
-                   for n in prog.nodes)
+        t = FuseContractionEpilogue if lower == "prologue" else FusePerDimChunkOFlash
+        prog = t(B, H, NC, C, D).apply(prog).program
+        want = "qk_prologue" if lower == "prologue" else "qkvp_flash_native"
+        assert any(isinstance(n, FusedNode) and n.kernel.startswith(want) for n in prog.nodes)
     o = StagedExecutor().run(prog, binds)["o"]
     torch.cuda.synchronize()
     f = lambda t: t.float().cpu().numpy()
@@ -84,3 +86,23 @@ def test_kda_compile_verified_on_gpu():
     ref = orc.kda_forward(f(inp["q"]), f(inp["k"]), f(inp["v"]), f(inp["beta"]),
                           f(inp["g_in"]), D ** -0.5)
     assert orc.rel_l2(f(o), ref) < 2e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("C_,D_,DV", [(64, 64, 64), (128, 128, 128), (32, 64, 96)])
+def test_qkvp_flash_kernel(C_, D_, DV):
+    """ptof_qkvp_flash_exec against a torch fp32 product on the same fp16 operands."""
+    from pto_fuser.fused import default_fused_registry
+    M = 6
+    g = torch.Generator(device="cuda").manual_seed(C_ + D_)
+    r = lambda *s: torch.randn(*s, device="cuda", generator=g).half()
+    q, k, v = r(M, C_, D_), r(M, C_, D_), r(M, C_, DV)
+    ag = torch.exp(-torch.rand(M, C_, D_, device="cuda", generator=g)).half()
+    bg = (1.0 / ag.float()).half()
+    reg = default_fused_registry()
+    o = reg.run("qkvp_flash_native_v2", [q, k, v, ag, bg],
+                {"nc": M, "H": 1, "C": C_, "D": D_, "DV": DV})[0]
+    s = (q.float() * ag.float()) @ (k.float() * bg.float()).transpose(1, 2)
+    ref = torch.tril(s) @ v.float()
+    torch.cuda.synchronize()
+    assert orc.rel_l2(o.cpu().numpy(), ref.cpu().numpy()) < 1e-4
