@@ -1,9 +1,11 @@
 """Benchmark of the fused chunked Gated DeltaNet forward on B200.
 
 Workload (one "step"): BASELINE config 2 — the full GDN chunk forward, bf16,
-B=4, H=32, T=16384, Dk=Dv=128, C=64 — on every GPU (weak scaling: each rank runs
-its own config-2 batch of 128 independent (batch, head) pairs; no collective on
-the data path). Inputs are synthetic with the benchmark distributions (q, k
+B=4, H=32, T=16384, Dk=Dv=128, C=64 — with its 128 independent (batch, head)
+pairs sharded over the N GPUs (strong scaling: 128/64/32/16 pairs per GPU; no
+collective on the data path). A rank with fewer pairs than it has SMs also splits
+every pair's sequence into segments (the chunk-segment scan) so its SMs stay busy.
+At N > 1 the line also carries `weak_value`: every rank its own whole config-2 batch. Inputs are synthetic with the benchmark distributions (q, k
 L2-normalised N(0,1); v N(0,1); beta = sigmoid(N(0,1)); g = logsigmoid(N(2,1))).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -14,10 +16,10 @@ in HBM (device-timed with CUDA events, max over ranks); `e2e` is the same metric
 through the public API with pinned host buffers and every step's host<->device copies
 inside the timed region (uploads, kernels and downloads pipelined over three streams); `roofline` is the fused kernel's achieved HBM bandwidth on its
 algorithmic bytes against the measured copy peak; `cpu_baseline` is the CPU oracle
-timed on this host on a bounded sample. `--impl reference` times the CPU
-restatement of the reference forward (the reference itself is Ascend/CANN code and
-has no CPU or CUDA path; its fp32 torch oracle is restated in oracle/) with all host
-threads.
+timed on this host on a bounded sample. `--impl reference` times the reference's
+forward on the host cores: its fp32 torch `gdn_reference` chunk loop (the reference's
+device path is Ascend/CANN code with no CPU or CUDA build), restated in
+pto_fuser.forwards.gdn, with all host threads.
 """
 from __future__ import annotations
 
@@ -60,8 +62,8 @@ class ClockSampler:
     """SM clock and throttle-reason sampling (NVML, ~5 ms period) in a background
     thread during the timed region. Reads only; changes no GPU setting."""
 
-    def __init__(self, gpu_index: int, period_s: float = 0.001):
-        self.idx = gpu_index
+    def __init__(self, device, period_s: float = 0.001):
+        self.dev = device
         self.period = period_s
         self.rows = []
         self._stop = threading.Event()
@@ -91,7 +93,7 @@ class ClockSampler:
             import pynvml as nv
             nv.nvmlInit()
             self._nv = nv
-            h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            h, self.ident = _nvml_handle(nv, self.dev)
             mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
             self._sample(h, mx)          # the calls work before the timed region starts
             self.rows.clear()
@@ -120,7 +122,7 @@ class ClockSampler:
         reasons = sorted({n for _, _, r in self.rows for n, b in bits.items() if r & b})
         return {"sm_mhz": statistics.median(r[0] for r in self.rows),
                 "sm_max_mhz": max(r[1] for r in self.rows), "reasons": reasons,
-                "samples": len(self.rows)}
+                "samples": len(self.rows), "gpu": getattr(self, "ident", None)}
 
 
 def _dist():
@@ -131,23 +133,27 @@ def _dist():
 
 
 def cpu_reference(threads: int, heads: int, T: int, D: int, seed: int = 0):
-    """Times the CPU oracle (restated reference forward, fp32 numpy) on `heads`
-    (b, h) pairs of length T. Returns (seconds, sample description)."""
-    import numpy as np
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    from oracle import gdn_oracle as orc
-    rng = np.random.default_rng(seed)
-    q = rng.standard_normal((1, heads, T, D)).astype(np.float32)
-    k = rng.standard_normal((1, heads, T, D)).astype(np.float32)
-    q /= np.linalg.norm(q, axis=-1, keepdims=True)
-    k /= np.linalg.norm(k, axis=-1, keepdims=True)
-    v = rng.standard_normal((1, heads, T, D)).astype(np.float32)
-    beta = (1 / (1 + np.exp(-rng.standard_normal((1, heads, T))))).astype(np.float32)
-    g = (-np.log1p(np.exp(-(rng.standard_normal((1, heads, T)) + 2.0)))).astype(np.float32)
+    """Times the reference forward on the host cores: gdn_reference, the fp32 torch
+    chunk loop of the reference (examples/attention/_gdn_full.py:57-97, one (b, h)
+    pair and one chunk at a time) as restated in pto_fuser.forwards.gdn, on `heads`
+    pairs of length T with the benchmark's input distributions. Returns (seconds,
+    sample description)."""
+    import torch
+    from pto_fuser.forwards.gdn import gdn_reference
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(seed)
+    nc, C = T // 64, 64
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(1, heads, nc, C, D, generator=gen), dim=-1)
+    k = nrm(torch.randn(1, heads, nc, C, D, generator=gen), dim=-1)
+    v = torch.randn(1, heads, nc, C, D, generator=gen)
+    beta = torch.sigmoid(torch.randn(1, heads, nc, C, generator=gen))
+    g = torch.nn.functional.logsigmoid(torch.randn(1, heads, nc, C, generator=gen) + 2.0)
     t0 = time.perf_counter()
-    orc.gdn_forward(q, k, v, beta, g, D ** -0.5, dtype=np.float32)
+    gdn_reference(q, k, v, beta, g, D ** -0.5, return_final_state=True)
     dt = time.perf_counter() - t0
-    return dt, f"{heads} (b,h) pairs x T={T}, D={D}, fp32 numpy oracle, {threads} threads"
+    return dt, (f"{heads} of the (b,h) pairs x T={T}, D={D}: the reference's fp32 torch "
+                f"gdn_reference chunk loop on {threads} host threads")
 
 
 def run_reference(args):
@@ -169,15 +175,47 @@ def run_reference(args):
     tok_s = (B * T) * heads / (B * H) / tsec
     out = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s",
            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": tsec * 1e3, "higher_is_better": True, "scaling": "weak",
+           "ms_per_step": tsec * 1e3, "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "cfg2: GDN chunk forward B4 H32 T16384 D128 C64 (CPU sample)",
+           "config": {"workload": "cfg2: GDN chunk forward B4 H32 T16384 D128 C64 (CPU sample "
+                                  "of the 128 (b,h) pairs, scaled to the whole batch)",
                       "sample_pairs": heads, "T": T, "D": D},
            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
                             "sample": desc},
            "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
+
+
+def _segments_for(pairs: int, T: int, sms: int) -> int:
+    """Local token segments for a rank that holds `pairs` (b, h) pairs of length T.
+
+    The forward is one CTA per pair walking its chunks in order, so a shard with
+    fewer pairs than SMs leaves SMs idle. Splitting every pair's sequence into s
+    segments (the chunk-segment scan: an A run and a B run per segment, then a
+    tensor-core fix-up) runs 2 * pairs * s chains of T / s tokens each; s doubles
+    while those chains still fit on the SMs in one wave. 1 means the plain forward."""
+    s = 1
+    while 2 * pairs * (2 * s) <= sms and T % (128 * 2 * s) == 0:
+        s *= 2
+    return s
+
+
+def _nvml_handle(nv, dev):
+    """The NVML handle of the CUDA device `dev`, found by UUID (else PCI bus id):
+    NVML numbers GPUs in PCI order and ignores CUDA_VISIBLE_DEVICES, so the CUDA
+    ordinal may name another GPU."""
+    import torch
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", "") or "")
+    if uuid:
+        u = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        try:
+            return nv.nvmlDeviceGetHandleByUUID(u), u
+        except Exception:
+            pass
+    bus = "%08X:%02X:%02X.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+    return nv.nvmlDeviceGetHandleByPciBusId(bus), bus
 
 
 def run_ours(args):
@@ -190,16 +228,40 @@ def run_ours(args):
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
     from pto_fuser import GDNChunkForward, make_gdn_inputs
+    from pto_fuser.segment import GDNSegmentScan
+    from pto_fuser.shard import shard_pairs
 
     B, H, T, D = CFG["B"], CFG["H"], CFG["T"], CFG["D"]
-    inp = make_gdn_inputs(B, H, T, D, dtype=torch.bfloat16, device=dev, mu=2.0, seed=1234 + rank)
-    runner = GDNChunkForward(B, H, T, D, D, in_dtype=torch.bfloat16, device=dev)
-    o = torch.empty(B, H, T, D, device=dev, dtype=torch.bfloat16)
-    S = torch.empty(B, H, D, D, device=dev, dtype=torch.float32)
+    # strong scaling: the job's B*H pairs split into contiguous blocks, one per rank
+    p0, p1 = shard_pairs(B * H, world, rank)
+    P = p1 - p0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    segs = _segments_for(P, T, sms) if world > 1 else 1
+    inp = make_gdn_inputs(1, P, T, D, dtype=torch.bfloat16, device=dev, mu=2.0,
+                          seed=1234 + rank)
+    o = torch.empty(1, P, T, D, device=dev, dtype=torch.bfloat16)
+    S = torch.empty(1, P, D, D, device=dev, dtype=torch.float32)
     stream = torch.cuda.current_stream(dev)
+    if segs == 1:
+        runner = GDNChunkForward(1, P, T, D, D, in_dtype=torch.bfloat16, device=dev)
+
+        def forward(q, k, v, beta, g, o_, S_):
+            runner(q, k, v, beta, g, o=o_, final_state=S_)
+        launches = 2   # coefficient pre-pass + fused forward
+        how = "plain fused forward, one CTA per (b,h) pair"
+    else:
+        runner = GDNSegmentScan(P, T, D, segments=segs, device=dev)
+
+        def forward(q, k, v, beta, g, o_, S_):
+            _, Sx = runner(q[0], k[0], v[0], beta[0], g[0], None, o=o_[0])
+            S_.view(P, D, D).copy_(Sx)
+        # A and B runs (2 launches each), seg_scan, seg_fix, the final-state copy
+        launches = 7
+        how = (f"chunk-segment scan inside the GPU: {segs} segments per pair, "
+               f"{2 * P * segs} chains of {T // segs} tokens")
 
     def step():
-        runner(inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"], o=o, final_state=S)
+        forward(inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"], o, S)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -213,7 +275,7 @@ def run_ours(args):
 
     # ---- device-timed, inputs resident (per-launch events give the kernel average) ----
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    with ClockSampler(dev.index) as clk:
+    with ClockSampler(dev) as clk:
         barrier()
         evs[0].record(stream)
         for i in range(args.steps):
@@ -227,7 +289,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    tokens = B * T * world * args.steps
+    tokens = B * T * args.steps          # the whole job's tokens (all ranks together)
     value = tokens / (ms_max / 1e3)
 
     # ---- end to end through the public API: pinned host in, host out ----
@@ -263,7 +325,7 @@ def run_ours(args):
             if i >= 2:
                 stream.wait_event(ev_out[i - 2])   # its outputs' last download is done
             d = dev_in[j]
-            runner(d["q"], d["k"], d["v"], d["beta"], d["g"], o=dev_o[j], final_state=dev_S[j])
+            forward(d["q"], d["k"], d["v"], d["beta"], d["g"], dev_o[j], dev_S[j])
             ev_fw[i].record(stream)
             with torch.cuda.stream(down):
                 down.wait_event(ev_fw[i])
@@ -283,64 +345,93 @@ def run_ours(args):
     t2 = torch.tensor([e0.elapsed_time(e1)], device=dev)
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-    e2e_value = B * T * world * e2e_steps / (float(t2.item()) / 1e3)
+    e2e_value = B * T * e2e_steps / (float(t2.item()) / 1e3)
+    runner.check_status()
 
-    # ---- roofline of the fused kernel (HBM bound, algorithmic bytes) ----
+    # ---- secondary: weak scaling (every rank its own whole config-2 batch) ----
+    weak = None
+    if world > 1:
+        full = make_gdn_inputs(B, H, T, D, dtype=torch.bfloat16, device=dev, mu=2.0,
+                               seed=99 + rank)
+        wr = GDNChunkForward(B, H, T, D, D, in_dtype=torch.bfloat16, device=dev)
+        wo = torch.empty(B, H, T, D, device=dev, dtype=torch.bfloat16)
+        wS = torch.empty(B, H, D, D, device=dev)
+        wstep = lambda: wr(full["q"], full["k"], full["v"], full["beta"], full["g"], o=wo,
+                           final_state=wS)
+        for _ in range(3):
+            wstep()
+        n_w = max(3, min(args.steps, 10))
+        barrier()
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0.record(stream)
+        for _ in range(n_w):
+            wstep()
+        w1.record(stream)
+        barrier()
+        wr.check_status()
+        tw = torch.tensor([w0.elapsed_time(w1)], device=dev)
+        dist.all_reduce(tw, op=dist.ReduceOp.MAX)
+        weak = {"value": B * T * world * n_w / (float(tw.item()) / 1e3), "unit": "tokens/s",
+                "ms_per_step": float(tw.item()) / n_w, "steps": n_w,
+                "workload": "every rank its own config-2 batch (128 pairs per GPU)"}
+        del full, wo, wS
+        wr.close()
+
+    # ---- roofline of one GPU's share (HBM bound, algorithmic bytes) ----
     peak, peak_kind = _peaks()
     kern_ms = sum(per) / len(per)
-    algo = _algo_bytes(B, H, T, D)
+    algo = _algo_bytes(1, P, T, D)
     achieved = algo / (kern_ms / 1e3) / 1e9
-    traffic = _ncu_traffic()
 
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
             threads = os.cpu_count() or 1
-            nh = 16
+            nh = 48
             dt, desc = cpu_reference(threads, nh, T, D)
             cpu = {"value": (B * T) * nh / (B * H) / dt, "unit": "tokens/s", "cores": threads,
                    "kind": "port", "sample": desc}
+        wl = ("cfg2: GDN chunk forward B4 H32 T16384 Dk=Dv=128 C64 bf16, the 128 (b,h) "
+              f"pairs sharded over {world} GPU(s)" if not args.shape else
+              f"custom shape B{B} H{H} T{T} D{D} (profiling case)")
         out = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-               "data": "synthetic",
-               "config": {"workload": ("cfg2: GDN chunk forward B4 H32 T16384 Dk=Dv=128 C64 bf16 "
-                                       "per GPU (weak scaling, 128 (b,h) pairs per GPU)"
-                                       if not args.shape else
-                                       f"custom shape B{B} H{H} T{T} D{D} (profiling case)"),
-                          "B_per_gpu": B, "H": H, "T": T, "D": D, "C": CFG["C"],
-                          "global_batch": B * world, "parallelism": f"(b,h) shards x{world}",
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+               "dtype": "bf16", "data": "synthetic",
+               "config": {"workload": wl, "B": B, "H": H, "T": T, "D": D, "C": CFG["C"],
+                          "pairs_per_gpu": P, "segments_per_pair": segs, "plan": how,
+                          "global_batch": B, "parallelism": f"(b,h) shards x{world}",
                           "l2": f"inputs+outputs {algo / 1e9:.2f} GB per GPU vs 126 MB L2"
-                                + (" (no flush needed)" if algo > 126e6 * 4 else "")},
+                                + (" (no flush needed)" if algo > 126e6 * 4 else
+                                   " (smaller than 4x L2: not a bandwidth figure)")},
                "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                        "d2h_bytes_per_step": d2h},
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                            "frac": achieved / peak, "traffic": traffic,
+                            "frac": achieved / peak,
+                            "traffic": (FWD_DRAM_BYTES_PER_HEAD_TOKEN * P * T
+                                        if segs == 1 and not args.shape else None),
                             "peak_kind": peak_kind,
-                            "kernel": "gdn_coef_kernel + gdn_fwd_tc_kernel (one forward call)",
+                            "kernel": ("gdn_coef_kernel + gdn_fwd_tc_kernel (one forward call)"
+                                       if segs == 1 else "whole segment-scan step"),
                             "algo_bytes_per_launch": algo, "avg_launch_ms": kern_ms,
-                            "tflops": _algo_flops(B, H, T, D) / (kern_ms / 1e3) / 1e12},
+                            "tflops": _algo_flops(1, P, T, D) / (kern_ms / 1e3) / 1e12},
                "cpu_baseline": cpu,
-               "gpu_launches": 2 * args.steps,   # coefficient pre-pass + fused forward
+               "gpu_launches": launches * args.steps,
                "clocks": clk.summary()}
+        if weak is not None:
+            out["weak_value"] = weak
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def _ncu_traffic():
-    """DRAM bytes per launch of the fused kernel from the committed ncu summary
-    (profiles/gdn_fwd_tc_cfg2.md, line 'dram_bytes_per_launch: N'), else None."""
-    p = os.path.join(ROOT, "profiles", "gdn_fwd_tc_cfg2.md")
-    try:
-        with open(p) as f:
-            for line in f:
-                if line.strip().startswith("dram_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+# DRAM bytes (read + write) of one forward per head-token, from an ncu capture of the
+# fused kernel and its coefficient pre-pass on an L2-exceeding small case of config 2
+# (B4 H32 T2048 D128: 208.8 MB read + 48.4 MB written for 262,144 head-tokens; the
+# traffic grows in proportion to the tokens, so it scales to the full launch by the
+# head-tokens processed). The algorithmic figure is 1,034 B per head-token.
+FWD_DRAM_BYTES_PER_HEAD_TOKEN = (208.8e6 + 48.4e6) / (4 * 32 * 2048)
 
 
 def run_configs(args):
@@ -479,7 +570,7 @@ def run_long(args):
         torch.cuda.synchronize(dev)
 
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clk:
+    with ClockSampler(dev) as clk:
         barrier()
         e0.record(stream)
         for _ in range(args.steps):

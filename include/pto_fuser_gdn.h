@@ -220,6 +220,14 @@ PTOF_API int ptof_qkv_flash_exec(void* ws, const void* q, const void* k, const v
  * (B*H records). chunks = 0 turns tracing off. */
 PTOF_API int ptof_gdn_fwd_set_trace(void* ws, void* dev_buf, int chunks);
 
+/* Limit of every bounded device wait of the tensor-core forward launched on this
+ * workspace, in nanoseconds (default 2 s). No counterpart in the reference, whose
+ * kernels have no wait limit. A wait that exceeds it ends the launch early, records
+ * its site in the status word and makes ptof_check_status return PTOF_ETIMEOUT; the
+ * outputs of that launch are then undefined. Lowering it is for fault-path tests
+ * (a limit below the time one chunk takes makes a wait run out on purpose). */
+PTOF_API int ptof_ws_set_wait_limit(void* ws, unsigned long long ns);
+
 /* Reads (and clears) the workspace's device status word after synchronising
  * `stream`: PTOF_OK, or PTOF_ETIMEOUT when a bounded device wait gave up. */
 PTOF_API int ptof_check_status(void* ws, void* stream);

@@ -276,6 +276,14 @@ int ptof_gdn_fwd_set_trace(void* wsv, void* dev_buf, int chunks) {
   return PTOF_OK;
 }
 
+int ptof_ws_set_wait_limit(void* wsv, unsigned long long ns) {
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w || w->kind != kWsGdnFwd) return fail(PTOF_EINVAL, "not a gdn_fwd workspace");
+  if (ns == 0) return fail(PTOF_EINVAL, "wait limit must be positive");
+  w->wait_ns = ns;
+  return PTOF_OK;
+}
+
 int ptof_check_status(void* wsv, void* stream) {
   Workspace* w = static_cast<Workspace*>(wsv);
   if (!w) return fail(PTOF_EINVAL, "null workspace");

@@ -31,6 +31,7 @@ struct Workspace {
   int ex[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // per-kind extra integers
   void* trace = nullptr;         // caller-owned device buffer of stage timestamps
   int trace_chunks = 0;
+  unsigned long long wait_ns = 2000000000ull;  // limit of every bounded device wait
 };
 
 int fail(int code, const char* fmt, ...);

@@ -144,6 +144,7 @@ struct Params {
   int gqa;                         // value heads per query/key head (q, k have H / gqa heads)
   int64_t os_b, os_h, os_t;        // o strides (elements)
   float scale;
+  unsigned long long wait_ns;      // limit of every bounded wait
 };
 
 // Optional stage timestamps (globaltimer, ns) of CTA 0: slot layout per chunk.
@@ -166,12 +167,22 @@ __device__ __forceinline__ void trace_mark(const Params& P, int c, int slot) {
 struct Sync {
   volatile int* abort;
   int* status;
-  // one inlined probe, the bounded loop out of line
+  unsigned long long limit;
+  // one inlined probe, the bounded loop out of line. After an abort every wait
+  // returns false at once: the roles run out their loops without blocking, no new
+  // TMA load is issued, and the teardown drains what is in flight.
   __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, int site) const {
     if (mbar_try_wait(bar, parity)) return true;
-    return mbar_wait(bar, parity, abort, status, site);
+    return mbar_wait(bar, parity, abort, status, site, limit);
   }
 };
+
+// Bounded spin on a phase (teardown drains, not subject to the abort flag).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
+  }
+}
 
 __device__ __forceinline__ float ld_beta(const void* p, int dt, int64_t i) {
   if (dt == PTOF_F32) return static_cast<const float*>(p)[i];
@@ -336,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     }
     return;
   }
-  Sync sy{&abort_flag, P.status};
+  Sync sy{&abort_flag, P.status, P.wait_ns};
 
   if (tid == 0) {
     abort_flag = 0;
@@ -378,9 +389,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     const bool bhtd = (P.layout == PTOF_LAYOUT_BHTD);
     const unsigned char* crec = P.coef + static_cast<int64_t>(bh) * P.mnc * L::MISC_BYTES;
     const int Hg = P.H / P.gqa, hk = h / P.gqa;   // this value head's query/key head
+    int issued = 0;   // chunks whose loads were issued
     for (int c = 0; c < nc; ++c) {
       const int s = c % L::NIN;
-      if (c >= L::NIN) sy.wait(&bars[B_EMPTY0 + s], in_par(c) ^ 1, 1);
+      const bool ok = c < L::NIN || sy.wait(&bars[B_EMPTY0 + s], in_par(c) ^ 1, 1);
+      // after an abort no further load is issued (warp-uniform decision)
+      if (!__all_sync(0xffffffffu, ok && !abort_flag)) break;
+      issued = c + 1;
       unsigned char* st = stage(c);
       const int t0 = c * kC;
       // q, k: heads-outer {D, T, B*Hg} or token-major {D, Hg, tokens}
@@ -400,6 +415,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       }
       __syncwarp();
     }
+    // the loads of the last NIN issued chunks may still be in flight after an abort:
+    // the CTA does not exit (or release its shared memory) before they land
+    if (lane == 0)
+      for (int c = issued > L::NIN ? issued - L::NIN : 0; c < issued; ++c)
+        drain_wait(&bars[B_FULL0 + (c % L::NIN)], in_par(c));
   }
   // ================================================================ MMA ====
   // Three single-thread UMMA issuers, each blocking on its own in-order stream (a
@@ -556,9 +576,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       for (int vb = 0; vb < L::NVB; ++vb)
         tma_load_3d(sm + L::OFF_V + vb * L::V_REGION, &P.mapV, &bars[B_VFULL], vb * 64, y, z);
     };
+    int v_issued = -1;   // last chunk whose V load was issued (drained at exit)
     if (qp == 0) {
       prefetch_tmap(&P.mapV);
       issue_v(0);
+      v_issued = 0;
     }
     // E(c), then R(c - 1): the W^T readout follows its WY UMMAs as closely as the
     // epilogue allows, so the chain of chunk c - 1 starts early
@@ -648,9 +670,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       if (c >= 1) {
         // ================= R(c - 1): W^T readout =================
         const int cp = c - 1;
-        sy.wait(&bars[B_WUFULL], cp & 1, 27);
-        // W^T buffer cp & 1 was last read by the chain UMMA of chunk cp - 2
-        if (cp + 1 < nc && qp == 0) issue_v(cp + 1);   // P1(cp) has read V(cp)
+        const bool wu = sy.wait(&bars[B_WUFULL], cp & 1, 27);
+        // P1(cp) has read V(cp), so the single V buffer takes V(cp + 1); never after an
+        // abort (a V load still in flight would be armed twice)
+        if (cp + 1 < nc && qp == 0 && wu && !abort_flag) {
+          issue_v(cp + 1);
+          v_issued = cp + 1;
+        }
         // the W^T tile was last read by the chain UMMA of chunk cp - 1
         if (cp >= 1) sy.wait(&bars[B_WTFREE], (cp - 1) & 1, 28);
         tc_fence_after();
@@ -680,6 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         }
       }
     }
+    if (qp == 0 && v_issued >= 0) drain_wait(&bars[B_VFULL], v_issued & 1);
   } else if (warp >= 4 && warp < 8) {
     const int pp = tid - 128, q = warp & 3, l = lane;
     unsigned char* s_tp = sm + L::OFF_TP;
@@ -945,9 +972,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   // ============================================================ teardown ====
   if (warp >= 1 && warp <= 3 && lane == 0) {
     // every UMMA has retired before TMEM is released (bounded, even after an abort)
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(&bars[B_DONE], 0) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
-    }
+    drain_wait(&bars[B_DONE], 0);
   }
   __syncthreads();
   tc_fence_after();
@@ -1044,6 +1069,7 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.mnc = (p.T + kChunk - 1) / kChunk;
   P.gqa = p.H / Hg;
   P.scale = p.scale;
+  P.wait_ns = w->wait_ns;
   auto kern = varlen    ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false, true>
               : P.trace ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, true, false>
                         : tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false, false>;

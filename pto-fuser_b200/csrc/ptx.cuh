@@ -33,6 +33,20 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also ORs a predicate over the participating threads: every
+// thread gets the same result, so a loop can leave on it without splitting the group
+// (a group split across a later named barrier would wait forever).
+__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // --------------------------------------------------------------------------
 // mbarrier
 // --------------------------------------------------------------------------
@@ -93,16 +107,20 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Bounded wait on phase `parity` of `bar`. Returns false (and raises the abort
-// flag, recording `site` in *status) when the wait gives up, or immediately when
-// another thread of the CTA already aborted.
+// flag, recording `site` in *status) when the wait gives up after `limit_ns`, or
+// immediately when another thread of the CTA already aborted. The sleep hint never
+// exceeds the limit, so a short limit (a test's) is honoured within a few hints.
 static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                              volatile int* abort_flag, int* status, int site) {
-  if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+                                              volatile int* abort_flag, int* status, int site,
+                                              uint64_t limit_ns = kWaitTimeoutNs) {
+  if (*abort_flag) return false;
+  const uint32_t hint = limit_ns < 100000ull ? static_cast<uint32_t>(limit_ns) : 100000u;
+  if (mbar_try_wait_sleep(bar, parity, hint)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, hint)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       if (status) atomicCAS(status, 0, site);
       return false;

@@ -43,7 +43,8 @@ struct FLayout {
 };
 
 enum FBar { F_FULL0 = 0, F_EMPTY0 = 2, F_TFULL0 = 4, F_TFREE0 = 6, F_XFULL0 = 8, F_XFREE0 = 10,
-            F_COUNT = 12 };
+            F_DONE = 12, F_COUNT = 13 };
+static_assert(F_COUNT * 8 + 8 <= 256, "barrier area");
 
 struct FParams {
   CUtensorMap mapOA, mapO;
@@ -93,9 +94,14 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       prefetch_tmap(&P.mapO);
     }
     int cur = -1, f = 0;   // segment whose X is staged; X fills so far
+    int64_t issued = 0;    // tiles whose loads were issued
     for (int64_t i = 0; i < cnt; ++i) {
       const int s = static_cast<int>(i & 1);
-      if (i >= 2) wait(&bars[F_EMPTY0 + s], static_cast<uint32_t>(((i >> 1) + 1) & 1), 1);
+      // after a wait gave up (here or in another warp) no further load is issued; the
+      // decision is warp-uniform (the X staging below synchronises the warp)
+      bool ok = i < 2 || wait(&bars[F_EMPTY0 + s], static_cast<uint32_t>(((i >> 1) + 1) & 1), 1);
+      if (!__all_sync(0xffffffffu, ok && !abort_flag)) break;
+      issued = i + 1;
       if (lane == 0) {
         const int y = static_cast<int>((t0 + i) * kRows);
         mbar_arrive_expect_tx(&bars[F_FULL0 + s], 2 * L::TILE);
@@ -110,7 +116,9 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       const int u = unit_of(i);
       if (u != cur) {
         const int xb = f & 1;
-        if (f >= 2) wait(&bars[F_XFREE0 + xb], static_cast<uint32_t>(((f - 2) >> 1) & 1), 2);
+        const bool okx =
+            f < 2 || wait(&bars[F_XFREE0 + xb], static_cast<uint32_t>(((f - 2) >> 1) & 1), 2);
+        if (!__all_sync(0xffffffffu, okx)) break;
         // X[k][n] fp32 -> 16-bit, MN-major SW128: n-block n/64, row k, byte 2 (n % 64)
         unsigned char* xs = sm + L::OFF_X + xb * L::XT;
         const float4* xg = reinterpret_cast<const float4*>(P.X + static_cast<int64_t>(u) * D * D);
@@ -130,6 +138,16 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
         ++f;
       }
     }
+    // drain: the CTA must not exit (or release its shared memory) with TMA loads in
+    // flight, so wait (bounded, also after an abort) for the last two tiles' loads
+    if (lane == 0) {
+      for (int64_t i = issued > 2 ? issued - 2 : 0; i < issued; ++i) {
+        const uint64_t t_0 = globaltimer_ns();
+        while (!mbar_try_wait(&bars[F_FULL0 + (i & 1)], static_cast<uint32_t>((i >> 1) & 1)) &&
+               globaltimer_ns() - t_0 < kWaitTimeoutNs) {
+        }
+      }
+    }
   } else if (warp == 5) {
     // ============================== UMMA issuer ===============================
     if (lane == 0) {
@@ -141,11 +159,12 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
         if (u != cur) {
           if (f >= 0) umma_commit(&bars[F_XFREE0 + (f & 1)]);   // old X no longer read
           ++f;
-          wait(&bars[F_XFULL0 + (f & 1)], static_cast<uint32_t>((f >> 1) & 1), 3);
+          if (!wait(&bars[F_XFULL0 + (f & 1)], static_cast<uint32_t>((f >> 1) & 1), 3)) break;
           cur = u;
         }
-        wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 4);
-        if (i >= 2) wait(&bars[F_TFREE0 + b], static_cast<uint32_t>(((i >> 1) + 1) & 1), 5);
+        if (!wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 4)) break;
+        if (i >= 2 && !wait(&bars[F_TFREE0 + b], static_cast<uint32_t>(((i >> 1) + 1) & 1), 5))
+          break;
         tc_fence_after();
         const uint32_t a = smem_u32(sm + L::OFF_OA + s * L::TILE);
         const uint32_t x = smem_u32(sm + L::OFF_X + (f & 1) * L::XT);
@@ -156,13 +175,16 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
         umma_commit(&bars[F_TFULL0 + b]);
       }
       if (f >= 0) umma_commit(&bars[F_XFREE0 + (f & 1)]);
+      umma_commit(&bars[F_DONE]);   // arrives once every UMMA issued above has retired
     }
   } else {
     // =============================== epilogue =================================
     const int r = tid;   // tile row = TMEM lane
     for (int64_t i = 0; i < cnt; ++i) {
       const int s = static_cast<int>(i & 1), b = s;
-      wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 6);   // o^B visible
+      // o^B visible, then the product (after an abort the waits return at once and
+      // the barrier below ends the loop for the whole warpgroup)
+      wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 6);
       wait(&bars[F_TFULL0 + b], static_cast<uint32_t>((i >> 1) & 1), 7);
       tc_fence_after();
       unsigned char* ob = sm + L::OFF_OB + s * L::TILE;
@@ -193,7 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[F_TFREE0 + b]);
       fence_async_smem();
-      named_bar_sync(1, 128);   // the tile is complete in shared memory
+      // the tile is complete in shared memory; the OR over the warpgroup gives every
+      // thread the same answer, so an abort never stores a partial tile
+      if (named_bar_or(1, 128, abort_flag != 0)) break;
       if (tid == 0) {
         const int y = static_cast<int>((t0 + i) * kRows);
 #pragma unroll
@@ -204,6 +228,12 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       }
     }
     if (tid == 0) bulk_wait0();
+  }
+  if (warp == 5 && lane == 0) {
+    // every UMMA has retired before TMEM is released (bounded, also after an abort)
+    const uint64_t t_0 = globaltimer_ns();
+    while (!mbar_try_wait(&bars[F_DONE], 0) && globaltimer_ns() - t_0 < kWaitTimeoutNs) {
+    }
   }
   __syncthreads();
   tc_fence_after();

@@ -96,6 +96,11 @@ class GDNChunkForward:
         """Synchronise and raise if a bounded device wait of the last launch gave up."""
         nv.check(nv.lib().ptof_check_status(self._ws, nv.stream_handle(self.device)))
 
+    def set_wait_limit(self, ns: int) -> None:
+        """Limit of every bounded device wait of later launches, in ns (default 2 s).
+        A launch whose wait runs out ends early; ``check_status`` then raises."""
+        nv.check(nv.lib().ptof_ws_set_wait_limit(self._ws, int(ns)))
+
     def close(self) -> None:
         if getattr(self, "_ws", None):
             nv.lib().ptof_gdn_fwd_teardown(self._ws)

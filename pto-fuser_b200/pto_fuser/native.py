@@ -66,6 +66,7 @@ _SIGNATURES = {
     "ptof_seg_fix_exec": (_i32, [_vp] * 4 + [_i32] * 4 + [_vp]),
     "ptof_check_status": (_i32, [_vp, _vp]),
     "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),
+    "ptof_ws_set_wait_limit": (_i32, [_vp, ctypes.c_ulonglong]),
     "ptof_last_error": (ctypes.c_char_p, []),
     "ptof_ws_setup": (_vp, []),
     "ptof_ws_teardown": (None, [_vp]),

@@ -2,7 +2,9 @@
 segment_scan, ptof_seg_fix_exec against a torch product, and GDNSegmentScan (fused
 forward A / B runs, composition, prefix, output fix-up) against the serial oracle and
 the serial fused forward. The 2-rank NCCL case runs when the box has two GPUs."""
+import datetime
 import os
+import time
 import socket
 
 import numpy as np
@@ -153,8 +155,11 @@ def _nccl_worker(rank, world, port, out_dir):
     from pto_fuser.segment import GDNSegmentScan as Seg, split_tokens as split
     torch.cuda.set_device(rank)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    # a short collective timeout: a rank that fails before the all-gather ends its
+    # peer's wait in a minute instead of NCCL's default ten
     dist.init_process_group("nccl", rank=rank, world_size=world,
-                            device_id=torch.device("cuda", rank))
+                            device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
     try:
         P, T, D = 4, 4096, 128
         inp = mk(1, P, T, D, mu=3.0, s0_std=0.02, seed=21)
@@ -174,8 +179,16 @@ def _nccl_worker(rank, world, port, out_dir):
 def test_segment_scan_two_gpus_nccl(tmp_path):
     import torch.multiprocessing as mp
     world = 2
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
-                       join=True, start_method="spawn")
+    ctx = mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)),
+                             nprocs=world, join=False, start_method="spawn")
+    deadline = time.monotonic() + 240
+    # join with a limit: a failed rank raises here, a stuck one ends the test
+    while not ctx.join(timeout=5):
+        if time.monotonic() > deadline:
+            for p in ctx.processes:
+                if p.is_alive():
+                    p.kill()
+            pytest.fail("2-GPU segment-scan workers did not finish within 240 s")
     P, T, D = 4, 4096, 128
     inp = make_gdn_inputs(1, P, T, D, mu=3.0, s0_std=0.02, seed=21)
     n = lambda k: inp[k][:, :2].float().numpy()
