@@ -280,10 +280,16 @@ PTOF_API const char* ptof_last_error(void);
  *   bit2: A from TMEM; bit3: negate A. M in {64,128}, N%16==0 <= 256, K%32==0 <= 128.
  * selftest_tma: TMA SWIZZLE_128B load of the [64 x 64] bf16 box at column x0,
  *   row y0 of a row-major [rows, cols] bf16 matrix, de-swizzled into out[64*64].
+ * selftest_umma_rate: issue-rate probe. `issuers` threads (1-4) each issue `n`
+ *   back-to-back UMMAs (M=128, N, K=16; A from TMEM if a_tmem) into their own
+ *   accumulator; out (device int64 [3*issuers]) receives per issuer the issue
+ *   cycles, issue-to-completion cycles and one single UMMA's round trip (cycles).
  * `status` is a device int that receives a nonzero code if a bounded wait gave up.
  */
 PTOF_API int ptof_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,
                                 int mode, int* status, void* stream);
+PTOF_API int ptof_selftest_umma_rate(int N, int n, int issuers, int a_tmem, long long* out,
+                                     int* status, void* stream);
 PTOF_API int ptof_selftest_tma(const void* src, int rows, int cols, int x0, int y0, void* out,
                                int* status, void* stream);
 

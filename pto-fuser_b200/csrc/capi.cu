@@ -421,6 +421,16 @@ int ptof_selftest_umma(const float* A, const float* B, float* D, int M, int N, i
   return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "selftest_umma launch");
 }
 
+int ptof_selftest_umma_rate(int N, int n, int issuers, int a_tmem, long long* out, int* status,
+                            void* stream) {
+  if (N < 16 || N > 256 || N % 16 || n < 1 || issuers < 1 || issuers > 4 ||
+      issuers * N > 448 || !out)
+    return fail(PTOF_EINVAL, "selftest_umma_rate N=%d n=%d issuers=%d", N, n, issuers);
+  cudaError_t e = launch_selftest_umma_rate(N, n, issuers, a_tmem, out, status,
+                                            static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "selftest_umma_rate launch");
+}
+
 int ptof_selftest_tma(const void* src, int rows, int cols, int x0, int y0, void* out, int* status,
                       void* stream) {
   CUtensorMap map;

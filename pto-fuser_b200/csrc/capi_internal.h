@@ -78,6 +78,8 @@ int launch_qkv_flash(int in_dtype, const void* q, const void* k, const void* v, 
 
 cudaError_t launch_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,
                                  int mode, int* status, cudaStream_t stream);
+cudaError_t launch_selftest_umma_rate(int N, int n, int issuers, int a_tmem, long long* out,
+                                      int* status, cudaStream_t stream);
 cudaError_t launch_selftest_tma(const CUtensorMap& map, int x0, int y0, void* out, int* status,
                                 cudaStream_t stream);
 

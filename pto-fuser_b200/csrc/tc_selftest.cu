@@ -148,7 +148,82 @@ __global__ void tma_kernel(const __grid_constant__ CUtensorMap map, int x0, int 
   }
 }
 
+// Issue-rate probe: `issuers` threads (lane 0 of warps 0..issuers-1) each issue `n`
+// back-to-back UMMAs (M = 128, N, K = 16 each; A from shared memory or TMEM) into
+// their own accumulator, commit, and wait. Operand contents are irrelevant (zeros).
+// out[3 i + 0..2] = issue cycles, issue-to-completion cycles, and the cycles of one
+// further UMMA issued alone and waited for (its round trip), for issuer i.
+__global__ void __launch_bounds__(128) umma_rate_kernel(int N, int n, int issuers, int a_tmem,
+                                                         long long* out, int* status) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t base = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((base + 1023u) & ~1023u) - base);
+  unsigned char* sA = sm;                       // 128 x 128 bf16
+  unsigned char* sB = sm + 32768;               // 256 x 128 bf16
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sB + 65536);   // 4 x 2 barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 8);
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < (32768 + 65536) / 16; i += 128)
+    reinterpret_cast<uint4*>(sm)[i] = make_uint4(0, 0, 0, 0);
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < 8; ++i) mbar_init(&bar[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp < issuers && lane == 0) {
+    const uint32_t idesc = idesc_f16(128, N, false, false, true);
+    const uint32_t d = tmem + warp * N;          // accumulator of this issuer
+    const uint32_t a_t = tmem + 448;             // TMEM A operand (64 columns)
+    const uint32_t sa = smem_u32(sA), sb = smem_u32(sB);
+    const long long t0 = clock64();
+#pragma unroll 1
+    for (int i = 0; i < n; ++i) {
+      const int ks = i & 7;
+      const uint64_t bd = sdesc_sw128(sb + (ks >> 2) * (N * 128) + (ks & 3) * 32, 16, 1024);
+      if (a_tmem) umma_ts(d, a_t + ks * 8, bd, idesc, 1);
+      else umma_ss(d, sdesc_sw128(sa + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024), bd, idesc, 1);
+    }
+    const long long t1 = clock64();
+    umma_commit(&bar[2 * warp]);
+    mbar_wait(&bar[2 * warp], 0, &abort_flag, status, 300);
+    const long long t2 = clock64();
+    const uint64_t bd = sdesc_sw128(sb, 16, 1024);
+    if (a_tmem) umma_ts(d, a_t, bd, idesc, 1);
+    else umma_ss(d, sdesc_sw128(sa, 16, 1024), bd, idesc, 1);
+    umma_commit(&bar[2 * warp + 1]);
+    mbar_wait(&bar[2 * warp + 1], 0, &abort_flag, status, 301);
+    const long long t3 = clock64();
+    out[3 * warp + 0] = t1 - t0;
+    out[3 * warp + 1] = t2 - t0;
+    out[3 * warp + 2] = t3 - t2;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 }  // namespace selftest
+
+cudaError_t launch_selftest_umma_rate(int N, int n, int issuers, int a_tmem, long long* out,
+                                      int* status, cudaStream_t stream) {
+  const int smem = 32768 + 65536 + 256 + 1024;
+  cudaError_t e = cudaFuncSetAttribute(selftest::umma_rate_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  selftest::umma_rate_kernel<<<1, 128, smem, stream>>>(N, n, issuers, a_tmem, out, status);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,
                                  int mode, int* status, cudaStream_t stream) {

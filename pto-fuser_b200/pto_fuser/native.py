@@ -79,6 +79,7 @@ _SIGNATURES = {
     "ptof_chunk_h_scan_exec": (_i32, [_vp] * 7 + [_i32] * 8 + [_vp]),
     "ptof_qkv_flash_exec": (_i32, [_vp] * 6 + [_i32] * 5 + [_vp]),
     "ptof_selftest_umma": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "ptof_selftest_umma_rate": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     "ptof_selftest_tma": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
 }
 

@@ -1,6 +1,11 @@
-"""Compilation report: one record per proposed transform with the prediction and,
-when verified, the measured frob error, determinism and timing
-(interface of src/pto_fuser/report.py:15-63)."""
+"""What ``compile_program`` did with each proposal.
+
+One ``TransformRecord`` per transform the policy proposed: the cost model's
+prediction, whether the rewrite matched, and (verified compiles) the measured error,
+determinism and replay times that decided it. ``CompilationReport`` collects them.
+Field names follow the reference's report (src/pto_fuser/report.py:15-63), which
+callers read; the text rendering is this package's own.
+"""
 from __future__ import annotations
 
 from dataclasses import dataclass, field
@@ -25,19 +30,28 @@ class TransformRecord:
 
     @property
     def speedup(self) -> Optional[float]:
-        if self.t_base_ms and self.t_cand_ms:
-            return self.t_base_ms / self.t_cand_ms
-        return None
+        """Replay time of the program before the rewrite over the time after it."""
+        if not (self.t_base_ms and self.t_cand_ms):
+            return None
+        return self.t_base_ms / self.t_cand_ms
+
+    @property
+    def outcome(self) -> str:
+        if self.kept:
+            return "kept"
+        return "rejected" if self.attempted else "skipped"
 
     def __str__(self) -> str:
-        verdict = "KEEP" if self.kept else ("drop" if self.matched else "n/a ")
-        pred = f"pred {self.predicted_benefit:+.2f}"
+        parts = [f"{self.outcome:<8}", f"{self.name:<28}",
+                 f"predicted {self.predicted_benefit:+.2f}"]
         if self.speedup is not None:
-            meas = f"{self.t_base_ms:.3f}->{self.t_cand_ms:.3f}ms ({self.speedup:.2f}x)"
-            flags = f"frob={self.frob:.1e} {'det' if self.deterministic else 'NDET'}"
-        else:
-            meas, flags = ("(unverified)" if self.attempted else self.note), ""
-        return f"[{verdict}] {self.name:<26} {pred:<11} {flags:<20} {meas}"
+            parts.append(f"measured {self.t_base_ms:.3f} -> {self.t_cand_ms:.3f} ms "
+                         f"(x{self.speedup:.2f})")
+            parts.append(f"err {self.frob:.1e}")
+            parts.append("deterministic" if self.deterministic else "NOT deterministic")
+        elif self.note:
+            parts.append(f"({self.note})")
+        return "  ".join(parts)
 
 
 @dataclass
@@ -51,6 +65,8 @@ class CompilationReport:
         return [r for r in self.records if r.kept]
 
     def __str__(self) -> str:
-        head = (f"compile report ({'verified' if self.verified else 'unverified'}) "
-                f"- {len(self.kept)}/{len(self.records)} transforms kept")
-        return "\n".join([head] + [str(r) for r in self.records])
+        mode = "measured on the device" if self.verified else "not verified"
+        lines = [f"compilation ({mode}): kept {len(self.kept)} of {len(self.records)} "
+                 f"proposed transforms"]
+        lines += ["  " + str(r) for r in self.records]
+        return "\n".join(lines)
