@@ -90,6 +90,13 @@ class Prediction:
         return self.benefit > 0
 
 
+# the transforms the policy can propose (policy.Policy.candidates)
+_LIBRARY = frozenset({"fuse-gdn-forward", "lower-resident-scan", "lower-perdim-scan",
+                      "fuse-chunk-o-flash", "fuse-perdim-chunk-o-flash",
+                      "fuse-contraction-epilogue", "batch-chunk-intra-score",
+                      "enable-direct-reads", "enable-fused-store"})
+
+
 class CostModel:
     """Fitted predictor over the transform library (see the module docstring)."""
 
@@ -120,6 +127,8 @@ class CostModel:
             v2 = feat.C * feat.D >= 4096
         ln_s = self.predicted_log_speedup(n, feat)
         if ln_s is None:
+            if n not in _LIBRARY:
+                return Prediction(0.0, "unknown transform: no prediction")
             return Prediction(0.05, "not in the calibration table: neutral seed, verifier decides",
                               v2=v2)
         fit = self.fitted(n)
