@@ -281,7 +281,8 @@ PTOF_API const char* ptof_last_error(void);
  * selftest_tma: TMA SWIZZLE_128B load of the [64 x 64] bf16 box at column x0,
  *   row y0 of a row-major [rows, cols] bf16 matrix, de-swizzled into out[64*64].
  * selftest_umma_rate: issue-rate probe. `issuers` threads (1-4) each issue `n`
- *   back-to-back UMMAs (M=128, N, K=16; A from TMEM if a_tmem) into their own
+ *   back-to-back UMMAs (M=128, N, K=16; n a multiple of 8; a_tmem = mode bits: 1 A from
+ *   TMEM, 2 warp-uniform issue, 4 incremented descriptors, 8 unrolled) into their own
  *   accumulator; out (device int64 [3*issuers]) receives per issuer the issue
  *   cycles, issue-to-completion cycles and one single UMMA's round trip (cycles).
  * `status` is a device int that receives a nonzero code if a bounded wait gave up.

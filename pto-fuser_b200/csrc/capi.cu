@@ -423,8 +423,8 @@ int ptof_selftest_umma(const float* A, const float* B, float* D, int M, int N, i
 
 int ptof_selftest_umma_rate(int N, int n, int issuers, int a_tmem, long long* out, int* status,
                             void* stream) {
-  if (N < 16 || N > 256 || N % 16 || n < 1 || issuers < 1 || issuers > 4 ||
-      issuers * N > 448 || !out)
+  if (N < 16 || N > 256 || N % 16 || n < 8 || n % 8 || issuers < 1 || issuers > 4 ||
+      issuers * N > 448 || a_tmem < 0 || a_tmem > 15 || !out)
     return fail(PTOF_EINVAL, "selftest_umma_rate N=%d n=%d issuers=%d", N, n, issuers);
   cudaError_t e = launch_selftest_umma_rate(N, n, issuers, a_tmem, out, status,
                                             static_cast<cudaStream_t>(stream));

@@ -47,6 +47,15 @@ __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t nthreads, boo
   return r != 0;
 }
 
+// One lane of the (fully active) warp is elected; returns true on that lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // --------------------------------------------------------------------------
 // mbarrier
 // --------------------------------------------------------------------------

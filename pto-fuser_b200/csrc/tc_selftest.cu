@@ -9,6 +9,8 @@
 //    software swizzle the kernels use for their own smem tiles matches the hardware.
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -148,13 +150,18 @@ __global__ void tma_kernel(const __grid_constant__ CUtensorMap map, int x0, int 
   }
 }
 
-// Issue-rate probe: `issuers` threads (lane 0 of warps 0..issuers-1) each issue `n`
-// back-to-back UMMAs (M = 128, N, K = 16 each; A from shared memory or TMEM) into
-// their own accumulator, commit, and wait. Operand contents are irrelevant (zeros).
+// Issue-rate probe: `issuers` warps each issue `n` back-to-back UMMAs (M = 128, N,
+// K = 16 each) into their own accumulator, commit, and wait. Operand contents are
+// irrelevant (zeros). MODE bit 0: A from TMEM (else shared memory); bit 1: the whole
+// warp runs the loop and one elected lane issues (else lane 0 alone); bit 2: the
+// descriptors are formed once and advanced by constant increments (else rebuilt per
+// UMMA); bit 3: the 8 K-steps of the loop are unrolled.
 // out[3 i + 0..2] = issue cycles, issue-to-completion cycles, and the cycles of one
 // further UMMA issued alone and waited for (its round trip), for issuer i.
-__global__ void __launch_bounds__(128) umma_rate_kernel(int N, int n, int issuers, int a_tmem,
+template <int MODE>
+__global__ void __launch_bounds__(128) umma_rate_kernel(int N, int n, int issuers,
                                                          long long* out, int* status) {
+  constexpr bool kTmemA = MODE & 1, kUniform = MODE & 2, kIncr = MODE & 4, kUnroll = MODE & 8;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t base = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((base + 1023u) & ~1023u) - base);
@@ -180,32 +187,54 @@ __global__ void __launch_bounds__(128) umma_rate_kernel(int N, int n, int issuer
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp < issuers && lane == 0) {
+  if (warp < issuers && (kUniform || lane == 0)) {
     const uint32_t idesc = idesc_f16(128, N, false, false, true);
     const uint32_t d = tmem + warp * N;          // accumulator of this issuer
     const uint32_t a_t = tmem + 448;             // TMEM A operand (64 columns)
     const uint32_t sa = smem_u32(sA), sb = smem_u32(sB);
+    const uint64_t a0 = sdesc_sw128(sa, 16, 1024), b0 = sdesc_sw128(sb, 16, 1024);
+    const uint32_t bstep = (N * 128) >> 4;       // next 64-wide K block of B
+    const bool leader = kUniform ? elect_one() : true;
+    auto issue = [&](int ks) {
+      uint64_t ad, bd;
+      if (kIncr) {
+        ad = a0 + static_cast<uint64_t>((ks >> 2) * 1024 + (ks & 3) * 2);
+        bd = b0 + static_cast<uint64_t>((ks >> 2) * bstep + (ks & 3) * 2);
+      } else {
+        ad = sdesc_sw128(sa + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+        bd = sdesc_sw128(sb + (ks >> 2) * (N * 128) + (ks & 3) * 32, 16, 1024);
+      }
+      if (leader) {
+        if (kTmemA) umma_ts(d, a_t + ks * 8, bd, idesc, 1);
+        else umma_ss(d, ad, bd, idesc, 1);
+      }
+    };
     const long long t0 = clock64();
+    for (int i = 0; i < n; i += 8) {
+      if (kUnroll) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) issue(ks);
+      } else {
 #pragma unroll 1
-    for (int i = 0; i < n; ++i) {
-      const int ks = i & 7;
-      const uint64_t bd = sdesc_sw128(sb + (ks >> 2) * (N * 128) + (ks & 3) * 32, 16, 1024);
-      if (a_tmem) umma_ts(d, a_t + ks * 8, bd, idesc, 1);
-      else umma_ss(d, sdesc_sw128(sa + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024), bd, idesc, 1);
+        for (int ks = 0; ks < 8; ++ks) issue(ks);
+      }
     }
     const long long t1 = clock64();
-    umma_commit(&bar[2 * warp]);
+    if (leader) umma_commit(&bar[2 * warp]);
     mbar_wait(&bar[2 * warp], 0, &abort_flag, status, 300);
     const long long t2 = clock64();
-    const uint64_t bd = sdesc_sw128(sb, 16, 1024);
-    if (a_tmem) umma_ts(d, a_t, bd, idesc, 1);
-    else umma_ss(d, sdesc_sw128(sa, 16, 1024), bd, idesc, 1);
-    umma_commit(&bar[2 * warp + 1]);
+    if (leader) {
+      if (kTmemA) umma_ts(d, a_t, b0, idesc, 1);
+      else umma_ss(d, a0, b0, idesc, 1);
+      umma_commit(&bar[2 * warp + 1]);
+    }
     mbar_wait(&bar[2 * warp + 1], 0, &abort_flag, status, 301);
     const long long t3 = clock64();
-    out[3 * warp + 0] = t1 - t0;
-    out[3 * warp + 1] = t2 - t0;
-    out[3 * warp + 2] = t3 - t2;
+    if (leader) {
+      out[3 * warp + 0] = t1 - t0;
+      out[3 * warp + 1] = t2 - t0;
+      out[3 * warp + 2] = t3 - t2;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -213,16 +242,30 @@ __global__ void __launch_bounds__(128) umma_rate_kernel(int N, int n, int issuer
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-}  // namespace selftest
-
-cudaError_t launch_selftest_umma_rate(int N, int n, int issuers, int a_tmem, long long* out,
-                                      int* status, cudaStream_t stream) {
+template <int MODE>
+cudaError_t launch_rate(int N, int n, int issuers, long long* out, int* status, cudaStream_t st) {
   const int smem = 32768 + 65536 + 256 + 1024;
-  cudaError_t e = cudaFuncSetAttribute(selftest::umma_rate_kernel,
+  cudaError_t e = cudaFuncSetAttribute(umma_rate_kernel<MODE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  selftest::umma_rate_kernel<<<1, 128, smem, stream>>>(N, n, issuers, a_tmem, out, status);
+  umma_rate_kernel<MODE><<<1, 128, smem, st>>>(N, n, issuers, out, status);
   return cudaGetLastError();
+}
+
+template <int... M>
+cudaError_t launch_rate_mode(int mode, int N, int n, int issuers, long long* out, int* status,
+                             cudaStream_t st, std::integer_sequence<int, M...>) {
+  cudaError_t e = cudaErrorInvalidValue;
+  ((mode == M ? (e = launch_rate<M>(N, n, issuers, out, status, st), 0) : 0), ...);
+  return e;
+}
+
+}  // namespace selftest
+
+cudaError_t launch_selftest_umma_rate(int N, int n, int issuers, int mode, long long* out,
+                                      int* status, cudaStream_t stream) {
+  return selftest::launch_rate_mode(mode, N, n, issuers, out, status, stream,
+                                    std::make_integer_sequence<int, 16>{});
 }
 
 cudaError_t launch_selftest_umma(const float* A, const float* B, float* D, int M, int N, int K,

@@ -11,7 +11,9 @@ that loop on B200:
    captured as a CUDA graph and their replays timed with CUDA events, exactly as a
    verified ``compile_program`` does. Each point is one measured speed-up.
 2. ``fit`` fits, per transform, ``ln(speed-up) = a + b ln(nc) + c ln(N) + d ln(C D)``
-   (least squares with a small ridge; N = B H scan chains, nc chunks) to its points.
+   (least squares with a small ridge; N = B H scan chains, nc chunks) to its points,
+   and records the box of regressor values it saw (predictions do not extrapolate
+   beyond it).
 3. ``main`` writes the points and the coefficients to ``cost_table.json`` beside
    this file, which ``CostModel`` loads: a transform's benefit is its predicted
    ln(speed-up), so ``worth_trying`` means "predicted faster than the program
@@ -39,6 +41,8 @@ GRID: Tuple[Tuple[str, int, int, int, int, int], ...] = (
     ("gdn", 4, 8, 8, 32, 128), ("gdn", 1, 2, 16, 32, 64),
     ("kda", 1, 2, 4, 64, 64), ("kda", 1, 8, 8, 64, 64), ("kda", 2, 8, 16, 64, 64),
     ("kda", 1, 16, 4, 64, 128), ("kda", 1, 4, 16, 32, 64), ("kda", 2, 4, 8, 32, 128),
+    ("gdn", 1, 4, 8, 128, 128), ("gdn", 2, 8, 4, 128, 64),
+    ("kda", 1, 16, 8, 128, 128), ("kda", 1, 4, 4, 128, 64),
 )
 QUICK = GRID[:3] + GRID[7:8] + GRID[11:13]
 
@@ -105,7 +109,10 @@ def fit(points: Sequence[Dict], ridge: float = 1e-2) -> Dict[str, Dict]:
         coef = np.linalg.solve(X.T @ X + reg, X.T @ y)
         resid = float(np.sqrt(np.mean((X @ coef - y) ** 2)))
         out[name] = {"coef": [float(c) for c in coef], "rms_log_residual": resid,
-                     "points": len(pts)}
+                     "points": len(pts),
+                     # the measured box: predictions clamp the regressors to it
+                     "x_min": [float(v) for v in X.min(axis=0)],
+                     "x_max": [float(v) for v in X.max(axis=0)]}
     return out
 
 

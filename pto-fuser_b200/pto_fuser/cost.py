@@ -113,6 +113,9 @@ class CostModel:
         if fit is None:
             return None
         x = design_row(feat.nc, feat.N, feat.C, feat.D)
+        lo, hi = fit.get("x_min"), fit.get("x_max")
+        if lo and hi:      # no extrapolation beyond the measured shapes
+            x = [min(max(v, a), b) for v, a, b in zip(x, lo, hi)]
         return sum(c * v for c, v in zip(fit["coef"], x))
 
     def predict(self, transform_name: str, feat: "Features") -> Prediction:

@@ -90,16 +90,27 @@ def test_templates_and_flash():
     assert ks == {"qkv_flash_native_v2", "kkt_gated_native_v2"}
 
 
+UNCALIBRATED = CostModel(table={})   # every supported transform proposed (neutral seeds)
+
+
 def test_cost_and_policy():
     f = Features(B, H, NC, C, D)
-    cm = CostModel()
+    cm = UNCALIBRATED
     assert cm.predict("fuse-gdn-forward", f).worth_trying
     assert not cm.predict("fuse-gdn-forward", Features(B, H, NC, 32, 128)).worth_trying
     assert not cm.predict("enable-direct-reads", f).worth_trying
     assert not cm.predict("unknown", f).worth_trying
-    names = [p.name for p in Policy().pipeline(canonicalize(_gdn()), f)]
+    names = [p.name for p in Policy(cm).pipeline(canonicalize(_gdn()), f)]
     assert names[0] == "fuse-gdn-forward"
     assert names.index("lower-resident-scan") < names.index("fuse-contraction-epilogue")
+    # the calibrated model (fitted from B200 measurements) still leads with the fused
+    # forward and prunes what measured slower than the program without it (the chunk_o
+    # keys at C = 128)
+    calibrated = [p.name for p in Policy().pipeline(canonicalize(_gdn()), f)]
+    assert calibrated[0] == "fuse-gdn-forward"
+    big = Features(B, H, NC, 128, 128)
+    if CostModel().table is not None:
+        assert not CostModel().predict("fuse-chunk-o-flash", big).worth_trying
     assert f.M == B * H * NC and f.N == B * H and f.T == NC * C
 
 
@@ -113,7 +124,8 @@ def test_compile_unverified_whole_forward():
 def test_compile_unverified_partial_lowering():
     """With the whole-forward fusion not proposed (C=32), the partial fusions fire."""
     prog = build_gdn_program(B, H, NC, 32, D, D ** -0.5)
-    res = compile_program(prog, Features(B, H, NC, 32, D), verify=False)
+    res = compile_program(prog, Features(B, H, NC, 32, D), policy=Policy(UNCALIBRATED),
+                          verify=False)
     ks = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
     assert ks == {"chunk_h_scan", "qkv_flash_native_v2", "kkt_gated_native_v2"}
 
@@ -127,10 +139,11 @@ def test_policy_and_compile_kda():
     from pto_fuser.forwards import build_kda_program
     prog = build_kda_program(1, 16, 8, 128, 128, 128 ** -0.5)
     f = Features(1, 16, 8, 128, 128)
-    names = [p.name for p in Policy().pipeline(canonicalize(prog), f)]
+    pol = Policy(UNCALIBRATED)
+    names = [p.name for p in pol.pipeline(canonicalize(prog), f)]
     assert "lower-perdim-scan" in names and "fuse-contraction-epilogue" in names
     assert "lower-resident-scan" not in names and "fuse-gdn-forward" not in names
-    res = compile_program(prog, f, verify=False)
+    res = compile_program(prog, f, policy=pol, verify=False)
     ks = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
     assert ks == {"chunk_h_scan", "qkvp_flash_native_v2"}
     # perdim scan + perdim flash (the generator then finds no score; the reference's two

@@ -72,11 +72,13 @@ def test_kda_compile_verified_on_gpu():
     """compile_program on CUDA: the verifier times and checks each proposed transform
     (per-dim scan, qk_prologue template) and the compiled program still matches the
     oracle, whichever transforms it kept."""
-    from pto_fuser import Features, StagedExecutor, compile_program
+    from pto_fuser import CostModel, Features, Policy, StagedExecutor, compile_program
     inp = make_kda_inputs(B, H, NC, C, D, device="cuda")
     binds = prepare_kda_bindings(**inp)
     prog = build_kda_program(B, H, NC, C, D, D ** -0.5)
-    res = compile_program(prog, Features(B, H, NC, C, D), bindings=binds, iters=5, warmup=2)
+    # every supported transform proposed (uncalibrated), so the verifier sees them all
+    res = compile_program(prog, Features(B, H, NC, C, D), policy=Policy(CostModel(table={})),
+                          bindings=binds, iters=5, warmup=2)
     assert res.report.verified
     assert {r.name for r in res.report.records} >= {"lower-perdim-scan",
                                                       "fuse-contraction-epilogue"}

@@ -4,7 +4,7 @@ compile driver (mirroring the reference's *_npu.py device tests)."""
 import pytest
 import torch
 
-from pto_fuser import (Features, FusedNode, GraphReplayExecutor, StagedExecutor,
+from pto_fuser import (CostModel, Features, Policy, FusedNode, GraphReplayExecutor, StagedExecutor,
                        compile_program, default_registry, frob_rel, gate_determinism,
                        shared_fused_registry)
 from pto_fuser.forwards import (build_deltanet_program, build_gdn_program, build_kkt_fused_program,
@@ -43,7 +43,9 @@ def test_partial_lowering_runs_compat_kernels():
     """C = 32: the whole-forward kernel does not apply; the resident scan, the
     gated kkt and the chunk_o flash keys run instead."""
     prog, binds, ref = _gdn_case(C=32)
-    res = compile_program(prog, Features(1, 2, 4, 32, 128), verify=False)
+    # every supported transform proposed (uncalibrated policy): this exercises the keys
+    res = compile_program(prog, Features(1, 2, 4, 32, 128), policy=Policy(CostModel(table={})),
+                          verify=False)
     kinds = {n.kernel for n in res.program.nodes if isinstance(n, FusedNode)}
     assert {"chunk_h_scan", "qkv_flash_native_v2"} <= kinds
     out = StagedExecutor().run(res.program, binds)["o"]
