@@ -228,6 +228,13 @@ PTOF_API int ptof_gdn_fwd_set_trace(void* ws, void* dev_buf, int chunks);
  * (a limit below the time one chunk takes makes a wait run out on purpose). */
 PTOF_API int ptof_ws_set_wait_limit(void* ws, unsigned long long ns);
 
+/* Fault-path test hook (no counterpart in the reference): while `on` is nonzero, each
+ * tensor-core forward launched on this workspace first waits on a device barrier that
+ * nothing arrives at, so that wait runs out after the wait limit, the launch ends early
+ * (site 99 in the status word) and ptof_check_status returns PTOF_ETIMEOUT. No trap,
+ * fault or unbounded spin is involved. */
+PTOF_API int ptof_gdn_fwd_inject_stall(void* ws, int on);
+
 /* Reads (and clears) the workspace's device status word after synchronising
  * `stream`: PTOF_OK, or PTOF_ETIMEOUT when a bounded device wait gave up. */
 PTOF_API int ptof_check_status(void* ws, void* stream);

@@ -284,6 +284,13 @@ int ptof_ws_set_wait_limit(void* wsv, unsigned long long ns) {
   return PTOF_OK;
 }
 
+int ptof_gdn_fwd_inject_stall(void* wsv, int on) {
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w || w->kind != kWsGdnFwd) return fail(PTOF_EINVAL, "not a gdn_fwd workspace");
+  w->inject_stall = on ? 1 : 0;
+  return PTOF_OK;
+}
+
 int ptof_check_status(void* wsv, void* stream) {
   Workspace* w = static_cast<Workspace*>(wsv);
   if (!w) return fail(PTOF_EINVAL, "null workspace");

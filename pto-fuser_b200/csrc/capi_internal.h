@@ -32,6 +32,7 @@ struct Workspace {
   void* trace = nullptr;         // caller-owned device buffer of stage timestamps
   int trace_chunks = 0;
   unsigned long long wait_ns = 2000000000ull;  // limit of every bounded device wait
+  int inject_stall = 0;          // test only: make one device wait run out
 };
 
 int fail(int code, const char* fmt, ...);

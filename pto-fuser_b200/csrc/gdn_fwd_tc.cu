@@ -122,7 +122,9 @@ enum Bar {
   B_VFULL, B_WREADY, B_WTFREE,
   B_AREADY0, B_AREADY1, B_TAFREE0, B_TAFREE1,
   B_KQFULL, B_TREADY, B_WUFULL, B_RWFREE, B_VNFREE0, B_VNFREE1, B_SREADY, B_VNFULL,
-  B_VNREADY, B_SFULL, B_OFULL0, B_OFULL1, B_OFULL2, B_OFREE, B_DONE, B_KQFREE, B_O1DONE, B_COUNT
+  B_VNREADY, B_SFULL, B_OFULL0, B_OFULL1, B_OFULL2, B_OFREE, B_DONE, B_KQFREE, B_O1DONE,
+  B_NEVER,   // never arrived at: the injected stall of the fault-path test waits on it
+  B_COUNT
 };
 static_assert(B_COUNT * 8 + 8 <= 512, "barrier area");
 
@@ -145,6 +147,7 @@ struct Params {
   int64_t os_b, os_h, os_t;        // o strides (elements)
   float scale;
   unsigned long long wait_ns;      // limit of every bounded wait
+  int inject_stall;                // test only: the chain waits on B_NEVER before chunk 0
 };
 
 // Optional stage timestamps (globaltimer, ns) of CTA 0: slot layout per chunk.
@@ -422,14 +425,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         drain_wait(&bars[B_FULL0 + (c % L::NIN)], in_par(c));
   }
   // ================================================================ MMA ====
-  // Three single-thread UMMA issuers, each blocking on its own in-order stream (a
-  // commit tracks only the issuing thread's UMMAs, so the streams stay independent):
+  // Three UMMA issuer warps, each blocking on its own in-order stream (a commit
+  // tracks only the issuing thread's UMMAs, so the streams stay independent):
   //   warp 1, chain:  Vn^T = U^T - S^T W^T ; S^T += (Vn^T g) K
   //   warp 2, prep:   [K;Q] K^T ; W^T = K^T T'^T, U^T = V^T T''^T
   //   warp 3, output: O = S^T Q'^T ; O += Vn^T Aqk^T
-  // The UMMA loops are rolled: issue costs ~120 cycles per UMMA anyway, and the
-  // kernel's per-chunk code must fit the SM's instruction cache.
-  else if (warp >= 1 && warp <= 3 && lane == 0) {
+  // The whole warp runs each issue loop (the descriptors are then warp-uniform
+  // values) and one elected lane issues and commits; the K-step loops are unrolled.
+  // Measured on B200 (ptof_selftest_umma_rate): a lone lane in a rolled loop issues
+  // one UMMA per ~120 cycles, a warp-uniform unrolled loop one per ~35-45 cycles, and
+  // the commit-to-wait round trip drops from ~410 to ~280 cycles.
+  else if (warp >= 1 && warp <= 3) {
+    const bool leader = elect_one();
     constexpr uint32_t ID_KQ = idesc_f16(128, kC, false, false, !F16);
     constexpr uint32_t ID_WT = idesc_f16(DK, kC, true, false, !F16);
     constexpr uint32_t ID_UT = idesc_f16(DV, kC, true, false, !F16);
@@ -446,43 +453,56 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       return sdesc_sw128(s_sa + (ks >> 2) * (DV * 128) + (ks & 3) * 32, 16, 1024);
     };
     auto t_vn = [&](int c) { return tmem + ((c & 1) ? L::T_VN1 : L::T_VN0); };
+    auto commit = [&](uint64_t* bar) {
+      if (leader) umma_commit(bar);
+    };
     if (warp == 1) {
+      // fault-path test: a wait on a barrier nothing arrives at runs out, aborts the CTA
+      if (P.inject_stall) sy.wait(&bars[B_NEVER], 0, 99);
       for (int c = 0; c < nc; ++c) {
         sy.wait(&bars[B_SREADY], c & 1, 14);
         sy.wait(&bars[B_WREADY], c & 1, 15);
+        __syncwarp();
         tc_fence_after();
-        trace_mark<TRACE>(P, c, TR_MMA_C1);
-        const uint32_t wt = s_wt;
-#pragma unroll 1
+        if (leader) trace_mark<TRACE>(P, c, TR_MMA_C1);
+        const uint32_t vn = t_vn(c);
+#pragma unroll
         for (int ks = 0; ks < DK / 16; ++ks) {
-          const uint64_t bd = sdesc_sw128(wt + ks * 2048, DK * 128, 1024);
-          if constexpr (L::SA_TMEM) umma_ts(t_vn(c), t_sa + ks * 8, bd, ID_VN, 1);
-          else umma_ss(t_vn(c), a_desc_sa(ks), bd, ID_VN, 1);
+          const uint64_t bd = sdesc_sw128(s_wt + ks * 2048, DK * 128, 1024);
+          if (leader) {
+            if constexpr (L::SA_TMEM) umma_ts(vn, t_sa + ks * 8, bd, ID_VN, 1);
+            else umma_ss(vn, a_desc_sa(ks), bd, ID_VN, 1);
+          }
         }
-        umma_commit(&bars[B_VNFULL]);
-        umma_commit(&bars[B_WTFREE]);
+        commit(&bars[B_VNFULL]);
+        commit(&bars[B_WTFREE]);
         sy.wait(&bars[B_VNREADY], c & 1, 17);
+        __syncwarp();
         tc_fence_after();
-        trace_mark<TRACE>(P, c, TR_MMA_C2);
+        if (leader) trace_mark<TRACE>(P, c, TR_MMA_C2);
         const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
         // fast chunks: gamma is folded into U^T and W^T, so Vn^T itself; slow chunks:
         // the separate Vn^T gamma operand
         const bool fastc = reinterpret_cast<const int*>(misc(c))[L::M_FAST / 4] != 0;
         if constexpr (L::VN_TMEM) {
-          const uint32_t a0 = t_vn(c) + (fastc ? 0 : kC / 2);
-#pragma unroll 1
-          for (int ks = 0; ks < kC / 16; ++ks)
-            umma_ts(t_sm, a0 + ks * 8, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
+          const uint32_t a0 = vn + (fastc ? 0 : kC / 2);
+#pragma unroll
+          for (int ks = 0; ks < kC / 16; ++ks) {
+            const uint64_t bd = sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024);
+            if (leader) umma_ts(t_sm, a0 + ks * 8, bd, ID_S, 1);
+          }
         } else {
           const uint32_t s_vs = fastc ? s_vnt : s_vng;
-#pragma unroll 1
-          for (int ks = 0; ks < kC / 16; ++ks)
-            umma_ss(t_sm, sdesc_sw128(s_vs + ks * 32, 16, 1024),
-                    sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024), ID_S, 1);
+#pragma unroll
+          for (int ks = 0; ks < kC / 16; ++ks) {
+            const uint64_t ad = sdesc_sw128(s_vs + ks * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024);
+            if (leader) umma_ss(t_sm, ad, bd, ID_S, 1);
+          }
         }
-        umma_commit(&bars[B_SFULL]);
-        umma_commit(&bars[B_EMPTY0 + (c % L::NIN)]);
-        if (L::VN_TMEM) umma_commit(&bars[B_VNFREE0 + (c & 1)]);
+        commit(&bars[B_SFULL]);
+        commit(&bars[B_EMPTY0 + (c % L::NIN)]);
+        if (L::VN_TMEM) commit(&bars[B_VNFREE0 + (c & 1)]);
       }
     } else if (warp == 3) {
       for (int c = 0; c < nc; ++c) {
@@ -490,28 +510,35 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         // Q' of slow chunks is written before A(c) is handed over, long before W^T(c)
         sy.wait(&bars[B_WREADY], c & 1, 42);
         if (c >= 1) sy.wait(&bars[B_OFREE], (c - 1) & 1, 16);
+        __syncwarp();
         tc_fence_after();
         const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
-#pragma unroll 1
+#pragma unroll
         for (int ks = 0; ks < DK / 16; ++ks) {
           const uint64_t bd =
               sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + kC * 128 + (ks & 3) * 32, 16, 1024);
-          if constexpr (L::SA_TMEM) umma_ts(t_o, t_sa + ks * 8, bd, ID_O1, ks > 0);
-          else umma_ss(t_o, a_desc_sa(ks), bd, ID_O1, ks > 0);
+          if (leader) {
+            if constexpr (L::SA_TMEM) umma_ts(t_o, t_sa + ks * 8, bd, ID_O1, ks > 0);
+            else umma_ss(t_o, a_desc_sa(ks), bd, ID_O1, ks > 0);
+          }
         }
-        umma_commit(&bars[B_O1DONE]);   // the bf16 S^T copy may be overwritten after this
+        commit(&bars[B_O1DONE]);   // the bf16 S^T copy may be overwritten after this
         sy.wait(&bars[B_VNREADY], c & 1, 41);
+        __syncwarp();
         tc_fence_after();
         const uint32_t aq = smem_u32(aqk(c));
-#pragma unroll 1
+        const uint32_t vn = t_vn(c);
+#pragma unroll
         for (int ks = 0; ks < kC / 16; ++ks) {
           const uint64_t bd = sdesc_sw128(aq + ks * 32, 16, 1024);
-          if constexpr (L::VN_TMEM) umma_ts(t_o, t_vn(c) + ks * 8, bd, ID_O2, 1);
-          else umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024), bd, ID_O2, 1);
+          if (leader) {
+            if constexpr (L::VN_TMEM) umma_ts(t_o, vn + ks * 8, bd, ID_O2, 1);
+            else umma_ss(t_o, sdesc_sw128(s_vnt + ks * 32, 16, 1024), bd, ID_O2, 1);
+          }
         }
-        umma_commit(&bars[B_OFULL0 + (c % 3)]);
-        umma_commit(&bars[B_EMPTY0 + (c % L::NIN)]);
-        if (L::VN_TMEM) umma_commit(&bars[B_VNFREE0 + (c & 1)]);
+        commit(&bars[B_OFULL0 + (c % 3)]);
+        commit(&bars[B_EMPTY0 + (c % L::NIN)]);
+        if (L::VN_TMEM) commit(&bars[B_VNFREE0 + (c & 1)]);
       }
     } else {
       // P0(c) = [K;Q] K^T -> KQ, then P1(c - 1) = (W^T, U^T) of the previous chunk:
@@ -520,14 +547,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
         if (c < nc) {
           sy.wait(&bars[B_FULL0 + (c % L::NIN)], in_par(c), 10);
           if (c >= 1) sy.wait(&bars[B_KQFREE], (c - 1) & 1, 11);
+          __syncwarp();
           tc_fence_after();
           const uint32_t kq = smem_u32(stage(c) + L::OFF_KQ);
-#pragma unroll 1
+#pragma unroll
           for (int ks = 0; ks < DK / 16; ++ks) {
-            const uint32_t a = kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32;
-            umma_ss(t_kq, sdesc_sw128(a, 16, 1024), sdesc_sw128(a, 16, 1024), ID_KQ, ks > 0);
+            const uint64_t d = sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32, 16, 1024);
+            if (leader) umma_ss(t_kq, d, d, ID_KQ, ks > 0);
           }
-          umma_commit(&bars[B_KQFULL]);
+          commit(&bars[B_KQFULL]);
         }
         if (c >= 1) {
           const int cp = c - 1;
@@ -535,22 +563,27 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
           sy.wait(&bars[B_VFULL], cp & 1, 18);
           if (cp >= 2) sy.wait(&bars[B_VNFREE0 + (cp & 1)], ((cp >> 1) + 1) & 1, 19);
           if (cp >= 1) sy.wait(&bars[B_RWFREE], (cp - 1) & 1, 9);
+          __syncwarp();
           tc_fence_after();
           const uint32_t kq = smem_u32(stage(cp) + L::OFF_KQ);
           const uint32_t vt = smem_u32(sm + L::OFF_V);
           const uint32_t t_u = t_vn(cp);
-#pragma unroll 1
+#pragma unroll
           for (int ks = 0; ks < kC / 16; ++ks) {
-            umma_ss(t_rw, sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024),
-                    sdesc_sw128(s_tp + ks * 32, 16, 1024), ID_WT, ks > 0);
-            umma_ss(t_u, sdesc_sw128(vt + ks * 2048, L::V_REGION, 1024),
-                    sdesc_sw128(s_tpp + ks * 32, 16, 1024), ID_UT, ks > 0);
+            const uint64_t ka = sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024);
+            const uint64_t tb = sdesc_sw128(s_tp + ks * 32, 16, 1024);
+            const uint64_t va = sdesc_sw128(vt + ks * 2048, L::V_REGION, 1024);
+            const uint64_t ub = sdesc_sw128(s_tpp + ks * 32, 16, 1024);
+            if (leader) {
+              umma_ss(t_rw, ka, tb, ID_WT, ks > 0);
+              umma_ss(t_u, va, ub, ID_UT, ks > 0);
+            }
           }
-          umma_commit(&bars[B_WUFULL]);
+          commit(&bars[B_WUFULL]);
         }
       }
     }
-    umma_commit(&bars[B_DONE]);
+    commit(&bars[B_DONE]);
   }
   // =============================================================== PREP ====
   // Two warpgroups, each one chunk at a time, handing chunks over through mbarriers:
@@ -1070,6 +1103,7 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.gqa = p.H / Hg;
   P.scale = p.scale;
   P.wait_ns = w->wait_ns;
+  P.inject_stall = w->inject_stall;
   auto kern = varlen    ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false, true>
               : P.trace ? tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, true, false>
                         : tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false, false>;

@@ -67,6 +67,7 @@ _SIGNATURES = {
     "ptof_check_status": (_i32, [_vp, _vp]),
     "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),
     "ptof_ws_set_wait_limit": (_i32, [_vp, ctypes.c_ulonglong]),
+    "ptof_gdn_fwd_inject_stall": (_i32, [_vp, _i32]),
     "ptof_last_error": (ctypes.c_char_p, []),
     "ptof_ws_setup": (_vp, []),
     "ptof_ws_teardown": (None, [_vp]),

@@ -3,8 +3,9 @@ runs out ends the launch early with an error status the host reads, and the same
 workspace keeps working afterwards.
 
 Every wait in the tensor-core forward is bounded (default 2 s). Here the limit is set
-to one microsecond, below the time the first chunk's loads and prep take, so some
-wait of the launch gives up on purpose: the kernel raises its CTA abort flag, every
+to 200 microseconds and the test hook ptof_gdn_fwd_inject_stall makes the chain warp
+first wait on a barrier that nothing arrives at, so that wait gives up on purpose
+(site 99): the kernel raises its CTA abort flag, every
 role runs out its loop without blocking, no further TMA load is issued, the loads and
 UMMAs still in flight are drained and TMEM is released. Nothing traps, faults or
 spins without a limit. The host then sees PTOF_ETIMEOUT from ptof_check_status (a
@@ -30,14 +31,16 @@ def test_short_wait_limit_times_out_then_workspace_recovers():
     clean.check_status()
 
     run = GDNChunkForward(B, H, T, D, D)
-    run.set_wait_limit(1000)            # 1 us: a wait of the first chunk runs out
+    run.set_wait_limit(200_000)         # 200 us
+    nv.check(nv.lib().ptof_gdn_fwd_inject_stall(run._ws, 1))
     run(*args)
     with pytest.raises(RuntimeError) as ei:
         run.check_status()
     assert isinstance(ei.value, nv.NativeError) and ei.value.code == nv.ETIMEOUT
-    assert "gave up at site" in str(ei.value)
+    assert "gave up at site 99" in str(ei.value)
 
     # the context is usable and the status word was cleared by the read
+    nv.check(nv.lib().ptof_gdn_fwd_inject_stall(run._ws, 0))
     run.set_wait_limit(2_000_000_000)
     o, S = run(*args)
     run.check_status()
