@@ -84,7 +84,7 @@ class FusedKernelRegistry:
     def kernel(self, key: str, params: dict, device=None) -> FusedKernel:
         if key not in self._recipes:
             raise KeyError(f"no fused kernel registered under {key!r}")
-        dev = torch.device(device) if device is not None else torch.device(
+        dev = nv.cuda_device(device) if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
         ck = (key, dev)
         if ck not in self._cache:

@@ -29,7 +29,7 @@ class GDNChunkForward:
                  in_dtype=torch.bfloat16, beta_dtype=None, out_dtype=None,
                  gate: str = "raw", layout: str = "bhtd", scale: Optional[float] = None,
                  chunk: int = 64, device=None) -> None:
-        self.device = torch.device(device) if device is not None else torch.device(
+        self.device = nv.cuda_device(device) if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
         beta_dtype = beta_dtype or in_dtype
         out_dtype = out_dtype or in_dtype
@@ -153,7 +153,7 @@ class GDNChunkForwardVarlen:
     def __init__(self, N: int, H: int, Hg: int, T_total: int, max_len: int, Dk: int,
                  Dv: int, *, in_dtype=torch.bfloat16, beta_dtype=None, out_dtype=None,
                  gate: str = "raw", scale: Optional[float] = None, device=None) -> None:
-        self.device = torch.device(device) if device is not None else torch.device(
+        self.device = nv.cuda_device(device) if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
         beta_dtype = beta_dtype or in_dtype
         out_dtype = out_dtype or in_dtype

@@ -137,5 +137,14 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def cuda_device(device) -> torch.device:
+    """``device`` as a torch.device with an explicit index ("cuda" -> the current
+    CUDA device), so it compares equal to the devices of tensors allocated on it."""
+    d = torch.device(device)
+    if d.type == "cuda" and d.index is None:
+        d = torch.device("cuda", torch.cuda.current_device())
+    return d
+
+
 def stream_handle(device: Optional[torch.device] = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream

@@ -134,7 +134,7 @@ class GDNSegmentScan:
         self.gate = gate
         self.scale = D ** -0.5 if scale is None else float(scale)
         if forward is None:
-            self.device = torch.device(device) if device is not None else torch.device(
+            self.device = nv.cuda_device(device) if device is not None else torch.device(
                 "cuda", torch.cuda.current_device())
             mk = lambda: GDNChunkForward(pairs, segments, self.Tseg, D, D, in_dtype=in_dtype,
                                          beta_dtype=self.beta_dtype, out_dtype=self.out_dtype,
