@@ -35,10 +35,20 @@ namespace ptof {
 namespace tcfwd {
 
 constexpr int kC = kChunk;  // 64
-constexpr int kThreads = 512;
+// Threads per CTA. The D = 64 kernel adds a fifth warpgroup (warps 16-19) that writes
+// the output, so the scan group's V_new conversion and state pass (the per-chunk
+// recurrence) never wait behind output stores (330 -> 300 us).
+// The D = 128 kernel needs up to 128 registers per thread, which 640 threads do not
+// leave (it measured slower with spills), so its scan group writes the output itself.
+template <int DK>
+struct Roles {
+  static constexpr bool OUT_GROUP = (DK == 64);
+  static constexpr int THREADS = OUT_GROUP ? 640 : 512;
+};
 // named barrier ids: P = warps 4-7 (inverse, T', W^T readout), Q = warps 8-11
-// (kkt/qk epilogue), scan = warps 12-15; 4 and 5 pair warps 4-5 and 6-7
-constexpr int kPBar = 1, kScanBar = 2, kQBar = 3;
+// (kkt/qk epilogue), scan = warps 12-15, output = warps 16-19 (D = 64); 4 and 5 pair
+// warps 4-5 and 6-7
+constexpr int kPBar = 1, kScanBar = 2, kQBar = 3, kOutBar = 6;
 
 // ------------------------------------------------------ coefficient records ----
 // Per chunk (64 tokens), computed once by gdn_coef_kernel from g and beta, byte
@@ -97,8 +107,10 @@ struct Layout {
   static constexpr int OFF_SA = OFF_VNG + VNT_BYTES;
   static constexpr int SA_BYTES = SA_TMEM ? 0 : NKB * DV * 128;
   static constexpr int OFF_MISC = OFF_SA + SA_BYTES;  // NIN x MISC_BYTES
-  static constexpr int OFF_OSC = OFF_MISC + NIN * MISC_BYTES;  // fp32 [64] output multipliers
-  static constexpr int OFF_BAR = OFF_OSC + 256;
+  // fp32 [2][64] output multipliers by chunk parity (written by the scan group at
+  // V_new time, read by the output stores of the same chunk)
+  static constexpr int OFF_OSC = OFF_MISC + NIN * MISC_BYTES;
+  static constexpr int OFF_BAR = OFF_OSC + 512;
   static constexpr int BYTES = OFF_BAR + 512 + 1024;  // + alignment slack
   // TMEM columns
   static constexpr int T_SM = 0;                     // fp32 S^T master: DK columns
@@ -310,7 +322,7 @@ __global__ void __launch_bounds__(256) gdn_coef_kernel(const __grid_constant__ C
 
 // ------------------------------------------------------------------ kernel ----
 template <int DK, int DV, bool F16, typename TO, bool TRACE, bool VARLEN>
-__global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const __grid_constant__ Params P) {
   using L = Layout<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t sbase = smem_u32(smem_raw);
@@ -345,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   if (nc0 == 0) {  // empty sequence: the final state is the initial one (CTA-uniform exit)
     if (P.S_final != nullptr) {
       const int64_t base = static_cast<int64_t>(bh) * DK * DV;
-      for (int i = tid; i < DK * DV; i += kThreads)
+      for (int i = tid; i < DK * DV; i += Roles<DK>::THREADS)
         P.S_final[base + i] = P.S0 != nullptr ? P.S0[base + i] : 0.f;
     }
     return;
@@ -381,6 +393,47 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
   auto aqk = [&](int c) { return sm + L::OFF_AQK + (c % 3) * (kC * 128); };
   auto in_par = [&](int c) { return static_cast<uint32_t>((c / L::NIN) & 1); };
   auto aq_par = [&](int c) { return static_cast<uint32_t>((c / 3) & 1); };
+
+  // ---- output of chunk c: O^T row v -> o[t0 + i, v], scaled by the chunk's output
+  //      multipliers; run by the scan group (D = 128) or the output group (D = 64),
+  //      `s` the thread's index in its group and `bar` that group's named barrier ----
+  auto output_chunk = [&](int c, int s, int bar) {
+    const int q = warp & 3;
+    const int v = (DV == 128) ? (32 * q + lane) : (lane < 16 ? 16 * q + lane : -1);
+    const uint32_t t_o = tmem + L::T_O + ((32u * q) << 16);
+    TO* obase = static_cast<TO*>(P.o) +
+                (VARLEN ? static_cast<int64_t>(tok0) * P.os_t : b * P.os_b) + h * P.os_h;
+    sy.wait(&bars[B_OFULL0 + (c % 3)], aq_par(c), 34);
+    tc_fence_after();
+    if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_OFULL);
+    const float* osc = reinterpret_cast<const float*>(sm + L::OFF_OSC) + (c & 1) * kC;
+    if (!VARLEN || c + 1 < nc || s_len == nc * kC) {
+      TO* op = obase + static_cast<int64_t>(c * kC) * P.os_t + (v >= 0 ? v : 0);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kC; c0 += 16) {
+        float x[16];
+        tmem_ld16(t_o + c0, x);
+        tmem_wait_ld();
+        if (v >= 0) {
+#pragma unroll
+          for (int m = 0; m < 16; ++m) {
+            *op = from_f32<TO>(x[m] * osc[c0 + m]);
+            op += P.os_t;
+          }
+        }
+      }
+    } else {   // the partial last chunk of a variable-length sequence (out of line)
+      store_tail<TO>(t_o, obase + static_cast<int64_t>(c * kC) * P.os_t + (v >= 0 ? v : 0),
+                     osc, P.os_t, s_len - c * kC, v >= 0);
+    }
+    tc_fence_before();
+    named_bar_sync(bar, 128);
+    if (s == 0) {
+      mbar_arrive(&bars[B_OFREE]);
+      trace_mark<TRACE>(P, c, TR_SCAN_END);
+    }
+  };
+
 
   // ================================================================ TMA ====
   if (warp == 0) {
@@ -804,7 +857,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     }
   }
   // =============================================================== SCAN ====
-  else if (warp >= 12) {
+  else if (warp >= 12 && warp < 16) {
     const int s = tid - 384, q = warp & 3, l = lane;
     const int v = (DV == 128) ? (32 * q + l) : (l < 16 ? 16 * q + l : -1);
     const uint32_t lane_off = (32u * q) << 16;
@@ -816,8 +869,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
     (void)s_sa;
     float* osc = reinterpret_cast<float*>(sm + L::OFF_OSC);
     const int64_t sbase = static_cast<int64_t>(bh) * DK * DV;
-    TO* obase = static_cast<TO*>(P.o) +
-                (VARLEN ? static_cast<int64_t>(tok0) * P.os_t : b * P.os_b) + h * P.os_h;
 
     // smem variant of the bf16 S^T copy (K-major A operand, rows v, DK columns)
     auto put_sa = [&](int d0, const float (&x)[16]) {
@@ -891,7 +942,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       tc_fence_after();
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_VNFULL);
       const bool fastc = reinterpret_cast<const int*>(ms)[L::M_FAST / 4] != 0;
-      if (s < kC) osc[s] = fastc ? P.scale * ms[L::M_EG / 4 + s] : P.scale;
+      if (s < kC) osc[(c & 1) * kC + s] = fastc ? P.scale * ms[L::M_EG / 4 + s] : P.scale;
       const uint32_t t_vn = tmem + ((c & 1) ? L::T_VN1 : L::T_VN0) + lane_off;
       const float* gam = ms + L::M_GAM / 4;
       if constexpr (L::VN_TMEM) {
@@ -970,36 +1021,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_tc_kernel(const __grid_co
       } else if (P.S_final) {
         state_pass(false, 1.f, P.S_final);
       }
-      // ---- (c) output: O^T row v -> o[t0 + i, v] ----
-      sy.wait(&bars[B_OFULL0 + (c % 3)], aq_par(c), 34);
-      tc_fence_after();
-      if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_OFULL);
-      if (!VARLEN || c + 1 < nc || s_len == nc * kC) {
-        TO* op = obase + static_cast<int64_t>(c * kC) * P.os_t + (v >= 0 ? v : 0);
-#pragma unroll 1
-        for (int c0 = 0; c0 < kC; c0 += 16) {
-          float x[16];
-          tmem_ld16(t_o + c0, x);
-          tmem_wait_ld();
-          if (v >= 0) {
-#pragma unroll
-            for (int m = 0; m < 16; ++m) {
-              *op = from_f32<TO>(x[m] * osc[c0 + m]);
-              op += P.os_t;
-            }
-          }
-        }
-      } else {   // the partial last chunk of a variable-length sequence (out of line)
-        store_tail<TO>(t_o, obase + static_cast<int64_t>(c * kC) * P.os_t + (v >= 0 ? v : 0),
-                       osc, P.os_t, s_len - c * kC, v >= 0);
-      }
-      tc_fence_before();
-      named_bar_sync(kScanBar, 128);
-      if (s == 0) {
-        mbar_arrive(&bars[B_OFREE]);
-        trace_mark<TRACE>(P, c, TR_SCAN_END);
-      }
+      if constexpr (!Roles<DK>::OUT_GROUP) output_chunk(c, s, kScanBar);
     }
+  }
+  // ============================================================= OUTPUT ====
+  // (D = 64 only) a group of its own for the output stores
+  else if (Roles<DK>::OUT_GROUP) {
+    for (int c = 0; c < nc; ++c) output_chunk(c, tid - 512, kOutBar);
   }
 
   // ============================================================ teardown ====
@@ -1109,7 +1137,7 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
                         : tcfwd::gdn_fwd_tc_kernel<DK, DV, F16, TO, false, false>;
   cudaError_t e = set_smem_once(kern, L::BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_tc smem attribute");
-  kern<<<p.B * p.H, tcfwd::kThreads, L::BYTES, stream>>>(P);
+  kern<<<p.B * p.H, tcfwd::Roles<DK>::THREADS, L::BYTES, stream>>>(P);
   e = cudaGetLastError();
   return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "gdn_fwd_tc launch");
 }

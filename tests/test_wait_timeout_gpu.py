@@ -4,8 +4,9 @@ workspace keeps working afterwards.
 
 Every wait in the tensor-core forward is bounded (default 2 s). Here the limit is set
 to 200 microseconds and the test hook ptof_gdn_fwd_inject_stall makes the chain warp
-first wait on a barrier that nothing arrives at, so that wait gives up on purpose
-(site 99): the kernel raises its CTA abort flag, every
+first wait on a barrier that nothing arrives at, so waits give up on purpose (that
+one, site 99, or another wait of the stalled CTA that runs out first): the kernel
+raises its CTA abort flag, every
 role runs out its loop without blocking, no further TMA load is issued, the loads and
 UMMAs still in flight are drained and TMEM is released. Nothing traps, faults or
 spins without a limit. The host then sees PTOF_ETIMEOUT from ptof_check_status (a
@@ -37,7 +38,7 @@ def test_short_wait_limit_times_out_then_workspace_recovers():
     with pytest.raises(RuntimeError) as ei:
         run.check_status()
     assert isinstance(ei.value, nv.NativeError) and ei.value.code == nv.ETIMEOUT
-    assert "gave up at site 99" in str(ei.value)
+    assert "gave up at site" in str(ei.value)
 
     # the context is usable and the status word was cleared by the read
     nv.check(nv.lib().ptof_gdn_fwd_inject_stall(run._ws, 0))
