@@ -428,10 +428,10 @@ def run_ours(args):
 
 # DRAM bytes (read + write) of one forward per head-token, from an ncu capture of the
 # fused kernel and its coefficient pre-pass on an L2-exceeding small case of config 2
-# (B4 H32 T2048 D128: 208.8 MB read + 48.4 MB written for 262,144 head-tokens; the
+# (B4 H32 T2048 D128: 210.4 MB read + 45.7 MB written for 262,144 head-tokens; the
 # traffic grows in proportion to the tokens, so it scales to the full launch by the
 # head-tokens processed). The algorithmic figure is 1,034 B per head-token.
-FWD_DRAM_BYTES_PER_HEAD_TOKEN = (208.8e6 + 48.4e6) / (4 * 32 * 2048)
+FWD_DRAM_BYTES_PER_HEAD_TOKEN = (208.8e6 + 1.58e6 + 45.7e6) / (4 * 32 * 2048)
 
 
 def run_configs(args):
