@@ -220,6 +220,24 @@ PTOF_API int ptof_qkv_flash_exec(void* ws, const void* q, const void* k, const v
  * (B*H records). chunks = 0 turns tracing off. */
 PTOF_API int ptof_gdn_fwd_set_trace(void* ws, void* dev_buf, int chunks);
 
+/* Fused chunked KDA forward (Kimi Delta Attention: a per-key-dimension gate) on the
+ * tensor cores. Replaces the reference's lowered KDA chain — the per-dim scan
+ * (scan_exec with perdim_decay, kernels/scan_fused.h:136-180) plus the per-dim
+ * prologue/flash keys (pro_exec / qkvp_exec, kernels/prologue_fused.h:1-28,
+ * kernels/qkv_prologue_fused.h:1-24) — with one operand pre-pass and one fused
+ * launch, the semantics of kda_reference (examples/attention/_kda_full.py:38-77)
+ * plus an optional initial state and the final state.
+ * q, k, v bf16 [B,H,T,64]; beta [B,H,T] (beta_dtype); g fp32 [B,H,T,64] per-token
+ * per-dimension log decay; S0 / S_final fp32 [B,H,64,64] (optional); o [B,H,T,64]
+ * (out_dtype). Requires C = 64, Dk = Dv = 64, in_dtype BF16, layout BHTD. The gate is
+ * applied to the operands (k e^g, q e^g, k e^-g with g the chunk-local cumsum), as in
+ * the reference's factorised form: a chunk whose total decay in some dimension
+ * exceeds about 80 overflows the bf16 operands, as it does there. */
+PTOF_API void* ptof_kda_fwd_setup(const ptof_gdn_params* p);
+PTOF_API int ptof_kda_fwd_exec(void* ws, const void* q, const void* k, const void* v,
+                               const void* beta, const float* g, const float* S0, void* o,
+                               float* S_final, void* stream);
+
 /* Limit of every bounded device wait of the tensor-core forward launched on this
  * workspace, in nanoseconds (default 2 s). No counterpart in the reference, whose
  * kernels have no wait limit. A wait that exceeds it ends the launch early, records

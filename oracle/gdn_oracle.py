@@ -285,22 +285,26 @@ def linear_attention_recurrent(q, k, v, gates, dtype=np.float64):
     return o
 
 
-def kda_forward(q, k, v, beta, g_in, scale, C=C_DEFAULT, dtype=np.float64):
+def kda_forward(q, k, v, beta, g_in, scale, C=C_DEFAULT, dtype=np.float64, S0=None,
+                return_state=False):
     """Kimi Delta Attention forward (per-dimension gate), restating kda_reference
     (examples/attention/_kda_full.py:38-77): per chunk, g = per-dimension cumsum,
     A = tril((k e^g)(k e^-g)^T beta_i, -1), T = (I+A)^-1, W = T (k e^g beta), U = T (v beta),
     vc = U - W S, S = e^{g_tot} S + (k e^{g_tot-g})^T vc,
     o = scale ((q e^g) S_c + tril((q e^g)(k e^-g)^T, 0) vc).
-    q, k, v [B,H,nc,C,D]; beta [B,H,nc,C]; g_in [B,H,nc,C,D] -> o [B,H,nc,C,D]."""
+    q, k, v [B,H,nc,C,D]; beta [B,H,nc,C]; g_in [B,H,nc,C,D] -> o [B,H,nc,C,D].
+    S0 [B,H,D,D] optional initial state (the reference starts from 0); with
+    return_state the final state [B,H,D,D] is returned as well."""
     q, k, v, beta, g_in = (_f(x, dtype) for x in (q, k, v, beta, g_in))
     B, H, nc, Cc, D = q.shape
     g = np.cumsum(g_in, axis=3)
     eye = np.eye(Cc, dtype=dtype)
     causal = np.tril(np.ones((Cc, Cc), dtype=dtype))
     o = np.zeros((B, H, nc, Cc, D), dtype=dtype)
+    fin = np.zeros((B, H, D, D), dtype=dtype)
     for b in range(B):
         for h in range(H):
-            S = np.zeros((D, D), dtype=dtype)
+            S = np.zeros((D, D), dtype=dtype) if S0 is None else _f(S0[b, h], dtype).copy()
             for c in range(nc):
                 gc, kc, bc = g[b, h, c], k[b, h, c], beta[b, h, c]
                 ka, kb = kc * np.exp(gc), kc * np.exp(-gc)
@@ -313,7 +317,8 @@ def kda_forward(q, k, v, beta, g_in, scale, C=C_DEFAULT, dtype=np.float64):
                 o[b, h, c] = qe @ S + ((qe @ kb.T) * causal) @ vc
                 g_tot = gc[-1]
                 S = np.exp(g_tot)[:, None] * S + (kc * np.exp(g_tot[None, :] - gc)).T @ vc
-    return o * scale
+            fin[b, h] = S
+    return (o * scale, fin) if return_state else o * scale
 
 
 def segment_scan(A, B, X0, dtype=np.float64):

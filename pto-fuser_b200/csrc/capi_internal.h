@@ -18,7 +18,7 @@ inline cudaError_t set_smem_once(K kern, int bytes) {
   return set_smem_attr_once(reinterpret_cast<const void*>(kern), bytes);
 }
 
-enum WsKind { kWsGdnFwd = 1, kWsGeneric = 2 };
+enum WsKind { kWsGdnFwd = 1, kWsGeneric = 2, kWsKdaFwd = 3 };
 
 // Library-owned per-setup state.
 struct Workspace {

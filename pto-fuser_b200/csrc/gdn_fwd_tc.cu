@@ -68,7 +68,7 @@ constexpr int BYTES = 1808;  // multiple of 16 (bulk copies)
 }  // namespace coef
 
 // ------------------------------------------------------------------ layout ----
-template <int DK, int DV>
+template <int DK, int DV, bool KDA = false>
 struct Layout {
   static constexpr int NKB = DK / 64;               // 64-wide d blocks
   static constexpr int NVB = DV / 64;
@@ -78,7 +78,9 @@ struct Layout {
   static constexpr bool VN_TMEM = SA_TMEM;
   // input ring (4 stages): [K | Q] per 64-wide d block, then the per-token arrays
   static constexpr int NIN = 4;
-  static constexpr int KQ_REGION = 2 * kC * 128;     // K rows 0-63 | Q rows 64-127, 16 KB
+  // K rows 0-63 | Q rows 64-127 (16 KB); KDA adds K e^{-g} in rows 128-191 (24 KB)
+  static constexpr int KQ_REGION = (KDA ? 3 : 2) * kC * 128;
+  static constexpr int OFF_K2 = 2 * kC * 128;        // KDA: K e^{-g} within a region
   static constexpr int OFF_KQ = 0;                   // within an input stage
   static constexpr int IN_STAGE = NKB * KQ_REGION;
   // per-chunk coefficient records written by gdn_coef_kernel (one per input stage,
@@ -109,7 +111,10 @@ struct Layout {
   static constexpr int OFF_MISC = OFF_SA + SA_BYTES;  // NIN x MISC_BYTES
   // fp32 [2][64] output multipliers by chunk parity (written by the scan group at
   // V_new time, read by the output stores of the same chunk)
-  static constexpr int OFF_OSC = OFF_MISC + NIN * MISC_BYTES;
+  // KDA: per input stage, the per-dimension decay e^{g_tot} of the PREVIOUS chunk
+  static constexpr int EGLD_BYTES = KDA ? DK * 4 : 0;
+  static constexpr int OFF_EGLD = OFF_MISC + NIN * MISC_BYTES;
+  static constexpr int OFF_OSC = OFF_EGLD + NIN * EGLD_BYTES;
   static constexpr int OFF_BAR = OFF_OSC + 512;
   static constexpr int BYTES = OFF_BAR + 512 + 1024;  // + alignment slack
   // TMEM columns
@@ -142,6 +147,8 @@ static_assert(B_COUNT * 8 + 8 <= 512, "barrier area");
 
 struct Params {
   CUtensorMap mapK, mapQ, mapV;   // 3D maps, box = 64 d x 64 tokens
+  CUtensorMap mapK2;               // KDA: k e^{-g} (mapK, mapQ: k e^{g}, q e^{g})
+  const float* egl;                // KDA: [B*H][nc + 1][DK] e^{g_tot} of chunk c - 1 at c
   const unsigned char* coef;       // [B*H][nc] coefficient records (gdn_coef_kernel)
   const float* S0;                 // [B,H,DK,DV] or null
   void* o;
@@ -321,9 +328,9 @@ __global__ void __launch_bounds__(256) gdn_coef_kernel(const __grid_constant__ C
 }
 
 // ------------------------------------------------------------------ kernel ----
-template <int DK, int DV, bool F16, typename TO, bool TRACE, bool VARLEN>
+template <int DK, int DV, bool F16, typename TO, bool TRACE, bool VARLEN, bool KDA = false>
 __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const __grid_constant__ Params P) {
-  using L = Layout<DK, DV>;
+  using L = Layout<DK, DV, KDA>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t sbase = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((sbase + 1023u) & ~1023u) - sbase);
@@ -458,15 +465,23 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
       const int y = bhtd ? t0 : hk;
       const int z = bhtd ? b * Hg + hk : static_cast<int>(tok0 + t0);
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bars[B_FULL0 + s], 2 * DK * kC * 2 + L::MISC_BYTES);
+        mbar_arrive_expect_tx(&bars[B_FULL0 + s], (KDA ? 3 : 2) * DK * kC * 2 + L::MISC_BYTES +
+                                                      L::EGLD_BYTES);
 #pragma unroll
         for (int kb = 0; kb < L::NKB; ++kb) {
           tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION, &P.mapK, &bars[B_FULL0 + s], kb * 64, y, z);
           tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION + kC * 128, &P.mapQ, &bars[B_FULL0 + s],
                       kb * 64, y, z);
+          if constexpr (KDA)
+            tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION + L::OFF_K2, &P.mapK2,
+                        &bars[B_FULL0 + s], kb * 64, y, z);
         }
         bulk_load(misc(c), crec + static_cast<int64_t>(c) * L::MISC_BYTES, L::MISC_BYTES,
                   &bars[B_FULL0 + s]);
+        if constexpr (KDA)
+          bulk_load(sm + L::OFF_EGLD + s * L::EGLD_BYTES,
+                    P.egl + (static_cast<int64_t>(bh) * (P.nc + 1) + c) * DK, L::EGLD_BYTES,
+                    &bars[B_FULL0 + s]);
         trace_mark<TRACE>(P, c, TR_TMA_ISSUE);
       }
       __syncwarp();
@@ -541,7 +556,7 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
           const uint32_t a0 = vn + (fastc ? 0 : kC / 2);
 #pragma unroll
           for (int ks = 0; ks < kC / 16; ++ks) {
-            const uint64_t bd = sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024);
+            const uint64_t bd = sdesc_sw128(kq + (KDA ? L::OFF_K2 : 0) + ks * 2048, L::KQ_REGION, 1024);
             if (leader) umma_ts(t_sm, a0 + ks * 8, bd, ID_S, 1);
           }
         } else {
@@ -549,7 +564,9 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
 #pragma unroll
           for (int ks = 0; ks < kC / 16; ++ks) {
             const uint64_t ad = sdesc_sw128(s_vs + ks * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(kq + ks * 2048, L::KQ_REGION, 1024);
+            // KDA: the state update reads K e^-g (the per-dimension e^{g_tot} is applied
+            // to the whole state afterwards, in the state pass)
+            const uint64_t bd = sdesc_sw128(kq + (KDA ? L::OFF_K2 : 0) + ks * 2048, L::KQ_REGION, 1024);
             if (leader) umma_ss(t_sm, ad, bd, ID_S, 1);
           }
         }
@@ -606,7 +623,11 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
 #pragma unroll
           for (int ks = 0; ks < DK / 16; ++ks) {
             const uint64_t d = sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + (ks & 3) * 32, 16, 1024);
-            if (leader) umma_ss(t_kq, d, d, ID_KQ, ks > 0);
+            // KDA: [K e^g; Q e^g] (K e^-g)^T, the gate on the operands
+            const uint64_t db = KDA ? sdesc_sw128(kq + (ks >> 2) * L::KQ_REGION + L::OFF_K2 +
+                                                  (ks & 3) * 32, 16, 1024)
+                                    : d;
+            if (leader) umma_ss(t_kq, d, db, ID_KQ, ks > 0);
           }
           commit(&bars[B_KQFULL]);
         }
@@ -883,7 +904,9 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
     };
     // One pass over S^T row v in 32-column pieces: optional source (global S0),
     // bf16 copy -> SA, then master <- scale * value.
-    auto state_pass = [&](bool from_global, float mult, float* final_out) {
+    // KDA: `md` (per key dimension d) scales the state first: the per-dimension decay
+    // of the chunk just completed, so S_{c+1} = e^{g_tot} (S_c + (K e^-g)^T V_new)
+    auto state_pass = [&](bool from_global, float mult, float* final_out, const float* md) {
 #pragma unroll 1
       for (int d0 = 0; d0 < DK; d0 += 32) {
         float x[32];
@@ -898,6 +921,12 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
           tmem_wait_ld();
 #pragma unroll
           for (int m = 0; m < 16; ++m) { x[m] = a[m]; x[16 + m] = bq[m]; }
+        }
+        if constexpr (KDA) {
+          if (md != nullptr) {
+#pragma unroll
+            for (int m = 0; m < 32; ++m) x[m] *= md[d0 + m];
+          }
         }
         if (final_out) {
           if (v >= 0) {
@@ -927,9 +956,10 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
       tmem_wait_st();
     };
 
-    // initial state: S^T <- S0 (or 0), master pre-scaled by e^{g_last} of chunk 0
     sy.wait(&bars[B_FULL0], 0, 30);  // chunk 0
-    state_pass(true, misc(0)[L::M_EGL / 4], nullptr);
+    // initial state: S^T <- S0 (or 0); GDN pre-scales the master by e^{g_last} of chunk
+    // 0, KDA applies its per-dimension decays after each chunk's update instead
+    state_pass(true, KDA ? 1.f : misc(0)[L::M_EGL / 4], nullptr, nullptr);
     tc_fence_before();
     if (!L::SA_TMEM) fence_async_smem();
     named_bar_sync(kScanBar, 128);
@@ -1010,7 +1040,11 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
       if (s == 0) trace_mark<TRACE>(P, c, TR_SCAN_SFULL);
       if (c + 1 < nc) {
         sy.wait(&bars[B_FULL0 + ((c + 1) % L::NIN)], in_par(c + 1), 33);
-        state_pass(false, misc(c + 1)[L::M_EGL / 4], nullptr);
+        // KDA: the stage of chunk c + 1 carries the decay of chunk c
+        state_pass(false, KDA ? 1.f : misc(c + 1)[L::M_EGL / 4], nullptr,
+                   KDA ? reinterpret_cast<const float*>(sm + L::OFF_EGLD +
+                                                        ((c + 1) % L::NIN) * L::EGLD_BYTES)
+                       : nullptr);
         tc_fence_before();
         if (!L::SA_TMEM) fence_async_smem();
         named_bar_sync(kScanBar, 128);
@@ -1019,7 +1053,8 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
           trace_mark<TRACE>(P, c, TR_SCAN_SREADY);
         }
       } else if (P.S_final) {
-        state_pass(false, 1.f, P.S_final);
+        state_pass(false, 1.f, P.S_final,
+                   KDA ? P.egl + (static_cast<int64_t>(bh) * (P.nc + 1) + nc) * DK : nullptr);
       }
       if constexpr (!Roles<DK>::OUT_GROUP) output_chunk(c, s, kScanBar);
     }
@@ -1047,6 +1082,43 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
     rec[1] = globaltimer_ns();
     rec[2] = smid;
   }
+}
+
+// ---------------------------------------------------------- KDA operand pre-pass ----
+// Kimi Delta Attention gates every key dimension separately (per-token log decay g
+// [B,H,T,DK]), so the gate cannot ride on the scores as GDN's does: it rides on the
+// operands, as in the reference's factorised chunk form (examples/attention/
+// _kda_full.py:38-77, the prologue keys of kernels/qkv_prologue_fused.h). Per chunk
+// with G the chunk-local cumsum, this pass writes K e^G, Q e^G, K e^-G (bf16) and the
+// chunk's per-dimension decay e^{G_last} into slot c + 1 of `egl` (slot 0 = 1), so
+// the fused kernel runs the ungated GDN chain on these operands. One thread per key
+// dimension walks the 64 tokens of one chunk (coalesced rows of g, k, q).
+struct KdaPrepParams {
+  const __nv_bfloat16 *q, *k;
+  const float* g;
+  __nv_bfloat16 *q1, *k1, *k2;
+  float* egl;
+  int nc, T;
+};
+template <int DK>
+__global__ void __launch_bounds__(DK) kda_prep_kernel(const __grid_constant__ KdaPrepParams P) {
+  const int d = threadIdx.x;
+  const int bh = blockIdx.x / P.nc, c = blockIdx.x % P.nc;
+  const int64_t base = (static_cast<int64_t>(bh) * P.T + static_cast<int64_t>(c) * kC) * DK + d;
+  float G = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < kC; ++i) {
+    const int64_t e = base + static_cast<int64_t>(i) * DK;
+    G += P.g[e];
+    const float up = __expf(G), dn = __expf(-G);
+    const float kk = __bfloat162float(P.k[e]), qq = __bfloat162float(P.q[e]);
+    P.k1[e] = __float2bfloat16_rn(kk * up);
+    P.q1[e] = __float2bfloat16_rn(qq * up);
+    P.k2[e] = __float2bfloat16_rn(kk * dn);
+  }
+  float* eg = P.egl + static_cast<int64_t>(bh) * (P.nc + 1) * DK;
+  eg[static_cast<int64_t>(c + 1) * DK + d] = __expf(G);
+  if (c == 0) eg[d] = 1.f;
 }
 
 }  // namespace tcfwd
@@ -1161,6 +1233,97 @@ int launch_d(Workspace* w, const void* q, const void* k, const void* v, const vo
   return launch_o<DK, DV, false>(w, q, k, v, beta, g, S0, o, S_final, cu, st);
 }
 
+// KDA forward (DK = DV = 64, bf16 q/k/v, heads-outer): the operand pre-pass, then the
+// fused kernel's ungated chain on K e^g, Q e^g, K e^-g with the per-dimension decay
+// applied to the state after every chunk.
+struct KdaScratch {
+  size_t coef, egl, ops, total;   // byte offsets of the parts and the total
+};
+KdaScratch kda_scratch_layout(const ptof_gdn_params& p) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  const size_t nc = p.T / kChunk, pairs = static_cast<size_t>(p.B) * p.H;
+  KdaScratch s;
+  s.coef = 0;
+  s.egl = up(pairs * nc * tcfwd::coef::BYTES);
+  s.ops = s.egl + up(pairs * (nc + 1) * 64 * sizeof(float));
+  const size_t one = up(pairs * p.T * 64 * 2);   // one bf16 operand [B,H,T,64]
+  s.total = s.ops + 3 * one;
+  return s;
+}
+
+template <typename TO>
+int launch_kda_t(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
+                 const float* g, const float* S0, void* o, float* S_final, cudaStream_t stream) {
+  constexpr int D = 64;
+  using L = tcfwd::Layout<D, D, true>;
+  const ptof_gdn_params& p = w->p;
+  const KdaScratch ks = kda_scratch_layout(p);
+  if (!w->d_scratch || w->scratch_bytes < ks.total)
+    return fail(PTOF_EINVAL, "kda_fwd workspace has no scratch buffer");
+  unsigned char* base = static_cast<unsigned char*>(w->d_scratch);
+  const int nc = p.T / kChunk;
+  const size_t one = (ks.total - ks.ops) / 3;
+  auto* k1 = reinterpret_cast<__nv_bfloat16*>(base + ks.ops);
+  auto* q1 = reinterpret_cast<__nv_bfloat16*>(base + ks.ops + one);
+  auto* k2 = reinterpret_cast<__nv_bfloat16*>(base + ks.ops + 2 * one);
+  float* egl = reinterpret_cast<float*>(base + ks.egl);
+  {
+    tcfwd::CoefParams C;   // beta only: the gate is on the operands
+    C.g = nullptr;
+    C.beta = beta;
+    C.out = base + ks.coef;
+    C.B = p.B; C.H = p.H; C.nc = nc;
+    C.gate_mode = PTOF_GATE_NONE;
+    C.beta_dtype = p.beta_dtype;
+    C.allow_fast = 1;
+    const Strides3 sg = make_strides3(PTOF_LAYOUT_BHTD, p.H, p.T);
+    C.gs_b = sg.b; C.gs_h = sg.h; C.gs_t = sg.t;
+    C.cu_seqlens = nullptr;
+    C.T = p.T;
+    const int64_t chunks = static_cast<int64_t>(p.B) * p.H * nc;
+    tcfwd::gdn_coef_kernel<<<static_cast<unsigned>((chunks + 7) / 8), 256, 0, stream>>>(C);
+    tcfwd::KdaPrepParams K;
+    K.q = static_cast<const __nv_bfloat16*>(q);
+    K.k = static_cast<const __nv_bfloat16*>(k);
+    K.g = g;
+    K.q1 = q1; K.k1 = k1; K.k2 = k2;
+    K.egl = egl;
+    K.nc = nc; K.T = p.T;
+    tcfwd::kda_prep_kernel<D><<<static_cast<unsigned>(chunks), D, 0, stream>>>(K);
+  }
+  const int64_t tokens = static_cast<int64_t>(p.B) * p.T;
+  tcfwd::Params P;
+  int rc = make_act_map(&P.mapK, k1, PTOF_BF16, p, D, p.H, tokens);
+  if (!rc) rc = make_act_map(&P.mapQ, q1, PTOF_BF16, p, D, p.H, tokens);
+  if (!rc) rc = make_act_map(&P.mapK2, k2, PTOF_BF16, p, D, p.H, tokens);
+  if (!rc) rc = make_act_map(&P.mapV, v, PTOF_BF16, p, D, p.H, tokens);
+  if (rc) return rc;
+  P.egl = egl;
+  P.coef = base + ks.coef;
+  P.S0 = S0;
+  P.o = o;
+  P.S_final = S_final;
+  P.status = w->d_status;
+  P.trace = nullptr;
+  P.trace_chunks = 0;
+  P.B = p.B; P.H = p.H; P.T = p.T; P.nc = nc;
+  P.layout = PTOF_LAYOUT_BHTD;
+  const Strides4 so = make_strides4(PTOF_LAYOUT_BHTD, p.H, p.T, D);
+  P.os_b = so.b; P.os_h = so.h; P.os_t = so.t;
+  P.cu_seqlens = nullptr;
+  P.mnc = nc;
+  P.gqa = 1;
+  P.scale = p.scale;
+  P.wait_ns = w->wait_ns;
+  P.inject_stall = 0;
+  auto kern = tcfwd::gdn_fwd_tc_kernel<D, D, false, TO, false, false, true>;
+  cudaError_t e = set_smem_once(kern, L::BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "kda_fwd smem attribute");
+  kern<<<p.B * p.H, tcfwd::Roles<D>::THREADS, L::BYTES, stream>>>(P);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "kda_fwd launch");
+}
+
 }  // namespace
 
 size_t gdn_fwd_tc_scratch_bytes(const ptof_gdn_params& p) {
@@ -1250,4 +1413,45 @@ extern "C" int ptof_gdn_fwd_exec_noalloc(const ptof_gdn_params* p, const void* q
   w.scratch_bytes = static_cast<size_t>(kNoAllocMaxChunks) * tcfwd::coef::BYTES;
   return launch_gdn_fwd_tc(&w, q, k, v, beta, g, S0, o, S_final, nullptr,
                            static_cast<cudaStream_t>(stream));
+}
+
+// ----------------------------------------------------------------- KDA C ABI ----
+extern "C" void* ptof_kda_fwd_setup(const ptof_gdn_params* p) {
+  using namespace ptof;
+  if (!p) {
+    fail(PTOF_EINVAL, "null params");
+    return nullptr;
+  }
+  if (validate_gdn(*p) != PTOF_OK) return nullptr;
+  if (p->Dk != 64 || p->Dv != 64 || p->in_dtype != PTOF_BF16 || p->layout != PTOF_LAYOUT_BHTD) {
+    fail(PTOF_EUNSUPPORTED, "kda_fwd: Dk = Dv = 64, bf16 q/k/v, heads-outer layout only "
+         "(got Dk=%d Dv=%d in_dtype=%d layout=%d)", p->Dk, p->Dv, p->in_dtype, p->layout);
+    return nullptr;
+  }
+  Workspace* w = ws_create(kWsKdaFwd, p);
+  if (!w) return nullptr;
+  w->scratch_bytes = kda_scratch_layout(*p).total;
+  const cudaError_t e = cudaMalloc(&w->d_scratch, w->scratch_bytes);
+  if (e != cudaSuccess) {
+    cuda_fail(e, "kda_fwd scratch buffer");
+    ws_destroy(w);
+    return nullptr;
+  }
+  return w;
+}
+
+extern "C" int ptof_kda_fwd_exec(void* wsv, const void* q, const void* k, const void* v,
+                                 const void* beta, const float* g, const float* S0, void* o,
+                                 float* S_final, void* stream) {
+  using namespace ptof;
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w || w->kind != kWsKdaFwd) return fail(PTOF_EINVAL, "not a kda_fwd workspace");
+  int rc = check_ptrs({q, k, v, beta, g, o}, {S0, S_final});
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (w->p.out_dtype) {
+    case PTOF_F32: return launch_kda_t<float>(w, q, k, v, beta, g, S0, o, S_final, st);
+    case PTOF_F16: return launch_kda_t<__half>(w, q, k, v, beta, g, S0, o, S_final, st);
+    default: return launch_kda_t<__nv_bfloat16>(w, q, k, v, beta, g, S0, o, S_final, st);
+  }
 }

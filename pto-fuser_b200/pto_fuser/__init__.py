@@ -26,7 +26,7 @@ from .template import (EpilogueUnit, FuseChunkOFlash, FuseContractionEpilogue,
                        FusePerDimChunkOFlash, Template, default_templates, epilogue_report,
                        extract_epilogue_unit)
 from .transforms import FuseGDNForward, LowerResidentScan
-from .gdn import GDNChunkForward, GDNChunkForwardVarlen, chunk_gdn_forward
+from .gdn import GDNChunkForward, GDNChunkForwardVarlen, KDAChunkForward, chunk_gdn_forward
 from .inputs import make_gdn_inputs
 
 __all__ = [
@@ -40,5 +40,5 @@ __all__ = [
     "CompilationReport", "TransformRecord", "CompileResult", "compile_program", "EpilogueUnit",
     "extract_epilogue_unit", "Template", "default_templates", "FuseContractionEpilogue",
     "FuseChunkOFlash", "FusePerDimChunkOFlash", "epilogue_report", "LowerResidentScan",
-    "FuseGDNForward", "GDNChunkForward", "GDNChunkForwardVarlen", "chunk_gdn_forward", "make_gdn_inputs",
+    "FuseGDNForward", "GDNChunkForward", "GDNChunkForwardVarlen", "KDAChunkForward", "chunk_gdn_forward", "make_gdn_inputs",
 ]

@@ -113,6 +113,65 @@ class GDNChunkForward:
             pass
 
 
+class KDAChunkForward:
+    """One-shape persistent runner of the fused KDA (per-dimension gate) chunk forward
+    on the tensor cores: ``ptof_kda_fwd_setup`` once, ``ptof_kda_fwd_exec`` per call
+    on the current stream. Semantics of kda_reference (examples/attention/
+    _kda_full.py:38-77) with the output scale folded in, plus an optional initial
+    state and the final state. q, k, v bf16 [B,H,T,64]; beta [B,H,T]; g fp32
+    [B,H,T,64] (per-token, per-dimension log decay)."""
+
+    def __init__(self, B: int, H: int, T: int, D: int = 64, *, beta_dtype=torch.bfloat16,
+                 out_dtype=torch.bfloat16, scale: Optional[float] = None, device=None) -> None:
+        self.device = nv.cuda_device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.shape = (B, H, T, D)
+        self.beta_dtype, self.out_dtype = beta_dtype, out_dtype
+        self.scale = D ** -0.5 if scale is None else float(scale)
+        p = nv.GdnParams(B, H, T, 64, D, D, nv.BF16, nv.dtype_code(beta_dtype),
+                         nv.dtype_code(out_dtype), nv.GATE_RAW, nv.LAYOUT_BHTD, self.scale)
+        with torch.cuda.device(self.device):
+            self._ws = nv.lib().ptof_kda_fwd_setup(ctypes.byref(p))
+        if not self._ws:
+            raise nv.NativeError(nv.EUNSUPPORTED, nv.last_error())
+
+    def __call__(self, q, k, v, beta, g, initial_state=None, *, o=None, final_state=None):
+        B, H, T, D = self.shape
+        for name, t, shape, dt in (("q", q, (B, H, T, D), torch.bfloat16),
+                                   ("k", k, (B, H, T, D), torch.bfloat16),
+                                   ("v", v, (B, H, T, D), torch.bfloat16),
+                                   ("beta", beta, (B, H, T), self.beta_dtype),
+                                   ("g", g, (B, H, T, D), torch.float32)):
+            if tuple(t.shape) != shape or t.dtype != dt or not t.is_contiguous() \
+                    or t.device != self.device:
+                raise ValueError(f"{name}: expected contiguous {dt} {shape} on {self.device}, "
+                                 f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+        if o is None:
+            o = torch.empty(B, H, T, D, device=self.device, dtype=self.out_dtype)
+        if final_state is None:
+            final_state = torch.empty(B, H, D, D, device=self.device, dtype=torch.float32)
+        rc = nv.lib().ptof_kda_fwd_exec(
+            self._ws, q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(), g.data_ptr(),
+            nv.ptr(initial_state), o.data_ptr(), final_state.data_ptr(),
+            nv.stream_handle(self.device))
+        nv.check(rc)
+        return o, final_state
+
+    def check_status(self) -> None:
+        nv.check(nv.lib().ptof_check_status(self._ws, nv.stream_handle(self.device)))
+
+    def close(self) -> None:
+        if getattr(self, "_ws", None):
+            nv.lib().ptof_gdn_fwd_teardown(self._ws)
+            self._ws = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 _RUNNERS: Dict[tuple, GDNChunkForward] = {}
 
 

@@ -60,6 +60,8 @@ _SIGNATURES = {
     "ptof_gdn_fwd_teardown": (None, [_vp]),
     "ptof_gdn_fwd_varlen_setup": (_vp, [ctypes.POINTER(GdnVarlenParams)]),
     "ptof_gdn_fwd_varlen_exec": (_i32, [_vp] * 11),
+    "ptof_kda_fwd_setup": (_vp, [ctypes.POINTER(GdnParams)]),
+    "ptof_kda_fwd_exec": (_i32, [_vp] * 10),
     "ptof_gdn_fwd_exec_noalloc": (_i32, [ctypes.POINTER(GdnParams)] + [_vp] * 9),
     "ptof_seg_scan_exec": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64,
                                   _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
