@@ -510,6 +510,27 @@ def run_configs(args):
     fwd("cfg4", "long-context GDN bf16 B1 H64 T131072 D128, S0 ~ N(0,0.02^2), mu 3", 1, 64,
         131072, 128, torch.bfloat16, mu=3.0, s0_std=0.02)
 
+    # KDA (per-dimension gate; the reference's next family): the fused tensor-core
+    # forward at config 3's shape, g = -U(0,1) * 0.05 per token and dimension
+    from pto_fuser import KDAChunkForward
+    B, H, T, D = 16, 16, 4096, 64
+    q = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).bfloat16()
+    k = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(B, H, T, D, device=dev, generator=gen).bfloat16()
+    beta = torch.sigmoid(torch.randn(B, H, T, device=dev, generator=gen)).bfloat16()
+    g = -torch.rand(B, H, T, D, device=dev, generator=gen) * 0.05
+    r = KDAChunkForward(B, H, T, D)
+    o = torch.empty_like(v)
+    S = torch.empty(B, H, D, D, device=dev)
+    ms = timed(lambda: r(q, k, v, beta, g, o=o, final_state=S), args.steps)
+    r.check_status()
+    # algorithmic bytes: q, k, v, o bf16, beta bf16, g fp32 per (token, dimension),
+    # plus the final state (the operand pre-pass's own traffic is not algorithmic)
+    algo = B * H * T * (4 * D * 2 + 2 + 4 * D) + B * H * D * D * 4
+    line("kda", "KDA forward bf16 B16 H16 T4096 D64 (fused tcgen05, operand pre-pass)", ms,
+         B * T, algo, "bfloat16")
+    r.close()
+
 
 def run_long(args):
     """Config 4 (one long sequence, few heads) with the token axis split over the
