@@ -1092,7 +1092,7 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
 // with G the chunk-local cumsum, this pass writes K e^G, Q e^G, K e^-G (bf16) and the
 // chunk's per-dimension decay e^{G_last} into slot c + 1 of `egl` (slot 0 = 1), so
 // the fused kernel runs the ungated GDN chain on these operands. One thread per key
-// dimension walks the 64 tokens of one chunk (coalesced rows of g, k, q).
+// dimension and token group covers 16 tokens of one chunk (coalesced rows of g, k, q).
 struct KdaPrepParams {
   const __nv_bfloat16 *q, *k;
   const float* g;
@@ -1100,25 +1100,39 @@ struct KdaPrepParams {
   float* egl;
   int nc, T;
 };
+// 256 threads: thread (j, d) handles dimension d of tokens 16 j .. 16 j + 15 (all its
+// loads independent), the four token groups joined by a prefix over shared memory.
 template <int DK>
-__global__ void __launch_bounds__(DK) kda_prep_kernel(const __grid_constant__ KdaPrepParams P) {
-  const int d = threadIdx.x;
+__global__ void __launch_bounds__(4 * DK) kda_prep_kernel(const __grid_constant__ KdaPrepParams P) {
+  __shared__ float part[4][DK];
+  const int d = threadIdx.x % DK, j = threadIdx.x / DK;
   const int bh = blockIdx.x / P.nc, c = blockIdx.x % P.nc;
-  const int64_t base = (static_cast<int64_t>(bh) * P.T + static_cast<int64_t>(c) * kC) * DK + d;
-  float G = 0.f;
-#pragma unroll 4
-  for (int i = 0; i < kC; ++i) {
+  const int64_t base =
+      (static_cast<int64_t>(bh) * P.T + static_cast<int64_t>(c) * kC + 16 * j) * DK + d;
+  float gl[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) gl[i] = P.g[base + static_cast<int64_t>(i) * DK];
+#pragma unroll
+  for (int i = 1; i < 16; ++i) gl[i] += gl[i - 1];
+  part[j][d] = gl[15];
+  __syncthreads();
+  float off = 0.f;
+  for (int jj = 0; jj < j; ++jj) off += part[jj][d];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
     const int64_t e = base + static_cast<int64_t>(i) * DK;
-    G += P.g[e];
+    const float G = gl[i] + off;
     const float up = __expf(G), dn = __expf(-G);
     const float kk = __bfloat162float(P.k[e]), qq = __bfloat162float(P.q[e]);
     P.k1[e] = __float2bfloat16_rn(kk * up);
     P.q1[e] = __float2bfloat16_rn(qq * up);
     P.k2[e] = __float2bfloat16_rn(kk * dn);
   }
-  float* eg = P.egl + static_cast<int64_t>(bh) * (P.nc + 1) * DK;
-  eg[static_cast<int64_t>(c + 1) * DK + d] = __expf(G);
-  if (c == 0) eg[d] = 1.f;
+  if (j == 3) {
+    float* eg = P.egl + static_cast<int64_t>(bh) * (P.nc + 1) * DK;
+    eg[static_cast<int64_t>(c + 1) * DK + d] = __expf(gl[15] + off);
+    if (c == 0) eg[d] = 1.f;
+  }
 }
 
 }  // namespace tcfwd
@@ -1289,7 +1303,7 @@ int launch_kda_t(Workspace* w, const void* q, const void* k, const void* v, cons
     K.q1 = q1; K.k1 = k1; K.k2 = k2;
     K.egl = egl;
     K.nc = nc; K.T = p.T;
-    tcfwd::kda_prep_kernel<D><<<static_cast<unsigned>(chunks), D, 0, stream>>>(K);
+    tcfwd::kda_prep_kernel<D><<<static_cast<unsigned>(chunks), 4 * D, 0, stream>>>(K);
   }
   const int64_t tokens = static_cast<int64_t>(p.B) * p.T;
   tcfwd::Params P;
