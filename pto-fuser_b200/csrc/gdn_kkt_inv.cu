@@ -27,7 +27,9 @@ namespace kktinv {
 
 constexpr int kC = kChunk;   // 64
 constexpr int kThreads = 160;
-constexpr int kNS = 2;       // K ring depth (3 CTAs per SM fit with the T staging tile)
+constexpr int kNS = 2;       // K ring depth
+// four CTAs per SM: TMEM 4 x 128 columns; T is stored straight from the inverse's tile
+constexpr int kCtasPerSm = 4;
 constexpr int kAllBar = 1;   // named barriers: 1 = the four compute warps, 2-3 = pairs
 
 template <int D>
@@ -35,11 +37,9 @@ struct KLayout {
   static constexpr int NKB = D / 64;
   static constexpr int STAGE = NKB * kC * 128;       // K rows x (64 d) per 128B-swizzled region
   static constexpr int OFF_A = kNS * STAGE;          // fp16 A -> T tile, 8 KB
-  // fp32 T staging tile [64][64] for the chunk's bulk store
-  static constexpr int OFF_TS = OFF_A + kC * 128;
   // fp32 gcum[64], beta[64], rowfb[64] = beta_i e^{g_i - g_0}, colf[64] = e^{g_0 - g_j},
   // then the chunk's fast-path flag
-  static constexpr int OFF_G = OFF_TS + kC * kC * 4;
+  static constexpr int OFF_G = OFF_A + kC * 128;
   static constexpr int OFF_BAR = OFF_G + 1024 + 16;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
   static constexpr int TCOLS = 2 * kC;               // two fp32 64x64 accumulators
@@ -60,7 +60,7 @@ struct KParams {
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_constant__ KParams P) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gdn_kkt_inv_kernel(const __grid_constant__ KParams P) {
   using L = KLayout<D>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t sbase = smem_u32(smem_raw);
@@ -202,58 +202,57 @@ __global__ void __launch_bounds__(kThreads, 3) gdn_kkt_inv_kernel(const __grid_c
       tc_fence_after();
       const int i = 16 * w + l;
       const uint32_t tacc = tmem + bb * kC + ((32u * w) << 16);
-      float v[kC];
+      const bool fast = *fastp != 0;
+      const float gi = gcum[min(i, kC - 1)], bi = bsm[min(i, kC - 1)], rb = rowfb[min(i, kC - 1)];
+      // two 32-column halves (register budget of four CTAs per SM)
 #pragma unroll
-      for (int j0 = 0; j0 < kC; j0 += 16) tmem_ld16(tacc + j0, *reinterpret_cast<float(*)[16]>(v + j0));
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (l == 0) mbar_arrive(&bars[K_TFREE0 + bb]);
-      if (l < 16) {
-        const bool fast = *fastp != 0;
-        const float gi = gcum[i], bi = bsm[i], rb = rowfb[i];
+      for (int h0 = 0; h0 < kC; h0 += 32) {
+        float v[32];
+        tmem_ld16(tacc + h0, *reinterpret_cast<float(*)[16]>(v));
+        tmem_ld16(tacc + h0 + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+        tmem_wait_ld();
+        if (h0 + 32 == kC) {
+          tc_fence_before();
+          __syncwarp();
+          if (l == 0) mbar_arrive(&bars[K_TFREE0 + bb]);
+        }
+        if (l < 16) {
 #pragma unroll
-        for (int j0 = 0; j0 < kC; j0 += 8) {
-          uint32_t pk[4];
+          for (int j0 = 0; j0 < 32; j0 += 8) {
+            uint32_t pk[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float a2[2];
+            for (int u = 0; u < 4; ++u) {
+              float a2[2];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int j = j0 + 2 * u + e;
-              const float cf = fast ? rb * colf[j] : bi * kkt_coef(gi, gcum[j]);
-              a2[e] = (j < i) ? v[j] * cf : 0.f;
+              for (int e = 0; e < 2; ++e) {
+                const int j = h0 + j0 + 2 * u + e;
+                const float cf = fast ? rb * colf[j] : bi * kkt_coef(gi, gcum[j]);
+                a2[e] = (j < i) ? v[j0 + 2 * u + e] * cf : 0.f;
+              }
+              pk[u] = pack_f16(a2[0], a2[1]);
             }
-            pk[u] = pack_f16(a2[0], a2[1]);
+            const int jj = h0 + j0;
+            *reinterpret_cast<uint4*>(at + i * 128 + (((jj >> 3) ^ (i & 7)) << 4)) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-          *reinterpret_cast<uint4*>(at + i * 128 + (((j0 >> 3) ^ (i & 7)) << 4)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
       named_bar_sync(kAllBar, 128);   // A complete
       tri_inv64_inplace(at, w, l, 2, kAllBar);
-      // ---- T -> fp32 staging tile (linear float4 f = tid + 128 it: row f / 16,
-      //      columns 4 (f % 16) ..) -> one asynchronous 16 KB bulk store per chunk ----
-      float* ts = reinterpret_cast<float*>(sm + L::OFF_TS);
-      if (tid == 0) bulk_wait_read0();   // the previous chunk's store has read the tile
-      named_bar_sync(kAllBar, 128);
+      // ---- T (fp16 tile) -> fp32 rows of T in global memory: float4 f = tid + 128 it is
+      //      row f / 16, columns 4 (f % 16) .. (each row 256 contiguous bytes) ----
+      float4* tg = reinterpret_cast<float4*>(P.Tout + m * (kC * kC));
 #pragma unroll
       for (int it = 0; it < 8; ++it) {
         const int f = tid + 128 * it, row = f >> 4, col = (f & 15) * 4;
         const uint2 u = *reinterpret_cast<const uint2*>(
             at + row * 128 + ((((col >> 3) ^ (row & 7)) << 4) | ((col & 7) << 1)));
         const float2 lo = unpack_f16(u.x), hi = unpack_f16(u.y);
-        reinterpret_cast<float4*>(ts)[f] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        tg[f] = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
-      fence_async_smem();
-      named_bar_sync(kAllBar, 128);   // staging complete; A tile and gcum free again
-      if (tid == 0) {
-        bulk_store(P.Tout + m * (kC * kC), ts, kC * kC * 4);
-        bulk_commit();
-      }
+      named_bar_sync(kAllBar, 128);   // A tile and gcum free again
     }
   }
-  if (tid == 0) bulk_wait0();   // the last T store has completed
   __syncthreads();
   tc_fence_after();
   if (warp == 4) tmem_dealloc(tmem, L::TCOLS);
@@ -299,7 +298,8 @@ int launch_kkt_inv_t(const ptof_gdn_params& p, int* status, const void* k, const
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t grid = P.M < 3LL * sms ? P.M : 3LL * sms;
+  const int64_t grid = P.M < kktinv::kCtasPerSm * static_cast<int64_t>(sms)
+                           ? P.M : kktinv::kCtasPerSm * static_cast<int64_t>(sms);
   kern<<<static_cast<unsigned>(grid), kktinv::kThreads, L::BYTES, st>>>(P);
   e = cudaGetLastError();
   return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "kkt_inv launch");
