@@ -246,6 +246,16 @@ PTOF_API int ptof_kda_fwd_exec(void* ws, const void* q, const void* k, const voi
  * (a limit below the time one chunk takes makes a wait run out on purpose). */
 PTOF_API int ptof_ws_set_wait_limit(void* ws, unsigned long long ns);
 
+/* Strided views for the tensor-core forward on this workspace (no counterpart in the
+ * reference, whose operands are always dense): with the heads-outer layout, head (b, h)
+ * of q, k, beta and g starts at token b * qk_pair + h * qk_seg of its buffer, of v at
+ * b * v_pair + h * v_seg, of o at b * o_pair + h * o_seg (strides in tokens; T tokens
+ * from there). All zero restores the dense [B,H,T,D] layout. Used by the chunk-segment
+ * scan inside one GPU, which runs segments of the caller's sequences in place. */
+PTOF_API int ptof_gdn_fwd_set_view(void* ws, long long qk_pair, long long qk_seg,
+                                   long long v_pair, long long v_seg, long long o_pair,
+                                   long long o_seg);
+
 /* Fault-path test hook (no counterpart in the reference): while `on` is nonzero, each
  * tensor-core forward launched on this workspace first waits on a device barrier that
  * nothing arrives at, so that wait runs out after the wait limit, the launch ends early
@@ -294,6 +304,14 @@ PTOF_API int ptof_seg_scan_exec(const float* A, int64_t a_head_stride, int64_t a
  * Launches on `stream`, no host synchronisation. */
 PTOF_API int ptof_seg_fix_exec(void* ws, void* o, const void* oa, const float* X, int units,
                                int Tseg, int D, int dtype, void* stream);
+
+/* The same fix-up with o a strided view (no counterpart in the reference): unit
+ * (pair, seg) of o starts at token pair * o_pair_stride + seg * o_seg_stride of o's
+ * buffer; o^A [pairs * segs, Tseg, D] and X [pairs * segs, D, D] are contiguous. */
+PTOF_API int ptof_seg_fix_exec_view(void* ws, void* o, const void* oa, const float* X, int pairs,
+                                    int segs, int Tseg, int D, int dtype,
+                                    long long o_pair_stride, long long o_seg_stride,
+                                    void* stream);
 
 /* Human-readable text of the last host-side error on this thread. */
 PTOF_API const char* ptof_last_error(void);

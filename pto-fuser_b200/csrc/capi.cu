@@ -92,6 +92,26 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, con
   return PTOF_OK;
 }
 
+int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(PTOF_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return fail(PTOF_EALIGN, "TMA base address not 16-byte aligned");
+  for (int i = 0; i < 3; ++i)
+    if (strides_bytes[i] % 16 != 0 || strides_bytes[i] == 0)
+      return fail(PTOF_EALIGN, "TMA stride %llu not a positive multiple of 16 bytes",
+                  (unsigned long long)strides_bytes[i]);
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t s[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t b[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t e[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, dt, 4, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PTOF_ECUDA, "cuTensorMapEncodeTiled(4d) failed (%d)", (int)r);
+  return PTOF_OK;
+}
+
 cudaError_t set_smem_attr_once(const void* kern, int bytes) {
   static std::mutex mu;
   static std::unordered_map<const void*, int> done;
@@ -281,6 +301,28 @@ int ptof_ws_set_wait_limit(void* wsv, unsigned long long ns) {
   if (!w || w->kind != kWsGdnFwd) return fail(PTOF_EINVAL, "not a gdn_fwd workspace");
   if (ns == 0) return fail(PTOF_EINVAL, "wait limit must be positive");
   w->wait_ns = ns;
+  return PTOF_OK;
+}
+
+int ptof_gdn_fwd_set_view(void* wsv, long long qk_pair, long long qk_seg, long long v_pair,
+                          long long v_seg, long long o_pair, long long o_seg) {
+  Workspace* w = static_cast<Workspace*>(wsv);
+  if (!w || w->kind != kWsGdnFwd) return fail(PTOF_EINVAL, "not a gdn_fwd workspace");
+  const long long all[6] = {qk_pair, qk_seg, v_pair, v_seg, o_pair, o_seg};
+  bool any = false;
+  for (long long x : all) {
+    if (x < 0) return fail(PTOF_EINVAL, "view strides must be >= 0");
+    any = any || x != 0;
+  }
+  if (any) {
+    if (w->p.layout != PTOF_LAYOUT_BHTD || w->ex[0] == 1)
+      return fail(PTOF_EUNSUPPORTED, "views need the heads-outer layout (not varlen)");
+    if (w->p.in_dtype == PTOF_F32 || !gdn_fwd_tc_supports(w->p))
+      return fail(PTOF_EUNSUPPORTED, "views are served by the tensor-core forward only");
+    for (long long x : all)
+      if (x == 0) return fail(PTOF_EINVAL, "every view stride must be positive");
+  }
+  for (int i = 0; i < 6; ++i) w->view[i] = all[i];
   return PTOF_OK;
 }
 

@@ -33,6 +33,10 @@ struct Workspace {
   int trace_chunks = 0;
   unsigned long long wait_ns = 2000000000ull;  // limit of every bounded device wait
   int inject_stall = 0;          // test only: make one device wait run out
+  // strided view (tokens): head (b, h) of q/k/beta/g starts at token b*view[0] + h*view[1]
+  // of its buffer, of v at b*view[2] + h*view[3], of o at b*view[4] + h*view[5]; all 0 =
+  // the contiguous [B,H,T,D] layout
+  long long view[6] = {0, 0, 0, 0, 0, 0};
 };
 
 int fail(int code, const char* fmt, ...);
@@ -40,6 +44,8 @@ int cuda_fail(cudaError_t e, const char* what);
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                  uint32_t box_outer, CUtensorMapSwizzle swz);
+int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
 int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t* dims,
                  const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
 Workspace* ws_create(int kind, const ptof_gdn_params* p);

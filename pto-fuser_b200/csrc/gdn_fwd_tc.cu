@@ -167,6 +167,7 @@ struct Params {
   float scale;
   unsigned long long wait_ns;      // limit of every bounded wait
   int inject_stall;                // test only: the chain waits on B_NEVER before chunk 0
+  int view;                        // strided view: 4D maps {D, T, H, B}, coordinates (x, t, h, b)
 };
 
 // Optional stage timestamps (globaltimer, ns) of CTA 0: slot layout per chunk.
@@ -469,6 +470,13 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
                                                       L::EGLD_BYTES);
 #pragma unroll
         for (int kb = 0; kb < L::NKB; ++kb) {
+          if (P.view) {
+            tma_load_4d(st + L::OFF_KQ + kb * L::KQ_REGION, &P.mapK, &bars[B_FULL0 + s], kb * 64,
+                        t0, h, b);
+            tma_load_4d(st + L::OFF_KQ + kb * L::KQ_REGION + kC * 128, &P.mapQ,
+                        &bars[B_FULL0 + s], kb * 64, t0, h, b);
+            continue;
+          }
           tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION, &P.mapK, &bars[B_FULL0 + s], kb * 64, y, z);
           tma_load_3d(st + L::OFF_KQ + kb * L::KQ_REGION + kC * 128, &P.mapQ, &bars[B_FULL0 + s],
                       kb * 64, y, z);
@@ -680,8 +688,12 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
       const int y = bhtd ? t0 : h, z = bhtd ? bh : static_cast<int>(tok0 + t0);
       mbar_arrive_expect_tx(&bars[B_VFULL], DV * kC * 2);
 #pragma unroll
-      for (int vb = 0; vb < L::NVB; ++vb)
-        tma_load_3d(sm + L::OFF_V + vb * L::V_REGION, &P.mapV, &bars[B_VFULL], vb * 64, y, z);
+      for (int vb = 0; vb < L::NVB; ++vb) {
+        if (P.view)
+          tma_load_4d(sm + L::OFF_V + vb * L::V_REGION, &P.mapV, &bars[B_VFULL], vb * 64, t0, h, b);
+        else
+          tma_load_3d(sm + L::OFF_V + vb * L::V_REGION, &P.mapV, &bars[B_VFULL], vb * 64, y, z);
+      }
     };
     int v_issued = -1;   // last chunk whose V load was issued (drained at exit)
     if (qp == 0) {
@@ -1166,6 +1178,20 @@ int make_act_map(CUtensorMap* m, const void* base, int dt, const ptof_gdn_params
   return make_tmap_3d(m, base, t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// 4D TMA map of a strided view of a heads-outer activation: dims {D, T, H, B}, head
+// (b, h) at token b*pair + h*seg of the buffer (strides in tokens).
+int make_view_map(CUtensorMap* m, const void* base, int dt, const ptof_gdn_params& p, int D,
+                  long long pair, long long seg) {
+  const CUtensorMapDataType t =
+      dt == PTOF_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(p.T),
+                            static_cast<uint64_t>(p.H), static_cast<uint64_t>(p.B)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(seg) * D * 2,
+                               static_cast<uint64_t>(pair) * D * 2};
+  const uint32_t box[4] = {64, 64, 1, 1};
+  return make_tmap_4d(m, base, t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 template <int DK, int DV, bool F16, typename TO>
 int launch_t(Workspace* w, const void* q, const void* k, const void* v, const void* beta,
              const float* g, const float* S0, void* o, float* S_final, const int* cu_seqlens,
@@ -1178,9 +1204,19 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   const int Hg = varlen ? w->ex[1] : p.H;
   const int64_t tokens = varlen ? w->ex[2] : static_cast<int64_t>(p.B) * p.T;
   tcfwd::Params P;
-  int rc = make_act_map(&P.mapK, k, p.in_dtype, p, DK, Hg, tokens);
-  if (!rc) rc = make_act_map(&P.mapQ, q, p.in_dtype, p, DK, Hg, tokens);
-  if (!rc) rc = make_act_map(&P.mapV, v, p.in_dtype, p, DV, p.H, tokens);
+  const long long* vw = w->view;
+  P.view = (vw[0] != 0) ? 1 : 0;
+  int rc;
+  if (P.view) {
+    // strided view: head (b, h) starts at token b*pair + h*seg of its buffer
+    rc = make_view_map(&P.mapK, k, p.in_dtype, p, DK, vw[0], vw[1]);
+    if (!rc) rc = make_view_map(&P.mapQ, q, p.in_dtype, p, DK, vw[0], vw[1]);
+    if (!rc) rc = make_view_map(&P.mapV, v, p.in_dtype, p, DV, vw[2], vw[3]);
+  } else {
+    rc = make_act_map(&P.mapK, k, p.in_dtype, p, DK, Hg, tokens);
+    if (!rc) rc = make_act_map(&P.mapQ, q, p.in_dtype, p, DK, Hg, tokens);
+    if (!rc) rc = make_act_map(&P.mapV, v, p.in_dtype, p, DV, p.H, tokens);
+  }
   if (rc) return rc;
   // per-chunk coefficient records, then the fused forward (same stream)
   if (!w->d_scratch || w->scratch_bytes < gdn_fwd_tc_scratch_bytes(p))
@@ -1196,6 +1232,9 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
     C.allow_fast = F16 ? 0 : 1;
     const Strides3 sg = make_strides3(p.layout, p.H, p.T);
     C.gs_b = sg.b; C.gs_h = sg.h; C.gs_t = sg.t;
+    if (P.view) {
+      C.gs_b = vw[0]; C.gs_h = vw[1]; C.gs_t = 1;
+    }
     C.cu_seqlens = varlen ? cu_seqlens : nullptr;
     C.T = p.T;
     const int64_t chunks = static_cast<int64_t>(p.B) * p.H * C.nc;
@@ -1212,6 +1251,9 @@ int launch_t(Workspace* w, const void* q, const void* k, const void* v, const vo
   P.layout = p.layout;
   const Strides4 so = make_strides4(p.layout, p.H, p.T, DV);
   P.os_b = so.b; P.os_h = so.h; P.os_t = so.t;
+  if (P.view) {
+    P.os_b = vw[4] * DV; P.os_h = vw[5] * DV; P.os_t = DV;
+  }
   P.cu_seqlens = varlen ? cu_seqlens : nullptr;
   P.mnc = (p.T + kChunk - 1) / kChunk;
   P.gqa = p.H / Hg;
@@ -1330,6 +1372,7 @@ int launch_kda_t(Workspace* w, const void* q, const void* k, const void* v, cons
   P.scale = p.scale;
   P.wait_ns = w->wait_ns;
   P.inject_stall = 0;
+  P.view = 0;
   auto kern = tcfwd::gdn_fwd_tc_kernel<D, D, false, TO, false, false, true>;
   cudaError_t e = set_smem_once(kern, L::BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "kda_fwd smem attribute");

@@ -52,6 +52,7 @@ struct FParams {
   int* status;
   int64_t tiles;       // units * tiles_per_unit
   int tiles_per_unit;
+  int view_segs;       // > 0: o is a strided view, mapO 4D {D, Tseg, segs, pairs}
 };
 
 template <int D, bool BF16>
@@ -105,12 +106,19 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       if (lane == 0) {
         const int y = static_cast<int>((t0 + i) * kRows);
         mbar_arrive_expect_tx(&bars[F_FULL0 + s], 2 * L::TILE);
+        const int64_t tile = t0 + i;
+        const int u = static_cast<int>(tile / P.tiles_per_unit);
+        const int r = static_cast<int>(tile % P.tiles_per_unit) * kRows;
 #pragma unroll
         for (int kb = 0; kb < L::NKB; ++kb) {
           tma_load_2d(sm + L::OFF_OA + s * L::TILE + kb * kRows * 128, &P.mapOA,
                       &bars[F_FULL0 + s], kb * 64, y);
-          tma_load_2d(sm + L::OFF_OB + s * L::TILE + kb * kRows * 128, &P.mapO,
-                      &bars[F_FULL0 + s], kb * 64, y);
+          if (P.view_segs > 0)
+            tma_load_4d(sm + L::OFF_OB + s * L::TILE + kb * kRows * 128, &P.mapO,
+                        &bars[F_FULL0 + s], kb * 64, r, u % P.view_segs, u / P.view_segs);
+          else
+            tma_load_2d(sm + L::OFF_OB + s * L::TILE + kb * kRows * 128, &P.mapO,
+                        &bars[F_FULL0 + s], kb * 64, y);
         }
       }
       const int u = unit_of(i);
@@ -220,8 +228,17 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       if (named_bar_or(1, 128, abort_flag != 0)) break;
       if (tid == 0) {
         const int y = static_cast<int>((t0 + i) * kRows);
+        const int64_t tile = t0 + i;
+        const int u = static_cast<int>(tile / P.tiles_per_unit);
+        const int r = static_cast<int>(tile % P.tiles_per_unit) * kRows;
 #pragma unroll
-        for (int kb = 0; kb < L::NKB; ++kb) tma_store_2d(&P.mapO, ob + kb * kRows * 128, kb * 64, y);
+        for (int kb = 0; kb < L::NKB; ++kb) {
+          if (P.view_segs > 0)
+            tma_store_4d(&P.mapO, ob + kb * kRows * 128, kb * 64, r, u % P.view_segs,
+                         u / P.view_segs);
+          else
+            tma_store_2d(&P.mapO, ob + kb * kRows * 128, kb * 64, y);
+        }
         bulk_commit();
         bulk_wait_read0();
         mbar_arrive(&bars[F_EMPTY0 + s]);
@@ -242,16 +259,31 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
 
 template <int D, bool BF16>
 int launch_t(int* status, void* o, const void* oa, const float* X, int units, int Tseg,
-             cudaStream_t st) {
+             cudaStream_t st, int view_segs = 0, long long o_pair = 0, long long o_seg = 0) {
   using L = FLayout<D>;
   FParams P;
   const CUtensorMapDataType t = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const uint64_t rows = static_cast<uint64_t>(units) * Tseg;
   int rc = make_tmap_2d(&P.mapOA, oa, t, 2, D, rows, static_cast<uint64_t>(D) * 2, 64, kRows,
                         CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = make_tmap_2d(&P.mapO, o, t, 2, D, rows, static_cast<uint64_t>(D) * 2, 64, kRows,
-                             CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) {
+    if (view_segs > 0) {
+      // o strided: unit (pair, seg) starts at token pair*o_pair + seg*o_seg
+      const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Tseg),
+                                static_cast<uint64_t>(view_segs),
+                                static_cast<uint64_t>(units / view_segs)};
+      const uint64_t strides[3] = {static_cast<uint64_t>(D) * 2,
+                                   static_cast<uint64_t>(o_seg) * D * 2,
+                                   static_cast<uint64_t>(o_pair) * D * 2};
+      const uint32_t box[4] = {64, static_cast<uint32_t>(kRows), 1, 1};
+      rc = make_tmap_4d(&P.mapO, o, t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+      rc = make_tmap_2d(&P.mapO, o, t, 2, D, rows, static_cast<uint64_t>(D) * 2, 64, kRows,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+  }
   if (rc) return rc;
+  P.view_segs = view_segs;
   P.X = X;
   P.status = status;
   P.tiles_per_unit = Tseg / kRows;
@@ -291,4 +323,31 @@ int ptof_seg_fix_exec(void* ws, void* o, const void* oa, const float* X, int uni
               : segfix::launch_t<128, false>(status, o, oa, X, units, Tseg, st);
   return bf ? segfix::launch_t<64, true>(status, o, oa, X, units, Tseg, st)
             : segfix::launch_t<64, false>(status, o, oa, X, units, Tseg, st);
+}
+
+// The same fix-up with o a strided view (the chunk-segment scan inside one GPU writes
+// its tail segments straight into the caller's o): o^A and X are contiguous
+// [pairs * segs, Tseg, D] / [pairs * segs, D, D]; unit (pair, seg) of o starts at token
+// pair * o_pair_stride + seg * o_seg_stride of o's buffer.
+int ptof_seg_fix_exec_view(void* ws, void* o, const void* oa, const float* X, int pairs, int segs,
+                           int Tseg, int D, int dtype, long long o_pair_stride,
+                           long long o_seg_stride, void* stream) {
+  Workspace* w = static_cast<Workspace*>(ws);
+  if (pairs < 1 || segs < 1 || Tseg < segfix::kRows || Tseg % segfix::kRows ||
+      (D != 64 && D != 128) || o_pair_stride < 1 || o_seg_stride < 1 ||
+      static_cast<int64_t>(pairs) * segs * Tseg > (1LL << 31) - segfix::kRows)
+    return fail(PTOF_EINVAL, "seg_fix view shape pairs=%d segs=%d Tseg=%d D=%d", pairs, segs,
+                Tseg, D);
+  if (dtype != PTOF_BF16 && dtype != PTOF_F16) return fail(PTOF_EINVAL, "seg_fix dtype");
+  int rc = check_ptrs({o, oa, X}, {});
+  if (rc) return rc;
+  int* status = w ? w->d_status : nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == PTOF_BF16;
+  const int units = pairs * segs;
+  if (D == 128)
+    return bf ? segfix::launch_t<128, true>(status, o, oa, X, units, Tseg, st, segs, o_pair_stride, o_seg_stride)
+              : segfix::launch_t<128, false>(status, o, oa, X, units, Tseg, st, segs, o_pair_stride, o_seg_stride);
+  return bf ? segfix::launch_t<64, true>(status, o, oa, X, units, Tseg, st, segs, o_pair_stride, o_seg_stride)
+            : segfix::launch_t<64, false>(status, o, oa, X, units, Tseg, st, segs, o_pair_stride, o_seg_stride);
 }

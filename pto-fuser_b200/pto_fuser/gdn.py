@@ -96,6 +96,27 @@ class GDNChunkForward:
         """Synchronise and raise if a bounded device wait of the last launch gave up."""
         nv.check(nv.lib().ptof_check_status(self._ws, nv.stream_handle(self.device)))
 
+    def set_view(self, qk: Tuple[int, int], v: Tuple[int, int], o: Tuple[int, int]) -> None:
+        """Strided views for later ``call_view`` launches (ptof_gdn_fwd_set_view): head
+        (b, h) of q/k/beta/g starts at token ``b * qk[0] + h * qk[1]`` of its buffer, of v
+        at ``b * v[0] + h * v[1]``, of o at ``b * o[0] + h * o[1]``. (0, 0) x 3 restores
+        the dense layout."""
+        nv.check(nv.lib().ptof_gdn_fwd_set_view(self._ws, int(qk[0]), int(qk[1]), int(v[0]),
+                                                 int(v[1]), int(o[0]), int(o[1])))
+
+    def call_view(self, q, k, v, beta, g, initial_state, o, final_state) -> None:
+        """Launch on strided views set with ``set_view``: the tensors' data pointers are
+        the first tokens of head (0, 0); shapes are the caller's responsibility (the
+        runner's B, H, T and the view strides address every element)."""
+        for name, t in (("q", q), ("k", k), ("v", v), ("beta", beta), ("o", o)):
+            if t.device != self.device:
+                raise ValueError(f"{name} on {t.device}, runner on {self.device}")
+        rc = nv.lib().ptof_gdn_fwd_exec(
+            self._ws, q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(), nv.ptr(g),
+            nv.ptr(initial_state), o.data_ptr(), nv.ptr(final_state),
+            nv.stream_handle(self.device))
+        nv.check(rc)
+
     def set_wait_limit(self, ns: int) -> None:
         """Limit of every bounded device wait of later launches, in ns (default 2 s).
         A launch whose wait runs out ends early; ``check_status`` then raises."""

@@ -70,6 +70,8 @@ _SIGNATURES = {
     "ptof_gdn_fwd_set_trace": (_i32, [_vp, _vp, _i32]),
     "ptof_ws_set_wait_limit": (_i32, [_vp, ctypes.c_ulonglong]),
     "ptof_gdn_fwd_inject_stall": (_i32, [_vp, _i32]),
+    "ptof_gdn_fwd_set_view": (_i32, [_vp] + [ctypes.c_longlong] * 6),
+    "ptof_seg_fix_exec_view": (_i32, [_vp] * 4 + [_i32] * 5 + [ctypes.c_longlong] * 2 + [_vp]),
     "ptof_last_error": (ctypes.c_char_p, []),
     "ptof_ws_setup": (_vp, []),
     "ptof_ws_teardown": (None, [_vp]),

@@ -238,3 +238,142 @@ class GDNSegmentScan:
         if self._ws:
             nv.lib().ptof_ws_teardown(self._ws)
             self._ws = None
+
+
+# --------------------------------------------------------------------------------
+# Chunk-segment scan inside one GPU, with a long head segment
+# --------------------------------------------------------------------------------
+def plan_local_split(pairs: int, T: int, sms: int, *, chunk_us: float = 3.0,
+                     serial_chunk_us: float = 2.4, fix_gbs: float = 4000.0,
+                     fixed_us: float = 40.0, cta_us: float = 15.0, max_rounds: int = 2,
+                     D: int = 128
+                     ) -> Optional[Tuple[int, int, int]]:
+    """Head/tail split of ``pairs`` sequences of T tokens on ``sms`` SMs, or None when
+    the plain forward is predicted faster.
+
+    The forward is one CTA per chain walking its chunks in order, so with fewer pairs
+    than SMs the chains, not the SMs, set the time: ≈ ``serial_chunk_us`` per chunk when
+    one chain per pair runs, ≈ ``chunk_us`` once the split fills every SM (both
+    measured on B200: a split of 64 pairs x 16,384 tokens never beat the serial 0.61 ms,
+    16 pairs ran in 0.27 against 0.59 ms, config 4 in 4.0 against 4.7 ms). Each
+    pair's head segment of L0 tokens runs from the true initial state (one chain,
+    output final); its tail is cut into s segments of Ls tokens that run as A and B
+    chains (2 s chains per pair) on the SMs the heads leave free, composed by
+    ``seg_scan`` and fixed up by ``seg_fix``. Modelled time: max(head chain, rounds of
+    tail chains, each round with a CTA start-up) plus the fix-up's bytes and a fixed
+    cost. Returns (L0, s, Ls)."""
+    nchunks = T // CHUNK
+    plain_us = nchunks * serial_chunk_us
+    free = sms - pairs
+    if free <= 0 or T % (2 * CHUNK):
+        return None
+    best = None
+    for s in range(1, 9):
+        for tiles in range(1, T // (2 * CHUNK * s) + 1):
+            Ls = tiles * 2 * CHUNK            # whole 128-token fix-up tiles
+            L0 = T - s * Ls
+            if L0 < CHUNK:
+                break
+            rounds = -(-2 * pairs * s // free)
+            if rounds > max_rounds:   # later rounds start late: measured, not modelled
+                continue
+            # each round of tail CTAs also pays a CTA's start-up (TMEM, barriers, the
+            # first loads)
+            t = max(L0 // CHUNK * chunk_us, rounds * (Ls // CHUNK * chunk_us + cta_us))
+            t += pairs * s * Ls * D * 2 * 3 / (fix_gbs * 1e3) + fixed_us
+            if best is None or t < best[0]:
+                best = (t, L0, s, Ls)
+    if best is None or best[0] >= 0.95 * plain_us:
+        return None
+    return best[1], best[2], best[3]
+
+
+class GDNLocalSplit:
+    """GDN forward of ``pairs`` (b, h) sequences of T tokens on one GPU, each split into
+    a head of L0 tokens and s tail segments of Ls tokens (``plan_local_split``).
+
+    The head runs from the true initial state and writes its output in place; the tail
+    segments run twice side by side — the B run from a zero state (its output, written
+    in place into o, is o^B) and the A run from S0 = I with v = 0 (o^A into a scratch
+    buffer) — then ``seg_scan`` applies the tail maps in order from the head's final
+    state (the entry state X of every tail segment and the final state) and
+    ``ptof_seg_fix_exec_view`` adds o^A X into o. Every launch reads the caller's
+    tensors in place through strided views (``GDNChunkForward.set_view``). Operands:
+    q, k, v [pairs, T, D] bf16, beta [pairs, T], g [pairs, T] fp32 (per-token log
+    decay), initial_state [pairs, D, D] fp32 or None. Returns (o, final state).
+    Same result as the serial forward up to rounding (the affine algebra of the module
+    docstring)."""
+
+    def __init__(self, pairs: int, T: int, D: int, L0: int, segments: int, Ls: int, *,
+                 in_dtype=torch.bfloat16, scale: Optional[float] = None, device=None) -> None:
+        if L0 + segments * Ls != T or L0 % CHUNK or Ls % (2 * CHUNK) or L0 < CHUNK:
+            raise ValueError(f"split L0={L0} + {segments} x {Ls} does not tile T={T}")
+        self.pairs, self.T, self.D, self.L0, self.s, self.Ls = pairs, T, D, L0, segments, Ls
+        self.device = nv.cuda_device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.dtype = in_dtype
+        self.scale = D ** -0.5 if scale is None else float(scale)
+        P, s, dev = pairs, segments, self.device
+        mk = lambda H, TT: GDNChunkForward(P, H, TT, D, D, in_dtype=in_dtype, scale=self.scale,
+                                           device=dev)
+        self._head, self._tb, self._ta = mk(1, L0), mk(s, Ls), mk(s, Ls)
+        self._head.set_view((T, T), (T, T), (T, T))
+        self._tb.set_view((T, Ls), (T, Ls), (T, Ls))
+        self._ta.set_view((T, Ls), (s * Ls, Ls), (s * Ls, Ls))   # v = 0 and o^A dense
+        f32 = dict(device=dev, dtype=torch.float32)
+        self._v0 = torch.zeros(P, s, Ls, D, device=dev, dtype=in_dtype)
+        self._oa = torch.empty(P, s, Ls, D, device=dev, dtype=in_dtype)
+        self._eye = torch.eye(D, **f32).expand(P, s, D, D).contiguous()
+        self._A = torch.empty(P, s, D, D, **f32)
+        self._B = torch.empty(P, s, D, D, **f32)
+        self._S_head = torch.empty(P, D, D, **f32)
+        self._entry = torch.empty(P, s, D, D, **f32)
+        self._S_out = torch.empty(P, D, D, **f32)
+        self._streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev),
+                         torch.cuda.Stream(dev, priority=-1))
+        self._ws = nv.lib().ptof_ws_setup()
+        if not self._ws:
+            raise nv.NativeError(nv.EINVAL, nv.last_error())
+
+    def __call__(self, q, k, v, beta, g, initial_state=None, *, o=None):
+        P, T, D, L0 = self.pairs, self.T, self.D, self.L0
+        for name, t, shape in (("q", q, (P, T, D)), ("k", k, (P, T, D)), ("v", v, (P, T, D)),
+                               ("beta", beta, (P, T)), ("g", g, (P, T))):
+            if tuple(t.shape) != shape or not t.is_contiguous():
+                raise ValueError(f"{name}: expected contiguous {shape}, got {tuple(t.shape)}")
+        if o is None:
+            o = torch.empty(P, T, D, device=q.device, dtype=self.dtype)
+        main = torch.cuda.current_stream(self.device)
+        sa, sb, sh = self._streams
+        # the heads (the longest chains) on a high-priority stream so that their CTAs
+        # take SMs first, the tail runs on two side streams
+        sa.wait_stream(main)
+        sb.wait_stream(main)
+        sh.wait_stream(main)
+        with torch.cuda.stream(sh):
+            self._head.call_view(q, k, v, beta, g, initial_state, o, self._S_head)
+        tq, tk, tv, tb, tg, to = (t[:, L0:] for t in (q, k, v, beta, g, o))
+        with torch.cuda.stream(sb):
+            self._tb.call_view(tq, tk, tv, tb, tg, None, to, self._B)
+        with torch.cuda.stream(sa):
+            self._ta.call_view(tq, tk, self._v0, tb, tg, self._eye, self._oa, self._A)
+        main.wait_stream(sa)
+        main.wait_stream(sb)
+        main.wait_stream(sh)
+        seg_scan(self._A, self._B, self._S_head, self._entry, self._S_out, P, self.s, D, D)
+        nv.check(nv.lib().ptof_seg_fix_exec_view(
+            self._ws, to.data_ptr(), self._oa.data_ptr(), self._entry.data_ptr(), P, self.s,
+            self.Ls, D, nv.dtype_code(self.dtype), T, self.Ls, nv.stream_handle(self.device)))
+        return o, self._S_out
+
+    def check_status(self) -> None:
+        for r in (self._head, self._tb, self._ta):
+            r.check_status()
+        nv.check(nv.lib().ptof_check_status(self._ws, nv.stream_handle(self.device)))
+
+    def close(self) -> None:
+        for r in (self._head, self._tb, self._ta):
+            r.close()
+        if self._ws:
+            nv.lib().ptof_ws_teardown(self._ws)
+            self._ws = None

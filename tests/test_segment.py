@@ -138,3 +138,16 @@ def test_gloo_segment_scan_matches_serial(tmp_path, world):
         a = int(res["a"])
         assert np.allclose(res["o"], o_ref[:, a:a + sizes[r]], rtol=1e-5, atol=1e-6)
     assert np.allclose(res["S"], S_ref, rtol=1e-5, atol=1e-6)   # last rank: final state
+
+
+def test_local_split_planner():
+    """The head/tail planner: no split when the pairs fill the SMs, a split that tiles
+    T (whole 128-token tail tiles) when they do not."""
+    from pto_fuser.segment import plan_local_split
+    assert plan_local_split(148, 16384, 148) is None
+    assert plan_local_split(128, 16384, 148) is None
+    assert plan_local_split(64, 16384, 148) is None   # measured: no split beats serial
+    for P in (32, 16, 8):
+        L0, s, Ls = plan_local_split(P, 16384, 148)
+        assert L0 + s * Ls == 16384 and Ls % 128 == 0 and L0 % 64 == 0
+        assert s >= 1 and L0 < 16384
