@@ -21,25 +21,41 @@ def _has_fused(program: Program, prefix: str) -> bool:
     return any(isinstance(n, FusedNode) and n.kernel.startswith(prefix) for n in program.nodes)
 
 
-class LowerResidentScan(Transform):
-    name = "lower-resident-scan"
-    summary = "unrolled chunk_h scan -> chunk_h_scan FusedNode (resident S)"
+class _ResidentScanRewrite(Transform):
+    """Shared rewrite of an unrolled chunk scan into one resident-state scan key.
+
+    The canonical builders unroll the inter-chunk recurrence: per chunk c they emit
+    W S_c, v_new = U - W S_c, a key scaling, the (k')^T v_new update and the decayed
+    state S_{c+1}, then stack the states (``h_flat``) and the v_new (``vn_flat``). On
+    the device the recurrence belongs in one kernel that keeps S on chip, so the whole
+    per-chunk block is replaced by:
+
+      k' = kb5 * <key coefficient>        (the decay from each token to the chunk end)
+      [W, U, k'] -> token-major [B, nc, C, H, D] views
+      chunk_h_scan(W, U, k', decay)     -> every chunk's entry state and the final one
+      h_flat = entry states as [M, D, D]; vn_flat = U - W h_flat (all chunks at once)
+
+    Subclasses name the program input that identifies the forward, the per-chunk node
+    names to drop (format strings of the chunk index c and c1 = c + 1), the key coefficient, the decay's shape and whether it is per key
+    dimension."""
+
+    key_coef: str
+    chunk_names: tuple
+    perdim: bool
 
     def __init__(self, B: int, H: int, nc: int, C: int, D: int,
                  work: torch.dtype = torch.float16) -> None:
         self.B, self.H, self.nc, self.C, self.D, self.work = B, H, nc, C, D, work
 
     def _region(self, program: Program):
-        if _has_fused(program, "chunk_h_scan") or "coef_vcs" not in program.inputs:
+        if _has_fused(program, "chunk_h_scan") or self.key_coef not in program.inputs:
             return None
-        prod = producer_index(program)
-        if not {"S0", "h_flat", "vn_flat"} <= set(prod):
+        made = set(producer_index(program))
+        if not {"S0", "h_flat", "vn_flat"} <= made:
             return None
-        names = {"S0", "h_bh", "h_flat", "vn_bh", "vn_flat"}
-        for c in range(self.nc):
-            names |= {f"Wc{c}_s", f"Wc{c}", f"WS{c}", f"Uc{c}", f"vn{c}", f"vcs{c}", f"vn2{c}",
-                      f"kc{c}_s", f"kc{c}", f"dS{c}", f"sc{c}", f"Sd{c}", f"S{c + 1}"}
-        drop = {i for i, n in enumerate(program.nodes) if set(node_outputs(n)) & names}
+        doomed = {"S0", "h_bh", "h_flat", "vn_bh", "vn_flat"}
+        doomed.update(n.format(c=c, c1=c + 1) for c in range(self.nc) for n in self.chunk_names)
+        drop = {i for i, n in enumerate(program.nodes) if doomed.intersection(node_outputs(n))}
         return (drop, min(drop)) if drop else None
 
     def match(self, program: Program) -> int:
@@ -48,28 +64,43 @@ class LowerResidentScan(Transform):
     def apply(self, program: Program) -> TransformResult:
         region = self._region(program)
         if region is None:
-            return TransformResult(program, False, 0, "no canonical scan region")
+            return TransformResult(program, False, 0, f"{self.name}: no unrolled scan")
         drop, at = region
         B, H, nc, C, D, w = self.B, self.H, self.nc, self.C, self.D, self.work
-        M = B * H * nc
-        new = [VecGlueNode("mul", ["kb5", "coef_vcs"], "k_vcs", out_dtype=w)]
-        # the scan kernel takes token-major [B, nc, C, H, D] operands
-        for nm, src in (("sw", "Wb"), ("su", "Ub"), ("sk", "k_vcs")):
-            new.append(TensorOp("reshape", [src], f"{nm}5", params={"shape": [B, H, nc, C, D]}))
-            new.append(TensorOp("permute", [f"{nm}5"], nm, params={"dims": (0, 2, 3, 1, 4)}))
-        new += [
-            TensorOp("reshape", ["coef_S"], "sdecay", params={"shape": [B, H, nc]}),
-            FusedNode(kernel="chunk_h_scan", inputs=["sw", "su", "sk", "sdecay"],
-                      outputs=["h_out_k", "final_k"], params={"B": B, "H": H, "nc": nc},
-                      subsumes=["nc per-chunk WS / kv contraction pairs + residual glue"]),
-            TensorOp("permute", ["h_out_k"], "h_bhn", params={"dims": (0, 2, 1, 3, 4)}),
-            TensorOp("reshape", ["h_bhn"], "h_flat", params={"shape": [M, D, D]}),
+        tok_major = lambda src, dst: [
+            TensorOp("reshape", [src], dst + "_5d", params={"shape": [B, H, nc, C, D]}),
+            TensorOp("permute", [dst + "_5d"], dst, params={"dims": (0, 2, 3, 1, 4)})]
+        decay_shape = [B, H, nc, D] if self.perdim else [B, H, nc]
+        params = {"B": B, "H": H, "nc": nc}
+        if self.perdim:
+            params["perdim_decay"] = True
+        body = [VecGlueNode("mul", ["kb5", self.key_coef], "scan_k", out_dtype=w)]
+        body += tok_major("Wb", "scan_w") + tok_major("Ub", "scan_u") + tok_major("scan_k", "scan_kt")
+        body += [
+            TensorOp("reshape", ["coef_S"], "scan_decay", params={"shape": decay_shape}),
+            FusedNode(kernel="chunk_h_scan", inputs=["scan_w", "scan_u", "scan_kt", "scan_decay"],
+                      outputs=["scan_h", "scan_final"], params=params,
+                      subsumes=[f"the {nc} unrolled state updates and their glue"]),
+            TensorOp("permute", ["scan_h"], "scan_h_bh", params={"dims": (0, 2, 1, 3, 4)}),
+            TensorOp("reshape", ["scan_h_bh"], "h_flat", params={"shape": [B * H * nc, D, D]}),
             EinsumNode("nid,nde->nie", ["W_m", "h_flat"], "WS_all", out_dtype=w,
                        read_mode="NN", fuse_out=False),
             VecGlueNode("sub", ["U_m", "WS_all"], "vn_flat", out_dtype=w),
         ]
-        return TransformResult(splice(program, drop, at, new), True, 1,
-                               f"scan of {nc} chunks -> chunk_h_scan (resident state)")
+        kind = "per-dimension " if self.perdim else ""
+        return TransformResult(splice(program, drop, at, body), True, 1,
+                               f"{nc}-chunk {kind}scan -> chunk_h_scan (state resident)")
+
+
+class LowerResidentScan(_ResidentScanRewrite):
+    """GDN: scalar per-chunk decay (the reference's rewrite of the same name,
+    src/pto_fuser/transforms/gdn.py:30-102)."""
+    name = "lower-resident-scan"
+    summary = "unrolled chunk_h scan -> chunk_h_scan FusedNode (resident S)"
+    key_coef = "coef_vcs"
+    chunk_names = ("Wc{c}_s", "Wc{c}", "WS{c}", "Uc{c}", "vn{c}", "vcs{c}", "vn2{c}", "kc{c}_s",
+                   "kc{c}", "dS{c}", "sc{c}", "Sd{c}", "S{c1}")
+    perdim = False
 
 
 # names the canonical GDN builder emits for each stage (its documented contract)
