@@ -510,6 +510,22 @@ def run_configs(args):
     fwd("cfg4", "long-context GDN bf16 B1 H64 T131072 D128, S0 ~ N(0,0.02^2), mu 3", 1, 64,
         131072, 128, torch.bfloat16, mu=3.0, s0_std=0.02)
 
+    # config 4 through the head/tail split inside the GPU (segment.GDNLocalSplit): 64
+    # pairs leave 84 SMs idle in the serial forward; the plan is the measured best of
+    # a sweep (a 80,896-token head, 7 tail segments of 7,168 tokens)
+    from pto_fuser.segment import GDNLocalSplit
+    B, H, T, D = 1, 64, 131072, 128
+    q, k, v, beta, g = inputs(B, H, T, D, torch.bfloat16, 3.0, True)
+    S0 = torch.randn(H, D, D, device=dev, generator=gen) * 0.02
+    sp = GDNLocalSplit(H, T, D, 80896, 7, 7168, device=dev)
+    o = torch.empty(H, T, D, device=dev, dtype=torch.bfloat16)
+    ms = timed(lambda: sp(q[0], k[0], v[0], beta[0], g[0], S0, o=o), args.steps)
+    sp.check_status()
+    line("cfg4-split", "long-context GDN B1 H64 T131072 D128, S0, head/tail split in one GPU",
+         ms, B * T, B * H * T * 1030 + B * H * D * D * 4 * 2, "bfloat16")
+    sp.close()
+    del q, k, v, beta, g, o
+
     # KDA (per-dimension gate; the reference's next family): the fused tensor-core
     # forward at config 3's shape, g = -U(0,1) * 0.05 per token and dimension
     from pto_fuser import KDAChunkForward
