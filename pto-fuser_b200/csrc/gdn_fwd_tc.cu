@@ -77,7 +77,7 @@ struct Layout {
   static constexpr bool SA_TMEM = (DV == 128);
   static constexpr bool VN_TMEM = SA_TMEM;
   // input ring (4 stages): [K | Q] per 64-wide d block, then the per-token arrays
-  static constexpr int NIN = 4;
+  static constexpr int NIN = (DK == 128) ? 3 : 4;
   // K rows 0-63 | Q rows 64-127 (16 KB); KDA adds K e^{-g} in rows 128-191 (24 KB)
   static constexpr int KQ_REGION = (KDA ? 3 : 2) * kC * 128;
   static constexpr int OFF_K2 = 2 * kC * 128;        // KDA: K e^{-g} within a region
