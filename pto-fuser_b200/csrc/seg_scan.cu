@@ -9,7 +9,7 @@
 //   X_0 = X0 (or 0),   X_{j+1} = A_j X_j (+ B_j)
 //
 // writing the entry state X_j of every segment (Xout) and the exit state X_nseg
-// (Xfinal). One CTA owns 32 state columns of one head: the columns stay in shared
+// (Xfinal). One CTA owns 16 state columns of one head: the columns stay in shared
 // memory across segments and A_j streams into shared memory (double-buffered) once
 // per segment, so the work per segment is one [Dk,Dk] x [Dk,32] fp32 product. The same kernel
 // composes two maps (A1,B1) o (A0,B0) = (A1 A0, A1 B0 + B1) by scanning X0 = A0 with
@@ -30,7 +30,8 @@ struct Params {
   int nseg, Dv;
 };
 
-constexpr int kCols = 32;
+constexpr int kCols = 16;              // state columns per CTA
+constexpr int kGroups = kCols / 4;     // 4-column thread groups
 constexpr int kThreads = 256;
 
 // 16-byte asynchronous global -> shared copy (completion by cp.async.wait_group)
@@ -43,8 +44,9 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// Thread tile: R = D / 32 rows x 4 columns (thread t: columns 4 (t % 8), rows
-// R (t / 8)). A_j rows are padded to D + 4 floats so the R rows a warp reads at one
+// Thread tile: R = D kGroups / 256 rows x 4 columns (thread t: columns 4 (t % kGroups),
+// rows R (t / kGroups)); 16 columns per CTA, so a head's state spreads over Dv / 16
+// CTAs (the scan is latency-bound: more CTAs, shorter per-segment products). A_j rows are padded to D + 4 floats so the R rows a warp reads at one
 // k fall in different banks; A_{j+1} streams into the second buffer (cp.async) while
 // A_j is applied.
 template <int D>
@@ -69,15 +71,15 @@ template <int D>
 __global__ void __launch_bounds__(kThreads) seg_scan_kernel(Params p) {
   using SL = SLayout<D>;
   constexpr int AP = SL::AP;
-  constexpr int R = D / 32;
+  constexpr int R = D * kGroups / kThreads;              // rows per thread
   extern __shared__ __align__(16) float smem[];
   float* Abuf = smem;                                    // 2 x [D][AP]
   float* cur = smem + 2 * SL::A_FLOATS;                  // [D][kCols] running state columns
   const int head = blockIdx.x;
   const int c0 = blockIdx.y * kCols;
   const int t = threadIdx.x;
-  const int cq = (t % 8) * 4;                            // this thread's 4 columns
-  const int r0 = (t / 8) * R;                            // and R rows
+  const int cq = (t % kGroups) * 4;                      // this thread's 4 columns
+  const int r0 = (t / kGroups) * R;                      // and R rows
   const int Dv = p.Dv;
 
   if (p.nseg > 0) load_a_async<D>(Abuf, p.A + head * p.a_hs, t);
@@ -172,7 +174,7 @@ int ptof_seg_scan_exec(const float* A, int64_t a_head_stride, int64_t a_seg_stri
   if (heads < 1 || heads > 65535 || nseg < 0 || (D != 64 && D != 128) || Dv < segscan::kCols ||
       Dv % segscan::kCols || Dv / segscan::kCols > 65535)
     return fail(PTOF_EINVAL, "seg_scan shape heads=%d nseg=%d D=%d Dv=%d (D in {64,128}, "
-                "Dv a multiple of 32)", heads, nseg, D, Dv);
+                "Dv a multiple of 16)", heads, nseg, D, Dv);
   if (nseg > 0 && !A) return fail(PTOF_EINVAL, "seg_scan: A is NULL with nseg=%d", nseg);
   if (!Xout && !Xfinal) return fail(PTOF_EINVAL, "seg_scan: no output (Xout and Xfinal NULL)");
   if (a_head_stride < 0 || a_seg_stride < 0 || b_head_stride < 0 || b_seg_stride < 0 ||
