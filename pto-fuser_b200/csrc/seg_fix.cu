@@ -12,9 +12,10 @@
 //   o tile = o^B tile (TMA) + D, stored back with a TMA tensor store.
 //
 // Persistent CTAs (one per SM) walk contiguous tile ranges, so a CTA restages X only
-// when its range crosses a segment boundary. Roles (192 threads):
-//   warp 4  producer: TMA loads of o^A and o^B tiles (2 stages), X staging
+// when its range crosses a segment boundary. Roles (320 threads):
+//   warp 4  producer: TMA loads of o^A and o^B tiles (2 stages for D = 128, 4 for D = 64)
 //   warp 5  TMEM owner and UMMA issuer (one thread; two accumulators)
+//   warps 6-9 X staging: fp32 -> 16-bit, two buffers
 //   warps 0-3 epilogue: TMEM -> registers, + o^B from shared memory, TMA store.
 // HBM-bound: per token 2 Dk bytes of o^A read, 2 Dv bytes of o read and written.
 #include <cuda_runtime.h>
@@ -27,23 +28,29 @@ namespace ptof {
 namespace segfix {
 
 constexpr int kRows = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 
 template <int D>
 struct FLayout {
   static constexpr int NKB = D / 64;
   static constexpr int TILE = NKB * kRows * 128;   // [128 tokens x D] 16-bit, SW128 blocks
   static constexpr int XT = NKB * D * 128;         // X [D k-rows x D n], n-blocks of 64
-  static constexpr int OFF_OA = 0;                 // 2 stages
-  static constexpr int OFF_OB = 2 * TILE;          // 2 stages
-  static constexpr int OFF_X = 4 * TILE;           // 2 buffers
-  static constexpr int OFF_BAR = OFF_X + 2 * XT;
+  // input stages (o^A and o^B tiles) and X buffers (double-buffered, so X restaging
+  // overlaps the previous unit's tiles): four stages for D = 64, two for D = 128
+  // (three beside a single X measured no faster once X staging had its own warps)
+  static constexpr int NS = (D == 128) ? 2 : 4;
+  static constexpr int NX = 2;
+  static constexpr int OFF_OA = 0;
+  static constexpr int OFF_OB = NS * TILE;
+  static constexpr int OFF_X = 2 * NS * TILE;
+  static constexpr int OFF_BAR = OFF_X + NX * XT;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
+  static_assert(BYTES <= 227 * 1024, "seg_fix shared memory");
   static constexpr int TCOLS = 2 * D;
 };
 
-enum FBar { F_FULL0 = 0, F_EMPTY0 = 2, F_TFULL0 = 4, F_TFREE0 = 6, F_XFULL0 = 8, F_XFREE0 = 10,
-            F_DONE = 12, F_COUNT = 13 };
+enum FBar { F_FULL0 = 0, F_EMPTY0 = 4, F_TFULL0 = 8, F_TFREE0 = 10, F_XFULL0 = 12, F_XFREE0 = 14,
+            F_DONE = 16, F_COUNT = 17 };
 static_assert(F_COUNT * 8 + 8 <= 256, "barrier area");
 
 struct FParams {
@@ -94,13 +101,13 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       prefetch_tmap(&P.mapOA);
       prefetch_tmap(&P.mapO);
     }
-    int cur = -1, f = 0;   // segment whose X is staged; X fills so far
     int64_t issued = 0;    // tiles whose loads were issued
     for (int64_t i = 0; i < cnt; ++i) {
-      const int s = static_cast<int>(i & 1);
+      const int s = static_cast<int>(i % L::NS);
       // after a wait gave up (here or in another warp) no further load is issued; the
-      // decision is warp-uniform (the X staging below synchronises the warp)
-      bool ok = i < 2 || wait(&bars[F_EMPTY0 + s], static_cast<uint32_t>(((i >> 1) + 1) & 1), 1);
+      // decision is warp-uniform
+      bool ok = i < L::NS ||
+                wait(&bars[F_EMPTY0 + s], static_cast<uint32_t>(((i / L::NS) + 1) & 1), 1);
       if (!__all_sync(0xffffffffu, ok && !abort_flag)) break;
       issued = i + 1;
       if (lane == 0) {
@@ -121,37 +128,13 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
                         &bars[F_FULL0 + s], kb * 64, y);
         }
       }
-      const int u = unit_of(i);
-      if (u != cur) {
-        const int xb = f & 1;
-        const bool okx =
-            f < 2 || wait(&bars[F_XFREE0 + xb], static_cast<uint32_t>(((f - 2) >> 1) & 1), 2);
-        if (!__all_sync(0xffffffffu, okx)) break;
-        // X[k][n] fp32 -> 16-bit, MN-major SW128: n-block n/64, row k, byte 2 (n % 64)
-        unsigned char* xs = sm + L::OFF_X + xb * L::XT;
-        const float4* xg = reinterpret_cast<const float4*>(P.X + static_cast<int64_t>(u) * D * D);
-#pragma unroll 4
-        for (int idx = lane; idx < D * D / 4; idx += 32) {
-          const float4 x = xg[idx];
-          const int k = idx / (D / 4), n = (idx % (D / 4)) * 4;
-          const uint32_t lo = BF16 ? pack_bf16(x.x, x.y) : pack_f16(x.x, x.y);
-          const uint32_t hi = BF16 ? pack_bf16(x.z, x.w) : pack_f16(x.z, x.w);
-          *reinterpret_cast<uint2*>(xs + (n >> 6) * (D * 128) + sw128_off(k, (n & 63) * 2)) =
-              make_uint2(lo, hi);
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[F_XFULL0 + xb]);
-        cur = u;
-        ++f;
-      }
     }
     // drain: the CTA must not exit (or release its shared memory) with TMA loads in
-    // flight, so wait (bounded, also after an abort) for the last two tiles' loads
+    // flight, so wait (bounded, also after an abort) for the last NS tiles' loads
     if (lane == 0) {
-      for (int64_t i = issued > 2 ? issued - 2 : 0; i < issued; ++i) {
+      for (int64_t i = issued > L::NS ? issued - L::NS : 0; i < issued; ++i) {
         const uint64_t t_0 = globaltimer_ns();
-        while (!mbar_try_wait(&bars[F_FULL0 + (i & 1)], static_cast<uint32_t>((i >> 1) & 1)) &&
+        while (!mbar_try_wait(&bars[F_FULL0 + i % L::NS], static_cast<uint32_t>((i / L::NS) & 1)) &&
                globaltimer_ns() - t_0 < kWaitTimeoutNs) {
         }
       }
@@ -162,37 +145,72 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
       constexpr uint32_t ID = idesc_f16(kRows, D, false, true, BF16);
       int cur = -1, f = -1;
       for (int64_t i = 0; i < cnt; ++i) {
-        const int s = static_cast<int>(i & 1), b = s;
+        const int s = static_cast<int>(i % L::NS), b = static_cast<int>(i & 1);
         const int u = unit_of(i);
         if (u != cur) {
-          if (f >= 0) umma_commit(&bars[F_XFREE0 + (f & 1)]);   // old X no longer read
+          if (f >= 0) umma_commit(&bars[F_XFREE0 + f % L::NX]);   // old X no longer read
           ++f;
-          if (!wait(&bars[F_XFULL0 + (f & 1)], static_cast<uint32_t>((f >> 1) & 1), 3)) break;
+          if (!wait(&bars[F_XFULL0 + f % L::NX], static_cast<uint32_t>((f / L::NX) & 1), 3)) break;
           cur = u;
         }
-        if (!wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 4)) break;
+        if (!wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i / L::NS) & 1), 4)) break;
         if (i >= 2 && !wait(&bars[F_TFREE0 + b], static_cast<uint32_t>(((i >> 1) + 1) & 1), 5))
           break;
         tc_fence_after();
         const uint32_t a = smem_u32(sm + L::OFF_OA + s * L::TILE);
-        const uint32_t x = smem_u32(sm + L::OFF_X + (f & 1) * L::XT);
+        const uint32_t x = smem_u32(sm + L::OFF_X + (f % L::NX) * L::XT);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
           umma_ss(tmem + b * D, sdesc_sw128(a + (ks >> 2) * (kRows * 128) + (ks & 3) * 32, 16, 1024),
                   sdesc_sw128(x + ks * 2048, D * 128, 1024), ID, ks > 0);
         umma_commit(&bars[F_TFULL0 + b]);
       }
-      if (f >= 0) umma_commit(&bars[F_XFREE0 + (f & 1)]);
+      if (f >= 0) umma_commit(&bars[F_XFREE0 + f % L::NX]);
       umma_commit(&bars[F_DONE]);   // arrives once every UMMA issued above has retired
+    }
+  } else if (warp >= 6) {
+    // ================================ X staging ===============================
+    // one fill per unit the CTA's tile range touches, in the issuer's order; the
+    // break decisions are uniform over the group (barrier OR)
+    const int xt = tid - 6 * 32;
+    const int u_first = unit_of(0), u_end = cnt > 0 ? unit_of(cnt - 1) + 1 : u_first;
+    for (int u = u_first, f = 0; u < u_end; ++u, ++f) {
+      const int xb = f % L::NX;
+      const bool ok = f < L::NX ||
+                      wait(&bars[F_XFREE0 + xb], static_cast<uint32_t>(((f / L::NX) + 1) & 1), 2);
+      if (named_bar_or(2, 128, !ok || abort_flag != 0)) break;
+      // X[k][n] fp32 -> 16-bit, MN-major SW128: n-block n/64, row k, byte 2 (n % 64)
+      unsigned char* xs = sm + L::OFF_X + xb * L::XT;
+      const float4* xg = reinterpret_cast<const float4*>(P.X + static_cast<int64_t>(u) * D * D);
+      constexpr int PER = D * D / 4 / 128;   // float4s per thread
+      static_assert(PER % 8 == 0, "X staging batches");
+#pragma unroll 1
+      for (int j0 = 0; j0 < PER; j0 += 8) {
+        float4 x[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = __ldg(xg + (j0 + j) * 128 + xt);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int idx = (j0 + j) * 128 + xt;
+          const int k = idx / (D / 4), n = (idx % (D / 4)) * 4;
+          const uint32_t lo = BF16 ? pack_bf16(x[j].x, x[j].y) : pack_f16(x[j].x, x[j].y);
+          const uint32_t hi = BF16 ? pack_bf16(x[j].z, x[j].w) : pack_f16(x[j].z, x[j].w);
+          *reinterpret_cast<uint2*>(xs + (n >> 6) * (D * 128) + sw128_off(k, (n & 63) * 2)) =
+              make_uint2(lo, hi);
+        }
+      }
+      fence_async_smem();
+      named_bar_sync(3, 128);
+      if (xt == 0) mbar_arrive(&bars[F_XFULL0 + xb]);
     }
   } else {
     // =============================== epilogue =================================
     const int r = tid;   // tile row = TMEM lane
     for (int64_t i = 0; i < cnt; ++i) {
-      const int s = static_cast<int>(i & 1), b = s;
+      const int s = static_cast<int>(i % L::NS), b = static_cast<int>(i & 1);
       // o^B visible, then the product (after an abort the waits return at once and
       // the barrier below ends the loop for the whole warpgroup)
-      wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i >> 1) & 1), 6);
+      wait(&bars[F_FULL0 + s], static_cast<uint32_t>((i / L::NS) & 1), 6);
       wait(&bars[F_TFULL0 + b], static_cast<uint32_t>((i >> 1) & 1), 7);
       tc_fence_after();
       unsigned char* ob = sm + L::OFF_OB + s * L::TILE;
@@ -260,7 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1) seg_fix_kernel(const __grid_const
 template <int D, bool BF16>
 int launch_t(int* status, void* o, const void* oa, const float* X, int units, int Tseg,
              cudaStream_t st, int view_segs = 0, long long o_pair = 0, long long o_seg = 0) {
-  using L = FLayout<D>;
   FParams P;
   const CUtensorMapDataType t = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const uint64_t rows = static_cast<uint64_t>(units) * Tseg;
@@ -289,13 +306,14 @@ int launch_t(int* status, void* o, const void* oa, const float* X, int units, in
   P.tiles_per_unit = Tseg / kRows;
   P.tiles = static_cast<int64_t>(units) * P.tiles_per_unit;
   auto kern = seg_fix_kernel<D, BF16>;
-  cudaError_t e = set_smem_once(kern, L::BYTES);
+  const int bytes = FLayout<D>::BYTES;
+  cudaError_t e = set_smem_once(kern, bytes);
   if (e != cudaSuccess) return cuda_fail(e, "seg_fix smem attribute");
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t grid = P.tiles < sms ? P.tiles : sms;
-  kern<<<static_cast<unsigned>(grid), kThreads, L::BYTES, st>>>(P);
+  kern<<<static_cast<unsigned>(grid), kThreads, bytes, st>>>(P);
   e = cudaGetLastError();
   return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "seg_fix launch");
 }
