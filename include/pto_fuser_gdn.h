@@ -127,13 +127,19 @@ PTOF_API int ptof_gdn_fwd_varlen_exec(void* ws, const void* q, const void* k, co
  *     device current (cudaGetSymbolAddress); make it before any stream capture;
  *   - every call shares the one array, so calls whose kernels overlap on the GPU
  *     (other streams, other host threads) race and corrupt each other's results;
- *   - there is no status word: a device-side wait that gives up ends the kernel
- *     early without a report (ptof_check_status does not apply).
+ *   - its bounded device waits report to a library status word of its own, read
+ *     with ptof_gdn_fwd_noalloc_status (ptof_check_status takes a workspace).
  * Inputs and outputs are as for ptof_gdn_fwd_exec; the call launches on `stream`
  * and does not synchronise. */
 PTOF_API int ptof_gdn_fwd_exec_noalloc(const ptof_gdn_params* p, const void* q, const void* k,
                                        const void* v, const void* beta, const float* g,
                                        const float* S0, void* o, float* S_final, void* stream);
+
+/* Status of the allocation-free forwards on the current device: synchronises `stream`,
+ * then reads and clears the status word they share. PTOF_OK, or PTOF_ETIMEOUT when a
+ * bounded device wait of one of them gave up since the last read (its outputs are then
+ * undefined). Allocates nothing. */
+PTOF_API int ptof_gdn_fwd_noalloc_status(void* stream);
 
 /* ---------------------------------------------------------------------------
  * Kernels behind the reference's finer-grained fused-node keys. They share one

@@ -1406,15 +1406,42 @@ int launch_gdn_fwd_tc(Workspace* w, const void* q, const void* k, const void* v,
 // off limits (inside a host allocator or an arena that owns all device memory, or
 // between the set-up and replay of a fixed memory plan) cannot create a workspace.
 // ptof_gdn_fwd_exec_noalloc runs the same tensor-core forward with its coefficient
-// records in this file-scope array instead of a workspace buffer. Its size is fixed:
-// every GPU that loads the library reserves it until the process exits.
+// records in this file-scope array instead of a workspace buffer, and its bounded
+// waits report to a file-scope status word (ptof_gdn_fwd_noalloc_status). The array's
+// size is fixed: every GPU that loads the library reserves it until the process exits.
 namespace {
 constexpr int64_t kNoAllocMaxChunks = 4096;   // B * H * T / 64, i.e. 262,144 head-tokens
 static __device__ __align__(256) unsigned char
     g_noalloc_coef[kNoAllocMaxChunks * tcfwd::coef::BYTES];   // 7.4 MB
+static __device__ int g_noalloc_status;
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
+void* g_noalloc_status_ptr[kMaxDevices] = {};
+
+// The device addresses of the array and the status word on the current device, looked
+// up once per device with that device current (in host code the symbols themselves are
+// only host-side stand-ins). Returns PTOF_OK or an error.
+int noalloc_symbols(int* dev_out, void** coef, int** status) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PTOF_EUNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* c = nullptr;
+    void* st = nullptr;
+    e = cudaGetSymbolAddress(&c, g_noalloc_coef);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&st, g_noalloc_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(allocation-free arrays)");
+    g_noalloc_status_ptr[dev] = st;
+    g_noalloc_ptr[dev] = c;
+  }
+  *dev_out = dev;
+  *coef = g_noalloc_ptr[dev];
+  *status = static_cast<int*>(g_noalloc_status_ptr[dev]);
+  return PTOF_OK;
+}
 }  // namespace
 
 }  // namespace ptof
@@ -1440,36 +1467,42 @@ extern "C" int ptof_gdn_fwd_exec_noalloc(const ptof_gdn_params* p, const void* q
   if (rc) return rc;
   if (p->gate_mode != PTOF_GATE_NONE && !g) return fail(PTOF_EINVAL, "g is NULL for a gated forward");
   int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(PTOF_EUNSUPPORTED, "device index %d", dev);
   void* base = nullptr;
-  {
-    // the array's device address, looked up once per device with that device
-    // current (in host code the symbol itself is only a host-side stand-in)
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-      e = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_coef);
-      if (e != cudaSuccess) {
-        g_noalloc_ptr[dev] = nullptr;
-        return cuda_fail(e, "cudaGetSymbolAddress(coefficient array)");
-      }
-    }
-    base = g_noalloc_ptr[dev];
-  }
-  // A workspace on the stack pointing at the array: no status word (a device-side
-  // wait that gives up ends the kernel early without a report), no trace. The
-  // coefficient pre-pass rewrites every record the forward reads, so nothing in the
-  // array has to start at zero.
+  int* status = nullptr;
+  rc = noalloc_symbols(&dev, &base, &status);
+  if (rc) return rc;
+  // A workspace on the stack pointing at the file-scope array and status word, no
+  // trace. The coefficient pre-pass rewrites every record the forward reads, so
+  // nothing in the array has to start at zero.
   Workspace w;
   w.kind = kWsGdnFwd;
   w.device = dev;
   w.p = *p;
-  w.d_status = nullptr;
+  w.d_status = status;
   w.d_scratch = base;
   w.scratch_bytes = static_cast<size_t>(kNoAllocMaxChunks) * tcfwd::coef::BYTES;
   return launch_gdn_fwd_tc(&w, q, k, v, beta, g, S0, o, S_final, nullptr,
                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ptof_gdn_fwd_noalloc_status(void* stream) {
+  using namespace ptof;
+  int dev = -1;
+  void* base = nullptr;
+  int* status = nullptr;
+  int rc = noalloc_symbols(&dev, &base, &status);
+  if (rc) return rc;
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+  int h = 0;
+  e = cudaMemcpy(&h, status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "status read");
+  if (h != 0) {
+    e = cudaMemset(status, 0, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "status clear");
+    return fail(PTOF_ETIMEOUT, "allocation-free forward: device wait gave up at site %d", h);
+  }
+  return PTOF_OK;
 }
 
 // ----------------------------------------------------------------- KDA C ABI ----

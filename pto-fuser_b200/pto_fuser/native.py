@@ -63,6 +63,7 @@ _SIGNATURES = {
     "ptof_kda_fwd_setup": (_vp, [ctypes.POINTER(GdnParams)]),
     "ptof_kda_fwd_exec": (_i32, [_vp] * 10),
     "ptof_gdn_fwd_exec_noalloc": (_i32, [ctypes.POINTER(GdnParams)] + [_vp] * 9),
+    "ptof_gdn_fwd_noalloc_status": (_i32, [_vp]),
     "ptof_seg_scan_exec": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64,
                                   _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
     "ptof_seg_fix_exec": (_i32, [_vp] * 4 + [_i32] * 4 + [_vp]),

@@ -54,6 +54,8 @@ def test_noalloc_matches_workspace_entry_twice(D):
         ref_o, ref_S = runner(inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"])
         torch.cuda.synchronize()
         runner.check_status()
+        # the entry's own status word: no bounded wait gave up
+        nv.check(nv.lib().ptof_gdn_fwd_noalloc_status(nv.stream_handle()))
         assert torch.isfinite(o.float()).all() and torch.isfinite(S).all()
         assert torch.equal(o, ref_o) and torch.equal(S, ref_S), (
             seed, _rel_l2(o, ref_o), _rel_l2(S, ref_S))
