@@ -9,9 +9,9 @@
 //   X_0 = X0 (or 0),   X_{j+1} = A_j X_j (+ B_j)
 //
 // writing the entry state X_j of every segment (Xout) and the exit state X_nseg
-// (Xfinal). One CTA owns 16 state columns of one head: the columns stay in shared
-// memory across segments and A_j streams into shared memory (double-buffered) once
-// per segment, so the work per segment is one [Dk,Dk] x [Dk,32] fp32 product. The same kernel
+// (Xfinal). One CTA owns 16 or 32 state columns of one head: the columns stay in
+// shared memory across segments and A_j streams into shared memory (double-buffered)
+// once per segment, so the work per segment is one [Dk,Dk] x [Dk,cols] fp32 product. The same kernel
 // composes two maps (A1,B1) o (A0,B0) = (A1 A0, A1 B0 + B1) by scanning X0 = A0 with
 // no offset and X0 = B0 with offset B1.
 #include <cstdint>
@@ -30,9 +30,8 @@ struct Params {
   int nseg, Dv;
 };
 
-constexpr int kCols = 16;              // state columns per CTA
-constexpr int kGroups = kCols / 4;     // 4-column thread groups
 constexpr int kThreads = 256;
+constexpr int kMinCols = 16;           // Dv granularity
 
 // 16-byte asynchronous global -> shared copy (completion by cp.async.wait_group)
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -44,21 +43,22 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// Thread tile: R = D kGroups / 256 rows x 4 columns (thread t: columns 4 (t % kGroups),
-// rows R (t / kGroups)); 16 columns per CTA, so a head's state spreads over Dv / 16
-// CTAs (the scan is latency-bound: more CTAs, shorter per-segment products). A_j rows are padded to D + 4 floats so the R rows a warp reads at one
-// k fall in different banks; A_{j+1} streams into the second buffer (cp.async) while
-// A_j is applied.
-template <int D>
+// Thread tile: R = D (COLS / 4) / 256 rows x 4 columns (thread t: columns
+// 4 (t % (COLS / 4)), rows R (t / (COLS / 4))); a head's state spreads over Dv / COLS
+// CTAs. Every CTA streams the whole A_j, so fewer columns per CTA only pay while the
+// grid would leave SMs idle (the launch picks 16 then, else 32). A_j rows are padded
+// to D + 4 floats so the R rows a warp reads at one k fall in different banks; A_{j+1}
+// streams into the second buffer (cp.async) while A_j is applied.
+template <int D, int COLS>
 struct SLayout {
   static constexpr int AP = D + 4;                       // padded A row (floats)
   static constexpr int A_FLOATS = D * AP;
-  static constexpr int BYTES = (2 * A_FLOATS + D * kCols) * 4;
+  static constexpr int BYTES = (2 * A_FLOATS + D * COLS) * 4;
 };
 
 template <int D>
 __device__ __forceinline__ void load_a_async(float* As, const float* a, int t) {
-  constexpr int AP = SLayout<D>::AP;
+  constexpr int AP = D + 4;
 #pragma unroll 4
   for (int e = t; e < D * D / 4; e += kThreads) {
     const int row = e / (D / 4), c4 = e % (D / 4);
@@ -67,10 +67,11 @@ __device__ __forceinline__ void load_a_async(float* As, const float* a, int t) {
   cp_async_commit();
 }
 
-template <int D>
+template <int D, int COLS>
 __global__ void __launch_bounds__(kThreads) seg_scan_kernel(Params p) {
-  using SL = SLayout<D>;
+  using SL = SLayout<D, COLS>;
   constexpr int AP = SL::AP;
+  constexpr int kCols = COLS, kGroups = COLS / 4;        // 4-column thread groups
   constexpr int R = D * kGroups / kThreads;              // rows per thread
   extern __shared__ __align__(16) float smem[];
   float* Abuf = smem;                                    // 2 x [D][AP]
@@ -150,14 +151,24 @@ __global__ void __launch_bounds__(kThreads) seg_scan_kernel(Params p) {
   }
 }
 
-template <int D>
-int launch(const Params& p, int heads, cudaStream_t st) {
-  const int smem = SLayout<D>::BYTES;
-  cudaError_t e = set_smem_once(seg_scan_kernel<D>, smem);
+template <int D, int COLS>
+int launch_c(const Params& p, int heads, cudaStream_t st) {
+  const int smem = SLayout<D, COLS>::BYTES;
+  cudaError_t e = set_smem_once(seg_scan_kernel<D, COLS>, smem);
   if (e != cudaSuccess) return cuda_fail(e, "seg_scan smem attribute");
-  seg_scan_kernel<D><<<dim3(heads, p.Dv / kCols), kThreads, smem, st>>>(p);
+  seg_scan_kernel<D, COLS><<<dim3(heads, p.Dv / COLS), kThreads, smem, st>>>(p);
   e = cudaGetLastError();
   return e == cudaSuccess ? PTOF_OK : cuda_fail(e, "seg_scan launch");
+}
+
+template <int D>
+int launch(const Params& p, int heads, cudaStream_t st) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // one CTA per SM (the A double buffer fills shared memory)
+  const bool wide = p.Dv % 32 == 0 && static_cast<int64_t>(heads) * (p.Dv / 32) >= sms;
+  return wide ? launch_c<D, 32>(p, heads, st) : launch_c<D, 16>(p, heads, st);
 }
 
 }  // namespace segscan
@@ -171,8 +182,8 @@ int ptof_seg_scan_exec(const float* A, int64_t a_head_stride, int64_t a_seg_stri
                        int64_t xout_head_stride, int64_t xout_seg_stride, float* Xfinal,
                        int64_t xfinal_head_stride, int heads, int nseg, int D, int Dv,
                        void* stream) {
-  if (heads < 1 || heads > 65535 || nseg < 0 || (D != 64 && D != 128) || Dv < segscan::kCols ||
-      Dv % segscan::kCols || Dv / segscan::kCols > 65535)
+  if (heads < 1 || heads > 65535 || nseg < 0 || (D != 64 && D != 128) || Dv < segscan::kMinCols ||
+      Dv % segscan::kMinCols || Dv / segscan::kMinCols > 65535)
     return fail(PTOF_EINVAL, "seg_scan shape heads=%d nseg=%d D=%d Dv=%d (D in {64,128}, "
                 "Dv a multiple of 16)", heads, nseg, D, Dv);
   if (nseg > 0 && !A) return fail(PTOF_EINVAL, "seg_scan: A is NULL with nseg=%d", nseg);
