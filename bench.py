@@ -187,20 +187,6 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
-def _segments_for(pairs: int, T: int, sms: int) -> int:
-    """Local token segments for a rank that holds `pairs` (b, h) pairs of length T.
-
-    The forward is one CTA per pair walking its chunks in order, so a shard with
-    fewer pairs than SMs leaves SMs idle. Splitting every pair's sequence into s
-    segments (the chunk-segment scan: an A run and a B run per segment, then a
-    tensor-core fix-up) runs 2 * pairs * s chains of T / s tokens each; s doubles
-    while those chains still fit on the SMs in one wave. 1 means the plain forward."""
-    s = 1
-    while 2 * pairs * (2 * s) <= sms and T % (128 * 2 * s) == 0:
-        s *= 2
-    return s
-
-
 def _nvml_handle(nv, dev):
     """The NVML handle of the CUDA device `dev`, found by UUID (else PCI bus id):
     NVML numbers GPUs in PCI order and ignores CUDA_VISIBLE_DEVICES, so the CUDA
@@ -228,7 +214,7 @@ def run_ours(args):
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
     from pto_fuser import GDNChunkForward, make_gdn_inputs
-    from pto_fuser.segment import GDNSegmentScan
+    from pto_fuser.segment import GDNLocalSplit, plan_local_split
     from pto_fuser.shard import shard_pairs
 
     B, H, T, D = CFG["B"], CFG["H"], CFG["T"], CFG["D"]
@@ -236,13 +222,19 @@ def run_ours(args):
     p0, p1 = shard_pairs(B * H, world, rank)
     P = p1 - p0
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    segs = _segments_for(P, T, sms) if world > 1 else 1
+    # The forward is one CTA per pair walking its chunks in order, so a shard with
+    # fewer pairs than SMs leaves SMs idle: such a rank splits every pair into a head
+    # segment (from the true initial state) and tail segments that run as A and B
+    # chains on the free SMs, composed by seg_scan and fixed up by seg_fix
+    # (segment.plan_local_split; None = the plain forward).
+    plan = plan_local_split(P, T, sms, D=D)
+    segs = 1 if plan is None else 1 + plan[1]
     inp = make_gdn_inputs(1, P, T, D, dtype=torch.bfloat16, device=dev, mu=2.0,
                           seed=1234 + rank)
     o = torch.empty(1, P, T, D, device=dev, dtype=torch.bfloat16)
     S = torch.empty(1, P, D, D, device=dev, dtype=torch.float32)
     stream = torch.cuda.current_stream(dev)
-    if segs == 1:
+    if plan is None:
         runner = GDNChunkForward(1, P, T, D, D, in_dtype=torch.bfloat16, device=dev)
 
         def forward(q, k, v, beta, g, o_, S_):
@@ -250,15 +242,17 @@ def run_ours(args):
         launches = 2   # coefficient pre-pass + fused forward
         how = "plain fused forward, one CTA per (b,h) pair"
     else:
-        runner = GDNSegmentScan(P, T, D, segments=segs, device=dev)
+        L0, ns, Ls = plan
+        runner = GDNLocalSplit(P, T, D, L0, ns, Ls, device=dev)
 
         def forward(q, k, v, beta, g, o_, S_):
             _, Sx = runner(q[0], k[0], v[0], beta[0], g[0], None, o=o_[0])
             S_.view(P, D, D).copy_(Sx)
-        # A and B runs (2 launches each), seg_scan, seg_fix, the final-state copy
-        launches = 7
-        how = (f"chunk-segment scan inside the GPU: {segs} segments per pair, "
-               f"{2 * P * segs} chains of {T // segs} tokens")
+        # head, tail B and tail A runs (coefficient pre-pass + forward each), seg_scan,
+        # seg_fix (the final-state copy is a torch copy)
+        launches = 8
+        how = (f"head/tail split inside the GPU: per pair a {L0}-token head and {ns} "
+               f"tail segments of {Ls} tokens; {P} head chains + {2 * P * ns} tail chains")
 
     def step():
         forward(inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"], o, S)
@@ -409,10 +403,10 @@ def run_ours(args):
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                             "frac": achieved / peak,
                             "traffic": (FWD_DRAM_BYTES_PER_HEAD_TOKEN * P * T
-                                        if segs == 1 and not args.shape else None),
+                                        if plan is None and not args.shape else None),
                             "peak_kind": peak_kind,
                             "kernel": ("gdn_coef_kernel + gdn_fwd_tc_kernel (one forward call)"
-                                       if segs == 1 else "whole segment-scan step"),
+                                       if plan is None else "whole split step"),
                             "algo_bytes_per_launch": algo, "avg_launch_ms": kern_ms,
                             "tflops": _algo_flops(1, P, T, D) / (kern_ms / 1e3) / 1e12},
                "cpu_baseline": cpu,

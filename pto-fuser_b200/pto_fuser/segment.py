@@ -245,7 +245,7 @@ class GDNSegmentScan:
 # --------------------------------------------------------------------------------
 def plan_local_split(pairs: int, T: int, sms: int, *, chunk_us: float = 3.0,
                      serial_chunk_us: float = 2.4, fix_gbs: float = 4000.0,
-                     fixed_us: float = 40.0, cta_us: float = 15.0, max_rounds: int = 2,
+                     fixed_us: float = 40.0, cta_us: float = 15.0, max_rounds: int = 1,
                      D: int = 128
                      ) -> Optional[Tuple[int, int, int]]:
     """Head/tail split of ``pairs`` sequences of T tokens on ``sms`` SMs, or None when
@@ -254,14 +254,18 @@ def plan_local_split(pairs: int, T: int, sms: int, *, chunk_us: float = 3.0,
     The forward is one CTA per chain walking its chunks in order, so with fewer pairs
     than SMs the chains, not the SMs, set the time: ≈ ``serial_chunk_us`` per chunk when
     one chain per pair runs, ≈ ``chunk_us`` once the split fills every SM (both
-    measured on B200: a split of 64 pairs x 16,384 tokens never beat the serial 0.61 ms,
-    16 pairs ran in 0.27 against 0.59 ms, config 4 in 4.0 against 4.7 ms). Each
+    measured on B200: a split of 64 pairs x 16,384 tokens never beat the serial 0.61 ms;
+    16 pairs ran in 0.224 ms against 0.594 serial and 0.237 for four equal segments,
+    32 pairs in 0.386 against 0.601 and 0.420 for two; config 4 in 4.0 against 4.7 ms
+    with tails in many rounds, a plan this model does not propose). Each
     pair's head segment of L0 tokens runs from the true initial state (one chain,
     output final); its tail is cut into s segments of Ls tokens that run as A and B
     chains (2 s chains per pair) on the SMs the heads leave free, composed by
     ``seg_scan`` and fixed up by ``seg_fix``. Modelled time: max(head chain, rounds of
     tail chains, each round with a CTA start-up) plus the fix-up's bytes and a fixed
-    cost. Returns (L0, s, Ls)."""
+    cost; by default every tail chain must start in the first round (plans with a
+    second round measured slower at 32 pairs: 0.459 against 0.386 ms). Returns
+    (L0, s, Ls)."""
     nchunks = T // CHUNK
     plain_us = nchunks * serial_chunk_us
     free = sms - pairs
