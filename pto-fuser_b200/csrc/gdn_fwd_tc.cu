@@ -1112,38 +1112,61 @@ struct KdaPrepParams {
   float* egl;
   int nc, T;
 };
-// 256 threads: thread (j, d) handles dimension d of tokens 16 j .. 16 j + 15 (all its
-// loads independent), the four token groups joined by a prefix over shared memory.
+// 4 DK threads: thread (j, d2) handles the dimension pair 2 d2, 2 d2 + 1 of the 8
+// tokens 8 j .. 8 j + 7 (4-byte loads and stores; every load of q, k and g is issued
+// before the prefix), the 8 token groups joined by a prefix over shared memory.
 template <int DK>
 __global__ void __launch_bounds__(4 * DK) kda_prep_kernel(const __grid_constant__ KdaPrepParams P) {
-  __shared__ float part[4][DK];
-  const int d = threadIdx.x % DK, j = threadIdx.x / DK;
+  constexpr int ND = DK / 2;          // dimension pairs
+  constexpr int NG = 4 * DK / ND;     // token groups
+  constexpr int TPG = kC / NG;        // tokens per group
+  static_assert(NG * TPG == kC, "token groups");
+  __shared__ float2 part[NG][ND];
+  const int d2 = threadIdx.x % ND, j = threadIdx.x / ND;
   const int bh = blockIdx.x / P.nc, c = blockIdx.x % P.nc;
-  const int64_t base =
-      (static_cast<int64_t>(bh) * P.T + static_cast<int64_t>(c) * kC + 16 * j) * DK + d;
-  float gl[16];
+  const int64_t row0 =
+      static_cast<int64_t>(bh) * P.T + static_cast<int64_t>(c) * kC + TPG * j;
+  const int64_t base = row0 * ND + d2;   // in dimension pairs
+  const float2* g2 = reinterpret_cast<const float2*>(P.g) + base;
+  const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(P.k) + base;
+  const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(P.q) + base;
+  float2 gl[TPG];
+  __nv_bfloat162 kk[TPG], qq[TPG];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) gl[i] = P.g[base + static_cast<int64_t>(i) * DK];
-#pragma unroll
-  for (int i = 1; i < 16; ++i) gl[i] += gl[i - 1];
-  part[j][d] = gl[15];
-  __syncthreads();
-  float off = 0.f;
-  for (int jj = 0; jj < j; ++jj) off += part[jj][d];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int64_t e = base + static_cast<int64_t>(i) * DK;
-    const float G = gl[i] + off;
-    const float up = __expf(G), dn = __expf(-G);
-    const float kk = __bfloat162float(P.k[e]), qq = __bfloat162float(P.q[e]);
-    P.k1[e] = __float2bfloat16_rn(kk * up);
-    P.q1[e] = __float2bfloat16_rn(qq * up);
-    P.k2[e] = __float2bfloat16_rn(kk * dn);
+  for (int i = 0; i < TPG; ++i) {
+    gl[i] = g2[i * ND];
+    kk[i] = k2[i * ND];
+    qq[i] = q2[i * ND];
   }
-  if (j == 3) {
-    float* eg = P.egl + static_cast<int64_t>(bh) * (P.nc + 1) * DK;
-    eg[static_cast<int64_t>(c + 1) * DK + d] = __expf(gl[15] + off);
-    if (c == 0) eg[d] = 1.f;
+#pragma unroll
+  for (int i = 1; i < TPG; ++i) {
+    gl[i].x += gl[i - 1].x;
+    gl[i].y += gl[i - 1].y;
+  }
+  part[j][d2] = gl[TPG - 1];
+  __syncthreads();
+  float2 off = make_float2(0.f, 0.f);
+  for (int jj = 0; jj < j; ++jj) {
+    off.x += part[jj][d2].x;
+    off.y += part[jj][d2].y;
+  }
+  __nv_bfloat162* k1o = reinterpret_cast<__nv_bfloat162*>(P.k1) + base;
+  __nv_bfloat162* q1o = reinterpret_cast<__nv_bfloat162*>(P.q1) + base;
+  __nv_bfloat162* k2o = reinterpret_cast<__nv_bfloat162*>(P.k2) + base;
+#pragma unroll
+  for (int i = 0; i < TPG; ++i) {
+    const float Gx = gl[i].x + off.x, Gy = gl[i].y + off.y;
+    const float ux = __expf(Gx), uy = __expf(Gy), dx = __expf(-Gx), dy = __expf(-Gy);
+    const float2 kf = __bfloat1622float2(kk[i]), qf = __bfloat1622float2(qq[i]);
+    k1o[i * ND] = __floats2bfloat162_rn(kf.x * ux, kf.y * uy);
+    q1o[i * ND] = __floats2bfloat162_rn(qf.x * ux, qf.y * uy);
+    k2o[i * ND] = __floats2bfloat162_rn(kf.x * dx, kf.y * dy);
+  }
+  if (j == NG - 1) {
+    float2* eg = reinterpret_cast<float2*>(P.egl + static_cast<int64_t>(bh) * (P.nc + 1) * DK);
+    eg[static_cast<int64_t>(c + 1) * ND + d2] =
+        make_float2(__expf(gl[TPG - 1].x + off.x), __expf(gl[TPG - 1].y + off.y));
+    if (c == 0) eg[d2] = make_float2(1.f, 1.f);
   }
 }
 
