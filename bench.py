@@ -469,7 +469,12 @@ def run_configs(args):
                           "roofline_frac_hbm": algo / (ms / 1e3) / 1e9 / hbm,
                           "peak_gbs": hbm}), flush=True)
 
+    def want(name):
+        return not args.only or name in args.only
+
     def fwd(name, desc, B, H, T, D, dt, mu=2.0, gate="raw", s0_std=None):
+        if not want(name):
+            return
         q, k, v, beta, g = inputs(B, H, T, D, dt, mu, gate != "none")
         S0 = (torch.randn(B, H, D, D, device=dev, generator=gen) * s0_std) if s0_std else None
         r = GDNChunkForward(B, H, T, D, D, in_dtype=dt, gate=gate)
@@ -484,62 +489,64 @@ def run_configs(args):
         r.close()
 
     fwd("cfg0", "GDN forward fp32 B1 H4 T512 D128 (SIMT fp32 path)", 1, 4, 512, 128, torch.float32)
-    # cfg1: kkt + inverse alone
-    B, H, T, D = 8, 32, 8192, 128
-    _, k, _, beta, g = inputs(B, H, T, D, torch.bfloat16)
-    out = torch.empty(B, H, T // 64, 64, 64, device=dev)
-    ws = nv.lib().ptof_ws_setup()
-    ms = timed(lambda: nv.check(nv.lib().ptof_kkt_inv_exec(
-        ws, k.data_ptr(), beta.data_ptr(), g.data_ptr(), out.data_ptr(), B, H, T, D, nv.BF16,
-        nv.BF16, nv.GATE_RAW, nv.LAYOUT_BHTD, nv.stream_handle())), args.steps)
-    nv.check(nv.lib().ptof_check_status(ws, nv.stream_handle()))
-    nv.lib().ptof_ws_teardown(ws)
-    M = B * H * (T // 64)
-    line("cfg1", "kkt + tri-inv B8 H32 T8192 D128 bf16 -> fp32 T", ms, B * T,
-         M * (64 * D * 2 + 64 * 2 + 64 * 4 + 64 * 64 * 4), "bf16")
-    del k, beta, g, out
+    if want("cfg1"):   # kkt + inverse alone
+        B, H, T, D = 8, 32, 8192, 128
+        _, k, _, beta, g = inputs(B, H, T, D, torch.bfloat16)
+        out = torch.empty(B, H, T // 64, 64, 64, device=dev)
+        ws = nv.lib().ptof_ws_setup()
+        ms = timed(lambda: nv.check(nv.lib().ptof_kkt_inv_exec(
+            ws, k.data_ptr(), beta.data_ptr(), g.data_ptr(), out.data_ptr(), B, H, T, D,
+            nv.BF16, nv.BF16, nv.GATE_RAW, nv.LAYOUT_BHTD, nv.stream_handle())), args.steps)
+        nv.check(nv.lib().ptof_check_status(ws, nv.stream_handle()))
+        nv.lib().ptof_ws_teardown(ws)
+        M = B * H * (T // 64)
+        line("cfg1", "kkt + tri-inv B8 H32 T8192 D128 bf16 -> fp32 T", ms, B * T,
+             M * (64 * D * 2 + 64 * 2 + 64 * 4 + 64 * 64 * 4), "bf16")
+        del k, beta, g, out
     fwd("cfg2", "GDN forward bf16 B4 H32 T16384 D128", 4, 32, 16384, 128, torch.bfloat16)
     fwd("cfg3", "DeltaNet (g = 0) bf16 B16 H16 T4096 D64", 16, 16, 4096, 64, torch.bfloat16,
         gate="none")
     fwd("cfg4", "long-context GDN bf16 B1 H64 T131072 D128, S0 ~ N(0,0.02^2), mu 3", 1, 64,
         131072, 128, torch.bfloat16, mu=3.0, s0_std=0.02)
 
-    # config 4 through the head/tail split inside the GPU (segment.GDNLocalSplit): 64
-    # pairs leave 84 SMs idle in the serial forward; the plan is the measured best of
-    # a sweep (a 80,896-token head, 7 tail segments of 7,168 tokens)
-    from pto_fuser.segment import GDNLocalSplit
-    B, H, T, D = 1, 64, 131072, 128
-    q, k, v, beta, g = inputs(B, H, T, D, torch.bfloat16, 3.0, True)
-    S0 = torch.randn(H, D, D, device=dev, generator=gen) * 0.02
-    sp = GDNLocalSplit(H, T, D, 80896, 7, 7168, device=dev)
-    o = torch.empty(H, T, D, device=dev, dtype=torch.bfloat16)
-    ms = timed(lambda: sp(q[0], k[0], v[0], beta[0], g[0], S0, o=o), args.steps)
-    sp.check_status()
-    line("cfg4-split", "long-context GDN B1 H64 T131072 D128, S0, head/tail split in one GPU",
-         ms, B * T, B * H * T * 1030 + B * H * D * D * 4 * 2, "bfloat16")
-    sp.close()
-    del q, k, v, beta, g, o
+    if want("cfg4-split"):
+        # config 4 through the head/tail split inside the GPU (segment.GDNLocalSplit): 64
+        # pairs leave 84 SMs idle in the serial forward; the plan is the measured best of
+        # a sweep (a 80,896-token head, 7 tail segments of 7,168 tokens)
+        from pto_fuser.segment import GDNLocalSplit
+        B, H, T, D = 1, 64, 131072, 128
+        q, k, v, beta, g = inputs(B, H, T, D, torch.bfloat16, 3.0, True)
+        S0 = torch.randn(H, D, D, device=dev, generator=gen) * 0.02
+        sp = GDNLocalSplit(H, T, D, 80896, 7, 7168, device=dev)
+        o = torch.empty(H, T, D, device=dev, dtype=torch.bfloat16)
+        ms = timed(lambda: sp(q[0], k[0], v[0], beta[0], g[0], S0, o=o), args.steps)
+        sp.check_status()
+        line("cfg4-split", "long-context GDN B1 H64 T131072 D128, S0, head/tail split in one GPU",
+             ms, B * T, B * H * T * 1030 + B * H * D * D * 4 * 2, "bfloat16")
+        sp.close()
+        del q, k, v, beta, g, o
 
-    # KDA (per-dimension gate; the reference's next family): the fused tensor-core
-    # forward at config 3's shape, g = -U(0,1) * 0.05 per token and dimension
-    from pto_fuser import KDAChunkForward
-    B, H, T, D = 16, 16, 4096, 64
-    q = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).bfloat16()
-    k = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).bfloat16()
-    v = torch.randn(B, H, T, D, device=dev, generator=gen).bfloat16()
-    beta = torch.sigmoid(torch.randn(B, H, T, device=dev, generator=gen)).bfloat16()
-    g = -torch.rand(B, H, T, D, device=dev, generator=gen) * 0.05
-    r = KDAChunkForward(B, H, T, D)
-    o = torch.empty_like(v)
-    S = torch.empty(B, H, D, D, device=dev)
-    ms = timed(lambda: r(q, k, v, beta, g, o=o, final_state=S), args.steps)
-    r.check_status()
-    # algorithmic bytes: q, k, v, o bf16, beta bf16, g fp32 per (token, dimension),
-    # plus the final state (the operand pre-pass's own traffic is not algorithmic)
-    algo = B * H * T * (4 * D * 2 + 2 + 4 * D) + B * H * D * D * 4
-    line("kda", "KDA forward bf16 B16 H16 T4096 D64 (fused tcgen05, operand pre-pass)", ms,
-         B * T, algo, "bfloat16")
-    r.close()
+    if want("kda"):
+        # KDA (per-dimension gate; the reference's next family): the fused tensor-core
+        # forward at config 3's shape, g = -U(0,1) * 0.05 per token and dimension
+        from pto_fuser import KDAChunkForward
+        B, H, T, D = 16, 16, 4096, 64
+        q = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).bfloat16()
+        k = nrm(torch.randn(B, H, T, D, device=dev, generator=gen), dim=-1).bfloat16()
+        v = torch.randn(B, H, T, D, device=dev, generator=gen).bfloat16()
+        beta = torch.sigmoid(torch.randn(B, H, T, device=dev, generator=gen)).bfloat16()
+        g = -torch.rand(B, H, T, D, device=dev, generator=gen) * 0.05
+        r = KDAChunkForward(B, H, T, D)
+        o = torch.empty_like(v)
+        S = torch.empty(B, H, D, D, device=dev)
+        ms = timed(lambda: r(q, k, v, beta, g, o=o, final_state=S), args.steps)
+        r.check_status()
+        # algorithmic bytes: q, k, v, o bf16, beta bf16, g fp32 per (token, dimension),
+        # plus the final state (the operand pre-pass's own traffic is not algorithmic)
+        algo = B * H * T * (4 * D * 2 + 2 + 4 * D) + B * H * D * D * 4
+        line("kda", "KDA forward bf16 B16 H16 T4096 D64 (fused tcgen05, operand pre-pass)", ms,
+             B * T, algo, "bfloat16")
+        r.close()
 
 
 def run_long(args):
@@ -645,6 +652,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--configs", action="store_true",
                     help="one supporting JSON line per BASELINE configuration (0-4), 1 GPU")
+    ap.add_argument("--only", nargs="+", metavar="NAME",
+                    help="with --configs: only these lines (cfg0 cfg1 cfg2 cfg3 cfg4 cfg4-split "
+                         "kda), e.g. for a launch list of one configuration")
     ap.add_argument("--shape", type=int, nargs=4, metavar=("B", "H", "T", "D"),
                     help="per-GPU problem other than config 2 (small cases for profiling; "
                          "not a bench line of the headline metric)")
