@@ -3,7 +3,7 @@
 // The full-precision path (fp32 inputs, reference tolerance 1e-4): every
 // contraction accumulates in fp32 FMA on the CUDA cores (value-column products in
 // register tiles of four columns), the (I+A)^-1 solve is a forward substitution
-// row by row with every column (and four partial sums of each) in parallel, the
+// per column (a warp per eight columns, shuffles only, no block barrier), the
 // per-token exponentials are computed once per chunk, and the state S[Dk, BV] of one
 // (batch, head, value-block) stays resident in shared memory across all chunks.
 // It restates, step for step, gdn_reference (examples/attention/_gdn_full.py:57-97):
@@ -88,6 +88,14 @@ __global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
   const float* gp = a.g ? a.g + b * a.sg.b + h * a.sg.h : nullptr;
   const int64_t sbase = static_cast<int64_t>(bh) * Dk * a.Dv;
 
+  // K and Q rows are read as float4 up to the next multiple of 4: zero that tail once
+  // (the chunk loads below write columns d < Dk only)
+  const int dk4 = (Dk + 3) / 4;
+  for (int idx = tid; idx < kC * (4 * dk4 - Dk); idx += kThreads) {
+    const int i = idx / (4 * dk4 - Dk), d = Dk + idx % (4 * dk4 - Dk);
+    s.K[i * ldk + d] = 0.f;
+    s.Q[i * ldk + d] = 0.f;
+  }
   // initial state
   for (int idx = tid; idx < Dk * kBV; idx += kThreads) {
     const int d = idx / kBV, j = idx % kBV;
@@ -145,44 +153,93 @@ __global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
     }
 
     // ---- A (strictly lower, gated) and Aqk (causal, gated) ----------------
-    for (int idx = tid; idx < kC * kC; idx += kThreads) {
-      const int i = idx / kC, j = idx % kC;
-      float akk = 0.f, aqk = 0.f;
-      if (j <= i) {
-        float dk = 0.f, dq = 0.f;
-        for (int d = 0; d < Dk; ++d) {
-          const float kj = s.K[j * ldk + d];
-          dk = fmaf(s.K[i * ldk + d], kj, dk);
-          dq = fmaf(s.Q[i * ldk + d], kj, dq);
+    // Register tiles: thread (ti, tj) owns rows ti + 16 r and columns tj + 16 c
+    // (r, c < 4) of both products and walks d four at a time; the 16 column rows a
+    // warp reads are consecutive, so its float4 loads of K rows are conflict-free
+    // (rows 4 apart would put 8 lanes on one bank with the 132-float row pitch).
+    {
+      const int ti = tid >> 4, tj = tid & 15;
+      float ak[4][4], aq[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ak[r][c] = aq[r][c] = 0.f;
+#pragma unroll 2
+      for (int d = 0; d < 4 * dk4; d += 4) {
+        float4 ki[4], qi[4], kj[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          ki[r] = *reinterpret_cast<const float4*>(&s.K[(ti + 16 * r) * ldk + d]);
+          qi[r] = *reinterpret_cast<const float4*>(&s.Q[(ti + 16 * r) * ldk + d]);
+          kj[r] = *reinterpret_cast<const float4*>(&s.K[(tj + 16 * r) * ldk + d]);
         }
-        const float x = s.g[i] - s.g[j];
-        if (j < i) akk = dk * (x <= 0.f ? expf(x) : 0.f) * s.beta[i];
-        aqk = dq * expf(fminf(x, 0.f));
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float x = ak[r][c], y = aq[r][c];
+            x = fmaf(ki[r].x, kj[c].x, x); y = fmaf(qi[r].x, kj[c].x, y);
+            x = fmaf(ki[r].y, kj[c].y, x); y = fmaf(qi[r].y, kj[c].y, y);
+            x = fmaf(ki[r].z, kj[c].z, x); y = fmaf(qi[r].z, kj[c].z, y);
+            x = fmaf(ki[r].w, kj[c].w, x); y = fmaf(qi[r].w, kj[c].w, y);
+            ak[r][c] = x;
+            aq[r][c] = y;
+          }
       }
-      s.A[i * ldc + j] = akk;
-      s.Aqk[i * ldc + j] = aqk;
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int i = ti + 16 * r, j = tj + 16 * c;
+          float akk = 0.f, aqk = 0.f;
+          if (j <= i) {
+            const float x = s.g[i] - s.g[j];
+            if (j < i) akk = ak[r][c] * (x <= 0.f ? expf(x) : 0.f) * s.beta[i];
+            aqk = aq[r][c] * expf(fminf(x, 0.f));
+          }
+          s.A[i * ldc + j] = akk;
+          s.Aqk[i * ldc + j] = aqk;
+        }
     }
     __syncthreads();
 
-    // ---- T = (I + A)^-1 by forward substitution, one row at a time:
-    //      T[i][j] = -sum_{j <= k < i} A[i][k] T[k][j]  (j < i), T[i][i] = 1.
-    //      Thread (j, part) = (tid / 4, tid % 4) sums every fourth k of column j; the
-    //      four partial sums meet by shuffles (same summation for every row) ----
+    // ---- T = (I + A)^-1: column j of T solves (I + A) x = e_j, and the 64 columns
+    //      are independent. Warp w owns columns w + 8 m (m < 8), lane l rows l and
+    //      l + 32 of each; a right-looking forward substitution walks k = 0..63: x_k is
+    //      final once every row above it has been applied, is broadcast by a shuffle,
+    //      and every row takes x_i -= A[i][k] x_k (A is strictly lower, so rows i <= k
+    //      take zero). No block barrier inside the solve. ----
     {
-      const int j = tid >> 2, part = tid & 3;
-      for (int i = 0; i < kC; ++i) {
-        float acc = 0.f;
-        for (int kk = j + part; kk < i; kk += 4) acc = fmaf(s.A[i * ldc + kk], s.Tm[kk * ldc + j], acc);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        if (part == 0) s.Tm[i * ldc + j] = (j < i) ? -acc : (j == i ? 1.f : 0.f);
-        __syncthreads();
+      const int w = tid >> 5, l = tid & 31;
+      constexpr int kCols = kC / (kThreads / 32);   // columns per warp
+      float x0[kCols], x1[kCols];
+#pragma unroll
+      for (int m = 0; m < kCols; ++m) {
+        const int j = w + 8 * m;
+        x0[m] = (l == j) ? 1.f : 0.f;
+        x1[m] = (l + 32 == j) ? 1.f : 0.f;
+      }
+#pragma unroll 2
+      for (int k = 0; k < kC; ++k) {
+        const float a0 = s.A[l * ldc + k], a1 = s.A[(l + 32) * ldc + k];
+#pragma unroll
+        for (int m = 0; m < kCols; ++m) {
+          const float xk = __shfl_sync(0xffffffffu, k < 32 ? x0[m] : x1[m], k & 31);
+          x0[m] = fmaf(-a0, xk, x0[m]);
+          x1[m] = fmaf(-a1, xk, x1[m]);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < kCols; ++m) {
+        const int j = w + 8 * m;
+        s.Tm[l * ldc + j] = x0[m];
+        s.Tm[(l + 32) * ldc + j] = x1[m];
       }
     }
+    __syncthreads();
 
     // ---- W = T (k * beta * exp(g)),  U = T (v * beta) ----------------------
     // (register tiles of 4 consecutive columns: one float4 shared load per 4 FMAs)
-    const int dk4 = (Dk + 3) / 4;
     for (int idx = tid; idx < kC * dk4; idx += kThreads) {
       const int i = idx / dk4, d = (idx % dk4) * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
