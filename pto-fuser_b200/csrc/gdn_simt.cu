@@ -157,6 +157,8 @@ __global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
     // (r, c < 4) of both products and walks d four at a time; the 16 column rows a
     // warp reads are consecutive, so its float4 loads of K rows are conflict-free
     // (rows 4 apart would put 8 lanes on one bank with the 132-float row pitch).
+    // Column block c > row block r lies wholly above the diagonal (j - i >= 1), so
+    // those 6 of the 16 tiles are skipped.
     {
       const int ti = tid >> 4, tj = tid & 15;
       float ak[4][4], aq[4][4];
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c <= r; ++c) {
             float x = ak[r][c], y = aq[r][c];
             x = fmaf(ki[r].x, kj[c].x, x); y = fmaf(qi[r].x, kj[c].x, y);
             x = fmaf(ki[r].y, kj[c].y, x); y = fmaf(qi[r].y, kj[c].y, y);
@@ -239,87 +241,129 @@ __global__ void __launch_bounds__(kThreads) gdn_fwd_simt_kernel(Args a) {
     __syncthreads();
 
     // ---- W = T (k * beta * exp(g)),  U = T (v * beta) ----------------------
-    // (register tiles of 4 consecutive columns: one float4 shared load per 4 FMAs)
-    for (int idx = tid; idx < kC * dk4; idx += kThreads) {
+    // Every product below gives a thread rows i and i + 32 (or four state rows) of
+    // one 4-column group: several independent accumulator chains per thread, one
+    // float4 shared load of the shared operand feeding both rows. T, Aqk are zero
+    // above the diagonal, so both rows run the longer row's j range; each output
+    // element sums its terms in the same order as a plain row loop.
+    for (int idx = tid; idx < (kC / 2) * dk4; idx += kThreads) {
       const int i = idx / dk4, d = (idx % dk4) * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int j = 0; j <= i; ++j) {
-        const float t = s.Tm[i * ldc + j] * s.wk[j];
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll 4
+      for (int j = 0; j <= i + kC / 2; ++j) {
+        const float wj = s.wk[j];
+        const float t0 = s.Tm[i * ldc + j] * wj, t1 = s.Tm[(i + kC / 2) * ldc + j] * wj;
         const float4 kv = *reinterpret_cast<const float4*>(&s.K[j * ldk + d]);
-        acc.x = fmaf(t, kv.x, acc.x); acc.y = fmaf(t, kv.y, acc.y);
-        acc.z = fmaf(t, kv.z, acc.z); acc.w = fmaf(t, kv.w, acc.w);
+        a0.x = fmaf(t0, kv.x, a0.x); a0.y = fmaf(t0, kv.y, a0.y);
+        a0.z = fmaf(t0, kv.z, a0.z); a0.w = fmaf(t0, kv.w, a0.w);
+        a1.x = fmaf(t1, kv.x, a1.x); a1.y = fmaf(t1, kv.y, a1.y);
+        a1.z = fmaf(t1, kv.z, a1.z); a1.w = fmaf(t1, kv.w, a1.w);
       }
-      *reinterpret_cast<float4*>(&s.W[i * ldk + d]) = acc;
+      *reinterpret_cast<float4*>(&s.W[i * ldk + d]) = a0;
+      *reinterpret_cast<float4*>(&s.W[(i + kC / 2) * ldk + d]) = a1;
     }
-    for (int idx = tid; idx < kC * (kBV / 4); idx += kThreads) {
-      const int i = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int j = 0; j <= i; ++j) {
-        const float t = s.Tm[i * ldc + j] * s.beta[j];
-        const float4 vv = *reinterpret_cast<const float4*>(&s.V[j * ldv + jv]);
-        acc.x = fmaf(t, vv.x, acc.x); acc.y = fmaf(t, vv.y, acc.y);
-        acc.z = fmaf(t, vv.z, acc.z); acc.w = fmaf(t, vv.w, acc.w);
+    static_assert((kC / 2) * (kBV / 4) == kThreads, "one row pair and column group per thread");
+    const int pi = tid / (kBV / 4), pj = (tid % (kBV / 4)) * 4;   // rows pi, pi + 32
+    {
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll 4
+      for (int j = 0; j <= pi + kC / 2; ++j) {
+        const float bj = s.beta[j];
+        const float t0 = s.Tm[pi * ldc + j] * bj, t1 = s.Tm[(pi + kC / 2) * ldc + j] * bj;
+        const float4 vv = *reinterpret_cast<const float4*>(&s.V[j * ldv + pj]);
+        a0.x = fmaf(t0, vv.x, a0.x); a0.y = fmaf(t0, vv.y, a0.y);
+        a0.z = fmaf(t0, vv.z, a0.z); a0.w = fmaf(t0, vv.w, a0.w);
+        a1.x = fmaf(t1, vv.x, a1.x); a1.y = fmaf(t1, vv.y, a1.y);
+        a1.z = fmaf(t1, vv.z, a1.z); a1.w = fmaf(t1, vv.w, a1.w);
       }
-      *reinterpret_cast<float4*>(&s.U[i * ldv + jv]) = acc;
+      *reinterpret_cast<float4*>(&s.U[pi * ldv + pj]) = a0;
+      *reinterpret_cast<float4*>(&s.U[(pi + kC / 2) * ldv + pj]) = a1;
     }
     __syncthreads();
 
     // ---- v_new = U - W S --------------------------------------------------
-    for (int idx = tid; idx < kC * (kBV / 4); idx += kThreads) {
-      const int i = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    {
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll 4
       for (int d = 0; d < Dk; ++d) {
-        const float w = s.W[i * ldk + d];
-        const float4 sv = *reinterpret_cast<const float4*>(&s.S[d * ldv + jv]);
-        acc.x = fmaf(w, sv.x, acc.x); acc.y = fmaf(w, sv.y, acc.y);
-        acc.z = fmaf(w, sv.z, acc.z); acc.w = fmaf(w, sv.w, acc.w);
+        const float w0 = s.W[pi * ldk + d], w1 = s.W[(pi + kC / 2) * ldk + d];
+        const float4 sv = *reinterpret_cast<const float4*>(&s.S[d * ldv + pj]);
+        a0.x = fmaf(w0, sv.x, a0.x); a0.y = fmaf(w0, sv.y, a0.y);
+        a0.z = fmaf(w0, sv.z, a0.z); a0.w = fmaf(w0, sv.w, a0.w);
+        a1.x = fmaf(w1, sv.x, a1.x); a1.y = fmaf(w1, sv.y, a1.y);
+        a1.z = fmaf(w1, sv.z, a1.z); a1.w = fmaf(w1, sv.w, a1.w);
       }
-      const float4 u = *reinterpret_cast<const float4*>(&s.U[i * ldv + jv]);
-      *reinterpret_cast<float4*>(&s.Vn[i * ldv + jv]) =
-          make_float4(u.x - acc.x, u.y - acc.y, u.z - acc.z, u.w - acc.w);
+      const float4 u0 = *reinterpret_cast<const float4*>(&s.U[pi * ldv + pj]);
+      const float4 u1 = *reinterpret_cast<const float4*>(&s.U[(pi + kC / 2) * ldv + pj]);
+      *reinterpret_cast<float4*>(&s.Vn[pi * ldv + pj]) =
+          make_float4(u0.x - a0.x, u0.y - a0.y, u0.z - a0.z, u0.w - a0.w);
+      *reinterpret_cast<float4*>(&s.Vn[(pi + kC / 2) * ldv + pj]) =
+          make_float4(u1.x - a1.x, u1.y - a1.y, u1.z - a1.z, u1.w - a1.w);
     }
     __syncthreads();
 
     // ---- o = scale * ((q S) * exp(g) + Aqk v_new) -------------------------
-    for (int idx = tid; idx < kC * (kBV / 4); idx += kThreads) {
-      const int i = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
-      float qs[4] = {0.f, 0.f, 0.f, 0.f}, in[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      float qs[2][4] = {}, in[2][4] = {};
+#pragma unroll 4
       for (int d = 0; d < Dk; ++d) {
-        const float qd = s.Q[i * ldk + d];
-        const float4 sv = *reinterpret_cast<const float4*>(&s.S[d * ldv + jv]);
-        qs[0] = fmaf(qd, sv.x, qs[0]); qs[1] = fmaf(qd, sv.y, qs[1]);
-        qs[2] = fmaf(qd, sv.z, qs[2]); qs[3] = fmaf(qd, sv.w, qs[3]);
+        const float q0 = s.Q[pi * ldk + d], q1 = s.Q[(pi + kC / 2) * ldk + d];
+        const float4 sv = *reinterpret_cast<const float4*>(&s.S[d * ldv + pj]);
+        qs[0][0] = fmaf(q0, sv.x, qs[0][0]); qs[0][1] = fmaf(q0, sv.y, qs[0][1]);
+        qs[0][2] = fmaf(q0, sv.z, qs[0][2]); qs[0][3] = fmaf(q0, sv.w, qs[0][3]);
+        qs[1][0] = fmaf(q1, sv.x, qs[1][0]); qs[1][1] = fmaf(q1, sv.y, qs[1][1]);
+        qs[1][2] = fmaf(q1, sv.z, qs[1][2]); qs[1][3] = fmaf(q1, sv.w, qs[1][3]);
       }
-      for (int j = 0; j <= i; ++j) {
-        const float aq = s.Aqk[i * ldc + j];
-        const float4 vn = *reinterpret_cast<const float4*>(&s.Vn[j * ldv + jv]);
-        in[0] = fmaf(aq, vn.x, in[0]); in[1] = fmaf(aq, vn.y, in[1]);
-        in[2] = fmaf(aq, vn.z, in[2]); in[3] = fmaf(aq, vn.w, in[3]);
+#pragma unroll 4
+      for (int j = 0; j <= pi + kC / 2; ++j) {
+        const float aq0 = s.Aqk[pi * ldc + j], aq1 = s.Aqk[(pi + kC / 2) * ldc + j];
+        const float4 vn = *reinterpret_cast<const float4*>(&s.Vn[j * ldv + pj]);
+        in[0][0] = fmaf(aq0, vn.x, in[0][0]); in[0][1] = fmaf(aq0, vn.y, in[0][1]);
+        in[0][2] = fmaf(aq0, vn.z, in[0][2]); in[0][3] = fmaf(aq0, vn.w, in[0][3]);
+        in[1][0] = fmaf(aq1, vn.x, in[1][0]); in[1][1] = fmaf(aq1, vn.y, in[1][1]);
+        in[1][2] = fmaf(aq1, vn.z, in[1][2]); in[1][3] = fmaf(aq1, vn.w, in[1][3]);
       }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float ov = a.scale * (qs[e] * s.eg[i] + in[e]);
-        if (jv + e < nv) op[static_cast<int64_t>(t0 + i) * a.sv.t + jv + e] = from_f32<TO>(ov);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int i = pi + h2 * (kC / 2);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float ov = a.scale * (qs[h2][e] * s.eg[i] + in[h2][e]);
+          if (pj + e < nv) op[static_cast<int64_t>(t0 + i) * a.sv.t + pj + e] = from_f32<TO>(ov);
+        }
       }
     }
     __syncthreads();
 
     // ---- S = exp(g_last) S + k^T (v_new * exp(g_last - g)) ----------------
-    const float gl = s.g[kC - 1];
-    const float egl = expf(gl);
-    for (int idx = tid; idx < Dk * (kBV / 4); idx += kThreads) {
-      const int d = idx / (kBV / 4), jv = (idx % (kBV / 4)) * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // thread: state rows d0 + 32 m (m < 4) of one 4-column group
+    {
+      const float egl = expf(s.g[kC - 1]);
+      const int d0 = tid / (kBV / 4), jv = (tid % (kBV / 4)) * 4;
+      float4 acc[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
       for (int i = 0; i < kC; ++i) {
-        const float kg = s.K[i * ldk + d] * s.gam[i];
+        const float gm = s.gam[i];
         const float4 vn = *reinterpret_cast<const float4*>(&s.Vn[i * ldv + jv]);
-        acc.x = fmaf(kg, vn.x, acc.x); acc.y = fmaf(kg, vn.y, acc.y);
-        acc.z = fmaf(kg, vn.z, acc.z); acc.w = fmaf(kg, vn.w, acc.w);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const float kg = s.K[i * ldk + d0 + 32 * m] * gm;
+          acc[m].x = fmaf(kg, vn.x, acc[m].x); acc[m].y = fmaf(kg, vn.y, acc[m].y);
+          acc[m].z = fmaf(kg, vn.z, acc[m].z); acc[m].w = fmaf(kg, vn.w, acc[m].w);
+        }
       }
-      float4* sp = reinterpret_cast<float4*>(&s.S[d * ldv + jv]);
-      const float4 o = *sp;
-      *sp = make_float4(fmaf(egl, o.x, acc.x), fmaf(egl, o.y, acc.y), fmaf(egl, o.z, acc.z),
-                        fmaf(egl, o.w, acc.w));
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int d = d0 + 32 * m;
+        if (d < Dk) {
+          float4* sp = reinterpret_cast<float4*>(&s.S[d * ldv + jv]);
+          const float4 o = *sp;
+          *sp = make_float4(fmaf(egl, o.x, acc[m].x), fmaf(egl, o.y, acc[m].y),
+                            fmaf(egl, o.z, acc[m].z), fmaf(egl, o.w, acc[m].w));
+        }
+      }
     }
   }
   __syncthreads();
