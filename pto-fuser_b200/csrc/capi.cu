@@ -201,11 +201,15 @@ void* ptof_gdn_fwd_setup(const ptof_gdn_params* p) {
   }
   if (validate_gdn(*p) != PTOF_OK) return nullptr;
   Workspace* w = ws_create(kWsGdnFwd, p);
-  if (w && p->in_dtype != PTOF_F32 && gdn_fwd_tc_supports(*p)) {
-    w->scratch_bytes = gdn_fwd_tc_scratch_bytes(*p);
+  if (!w) return nullptr;
+  // tensor-core path: per-chunk coefficient records; fp32 path: the two-phase
+  // kernels' per-chunk records when they apply (else nothing)
+  const bool tc = p->in_dtype != PTOF_F32 && gdn_fwd_tc_supports(*p);
+  w->scratch_bytes = tc ? gdn_fwd_tc_scratch_bytes(*p) : gdn_fwd_simt_split_bytes(*p);
+  if (w->scratch_bytes) {
     const cudaError_t e = cudaMalloc(&w->d_scratch, w->scratch_bytes);
     if (e != cudaSuccess) {
-      cuda_fail(e, "gdn_fwd coefficient buffer");
+      cuda_fail(e, "gdn_fwd workspace buffer");
       ws_destroy(w);
       return nullptr;
     }
@@ -226,7 +230,11 @@ int ptof_gdn_fwd_exec(void* wsv, const void* q, const void* k, const void* v, co
   if (p.in_dtype == PTOF_F32 || !gdn_fwd_tc_supports(p)) {
     if (!gdn_fwd_simt_supports(p))
       return fail(PTOF_EUNSUPPORTED, "no kernel for Dk=%d Dv=%d", p.Dk, p.Dv);
-    e = launch_gdn_fwd_simt(p, q, k, v, beta, g, S0, o, S_final, st);
+    const size_t split = gdn_fwd_simt_split_bytes(p);
+    if (split && w->d_scratch && w->scratch_bytes >= split)
+      e = launch_gdn_fwd_simt_split(p, q, k, v, beta, g, S0, o, S_final, w->d_scratch, st);
+    else
+      e = launch_gdn_fwd_simt(p, q, k, v, beta, g, S0, o, S_final, st);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_fwd_simt launch");
     return PTOF_OK;
   }

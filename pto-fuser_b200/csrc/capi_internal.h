@@ -59,6 +59,13 @@ cudaError_t launch_gdn_fwd_simt(const ptof_gdn_params& p, const void* q, const v
                                 const void* v, const void* beta, const float* g,
                                 const float* S0, void* o, float* S_final, cudaStream_t stream);
 bool gdn_fwd_simt_supports(const ptof_gdn_params& p);
+// Two-phase fp32 path (gdn_simt_split.cu): its per-chunk record bytes for these
+// params, 0 when it does not apply (then the single-kernel path runs).
+size_t gdn_fwd_simt_split_bytes(const ptof_gdn_params& p);
+cudaError_t launch_gdn_fwd_simt_split(const ptof_gdn_params& p, const void* q, const void* k,
+                                      const void* v, const void* beta, const float* g,
+                                      const float* S0, void* o, float* S_final, void* scratch,
+                                      cudaStream_t stream);
 bool gdn_fwd_tc_supports(const ptof_gdn_params& p);
 // bytes of the per-chunk coefficient records the tensor-core forward keeps in the
 // workspace (allocated by ptof_gdn_fwd_setup)

@@ -1,0 +1,488 @@
+// Two-phase fp32 SIMT forward of Gated DeltaNet (fp32 inputs, reference tolerance 1e-4).
+//
+// Everything of a chunk that does not depend on the state (the chunk-local cumsum of
+// g, the gated kk^T and qk^T, T = (I + A)^-1, W = T (k beta e^g) and T beta) runs
+// first for every (pair, chunk) at once, one CTA each, and lands in a per-chunk record
+// in the workspace. The recurrence then walks the chunks per (pair, 16 value columns):
+//   U = (T beta) v,  v_new = U - W S,  o = scale ((q S) e^g + Aqk v_new),
+//   S = e^{g_last} S + k^T (v_new e^{g_last - g})
+// which is gdn_reference (examples/attention/_gdn_full.py:57-97) split at the state,
+// as the single-kernel path in gdn_simt.cu restates it in one pass. The chain kernel
+// prefetches the next chunk's operands with cp.async into buffers that are already
+// dead (W, T beta, v and the double-buffered k and coefficients after v_new; q and
+// Aqk after the output), so their loads overlap the current chunk's products.
+//
+// Applies to fp32 q, k, v with Dk a multiple of 4 (<= 128) and Dv a multiple of 16;
+// other shapes and types use the single-kernel path.
+#include <cuda_runtime.h>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace ptof {
+namespace simt2 {
+
+constexpr int kThreads = 256;
+constexpr int kC = kChunk;    // 64
+constexpr int kMaxDk = 128;
+constexpr int kBV = 16;       // value columns per chain CTA
+
+// per-chunk record (floats); every offset a multiple of 4 (16-byte copies)
+constexpr int R_W = 0;                      // W [64][128] (row pitch 128)
+constexpr int R_TB = R_W + kC * kMaxDk;     // T beta [64][64]
+constexpr int R_AQK = R_TB + kC * kC;       // gated causal qk^T [64][64]
+constexpr int R_EG = R_AQK + kC * kC;       // e^{g_i}
+constexpr int R_GAM = R_EG + kC;            // e^{g_last - g_i}
+constexpr int R_EGL = R_GAM + kC;           // e^{g_last} (+ 3 pad)
+constexpr int R_FLOATS = R_EGL + 4;
+static_assert(R_FLOATS % 4 == 0, "record pitch");
+constexpr int R_COEF = R_EG;                // the coefficient block: eg, gam, egl
+constexpr int R_COEF_FLOATS = R_FLOATS - R_EG;
+
+struct PrepArgs {
+  const float* q;
+  const float* k;
+  const void* beta;
+  const float* g;
+  float* rec;
+  int H, T, Dk, gate_mode;
+  Strides4 sq;
+  Strides3 sg;
+};
+
+struct ChainArgs {
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* rec;
+  const float* S0;
+  void* o;
+  float* S_final;
+  int H, T, Dk, Dv;
+  float scale;
+  Strides4 sq, sv;
+};
+
+// ------------------------------------------------------------------ prep ----
+struct __align__(16) PrepSmem {
+  static constexpr int kLdK = kMaxDk + 4, kLdC = kC + 1;
+  float K[kC * kLdK];
+  float Q[kC * kLdK];
+  float A[kC * kLdC];
+  float Tm[kC * kLdC];
+  float g[kC];
+  float beta[kC];
+  float wk[kC];
+};
+
+template <typename TB>
+__global__ void __launch_bounds__(kThreads) simt_prep_kernel(PrepArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  PrepSmem& s = *reinterpret_cast<PrepSmem*>(smem_raw);
+  constexpr int ldk = PrepSmem::kLdK, ldc = PrepSmem::kLdC;
+  const int tid = threadIdx.x;
+  const int nc = a.T / kC;
+  const int bh = blockIdx.x / nc, c = blockIdx.x % nc;
+  const int b = bh / a.H, h = bh % a.H;
+  const int t0 = c * kC;
+  const int Dk = a.Dk, dk4 = Dk / 4;
+  const float* qp = a.q + b * a.sq.b + h * a.sq.h;
+  const float* kp = a.k + b * a.sq.b + h * a.sq.h;
+  const TB* bp = static_cast<const TB*>(a.beta) + b * a.sg.b + h * a.sg.h;
+  const float* gp = a.g ? a.g + b * a.sg.b + h * a.sg.h : nullptr;
+  float* rec = a.rec + static_cast<int64_t>(blockIdx.x) * R_FLOATS;
+
+  for (int idx = tid; idx < kC * dk4; idx += kThreads) {
+    const int i = idx / dk4, d = (idx % dk4) * 4;
+    const int64_t off = static_cast<int64_t>(t0 + i) * a.sq.t + d;
+    *reinterpret_cast<float4*>(&s.K[i * ldk + d]) = *reinterpret_cast<const float4*>(kp + off);
+    *reinterpret_cast<float4*>(&s.Q[i * ldk + d]) = *reinterpret_cast<const float4*>(qp + off);
+  }
+  if (tid < 32) {
+    // chunk-local inclusive cumsum of g, two tokens per lane (_gdn_full.py:63)
+    float x0 = 0.f, x1 = 0.f;
+    if (a.gate_mode != PTOF_GATE_NONE) {
+      x0 = gp[static_cast<int64_t>(t0 + 2 * tid) * a.sg.t];
+      x1 = gp[static_cast<int64_t>(t0 + 2 * tid + 1) * a.sg.t];
+    }
+    if (a.gate_mode == PTOF_GATE_RAW) {
+      x1 += x0;
+      float run = x1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, run, o);
+        if (tid >= o) run += y;
+      }
+      const float excl = run - x1;
+      x0 += excl;
+      x1 = run;
+    }
+    s.g[2 * tid] = x0;
+    s.g[2 * tid + 1] = x1;
+    s.beta[2 * tid] = to_f32(bp[static_cast<int64_t>(t0 + 2 * tid) * a.sg.t]);
+    s.beta[2 * tid + 1] = to_f32(bp[static_cast<int64_t>(t0 + 2 * tid + 1) * a.sg.t]);
+  }
+  __syncthreads();
+  if (tid < kC) {
+    const float gi = s.g[tid], e = expf(gi);
+    s.wk[tid] = s.beta[tid] * e;
+    rec[R_EG + tid] = e;
+    rec[R_GAM + tid] = expf(s.g[kC - 1] - gi);
+    if (tid == 0) rec[R_EGL] = expf(s.g[kC - 1]);
+  }
+
+  // ---- A (strictly lower, gated) into shared memory, Aqk (causal, gated) into the
+  //      record: register tiles as in gdn_simt.cu (rows ti + 16 r, columns tj + 16 c,
+  //      tiles above the diagonal skipped) ----
+  {
+    const int ti = tid >> 4, tj = tid & 15;
+    float ak[4][4], aq[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) ak[r][cc] = aq[r][cc] = 0.f;
+#pragma unroll 2
+    for (int d = 0; d < Dk; d += 4) {
+      float4 ki[4], qi[4], kj[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        ki[r] = *reinterpret_cast<const float4*>(&s.K[(ti + 16 * r) * ldk + d]);
+        qi[r] = *reinterpret_cast<const float4*>(&s.Q[(ti + 16 * r) * ldk + d]);
+        kj[r] = *reinterpret_cast<const float4*>(&s.K[(tj + 16 * r) * ldk + d]);
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int cc = 0; cc <= r; ++cc) {
+          float x = ak[r][cc], y = aq[r][cc];
+          x = fmaf(ki[r].x, kj[cc].x, x); y = fmaf(qi[r].x, kj[cc].x, y);
+          x = fmaf(ki[r].y, kj[cc].y, x); y = fmaf(qi[r].y, kj[cc].y, y);
+          x = fmaf(ki[r].z, kj[cc].z, x); y = fmaf(qi[r].z, kj[cc].z, y);
+          x = fmaf(ki[r].w, kj[cc].w, x); y = fmaf(qi[r].w, kj[cc].w, y);
+          ak[r][cc] = x;
+          aq[r][cc] = y;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int i = ti + 16 * r, j = tj + 16 * cc;
+        float akk = 0.f, aqk = 0.f;
+        if (j <= i) {
+          const float x = s.g[i] - s.g[j];
+          if (j < i) akk = ak[r][cc] * (x <= 0.f ? expf(x) : 0.f) * s.beta[i];
+          aqk = aq[r][cc] * expf(fminf(x, 0.f));
+        }
+        s.A[i * ldc + j] = akk;
+        rec[R_AQK + i * kC + j] = aqk;
+      }
+  }
+  __syncthreads();
+
+  // ---- T = (I + A)^-1, one forward substitution per column (as in gdn_simt.cu) ----
+  {
+    const int w = tid >> 5, l = tid & 31;
+    constexpr int kCols = kC / (kThreads / 32);
+    float x0[kCols], x1[kCols];
+#pragma unroll
+    for (int m = 0; m < kCols; ++m) {
+      const int j = w + 8 * m;
+      x0[m] = (l == j) ? 1.f : 0.f;
+      x1[m] = (l + 32 == j) ? 1.f : 0.f;
+    }
+#pragma unroll 2
+    for (int k = 0; k < kC; ++k) {
+      const float a0 = s.A[l * ldc + k], a1 = s.A[(l + 32) * ldc + k];
+#pragma unroll
+      for (int m = 0; m < kCols; ++m) {
+        const float xk = __shfl_sync(0xffffffffu, k < 32 ? x0[m] : x1[m], k & 31);
+        x0[m] = fmaf(-a0, xk, x0[m]);
+        x1[m] = fmaf(-a1, xk, x1[m]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < kCols; ++m) {
+      const int j = w + 8 * m;
+      s.Tm[l * ldc + j] = x0[m];
+      s.Tm[(l + 32) * ldc + j] = x1[m];
+    }
+  }
+  __syncthreads();
+
+  // ---- T beta into the record; W = T (k beta e^g) into the record (row pairs) ----
+  for (int idx = tid; idx < kC * kC; idx += kThreads) {
+    const int i = idx / kC, j = idx % kC;
+    rec[R_TB + idx] = s.Tm[i * ldc + j] * s.beta[j];
+  }
+  for (int idx = tid; idx < (kC / 2) * dk4; idx += kThreads) {
+    const int i = idx / dk4, d = (idx % dk4) * 4;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll 4
+    for (int j = 0; j <= i + kC / 2; ++j) {
+      const float wj = s.wk[j];
+      const float t0 = s.Tm[i * ldc + j] * wj, t1 = s.Tm[(i + kC / 2) * ldc + j] * wj;
+      const float4 kv = *reinterpret_cast<const float4*>(&s.K[j * ldk + d]);
+      a0.x = fmaf(t0, kv.x, a0.x); a0.y = fmaf(t0, kv.y, a0.y);
+      a0.z = fmaf(t0, kv.z, a0.z); a0.w = fmaf(t0, kv.w, a0.w);
+      a1.x = fmaf(t1, kv.x, a1.x); a1.y = fmaf(t1, kv.y, a1.y);
+      a1.z = fmaf(t1, kv.z, a1.z); a1.w = fmaf(t1, kv.w, a1.w);
+    }
+    *reinterpret_cast<float4*>(&rec[R_W + i * kMaxDk + d]) = a0;
+    *reinterpret_cast<float4*>(&rec[R_W + (i + kC / 2) * kMaxDk + d]) = a1;
+  }
+}
+
+// ----------------------------------------------------------------- chain ----
+struct __align__(16) ChainSmem {
+  static constexpr int kLdK = kMaxDk + 4, kLdC = kC + 4, kLdV = kBV + 4;
+  float W[kC * kLdK];
+  float Q[kC * kLdK];
+  float K[2][kC * kLdK];
+  float Tb[kC * kLdC];
+  float Aqk[kC * kLdC];
+  float V[kC * kLdV];
+  float Vn[kC * kLdV];
+  float S[kMaxDk * kLdV];
+  float coef[2][R_COEF_FLOATS];
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// [rows][cols] fp32 (cols a multiple of 4) from global rows of pitch `gp` floats into
+// shared rows of pitch `sp`, 16 bytes per copy
+__device__ __forceinline__ void copy_rows(float* dst, int sp, const float* src, int64_t gp,
+                                          int rows, int cols, int tid) {
+  const int c4 = cols / 4;
+  for (int idx = tid; idx < rows * c4; idx += kThreads) {
+    const int r = idx / c4, cc = (idx % c4) * 4;
+    cp_async16(dst + r * sp + cc, src + r * gp + cc);
+  }
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(kThreads) simt_chain_kernel(ChainArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  ChainSmem& s = *reinterpret_cast<ChainSmem*>(smem_raw);
+  constexpr int ldk = ChainSmem::kLdK, ldc = ChainSmem::kLdC, ldv = ChainSmem::kLdV;
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x;
+  const int b = bh / a.H, h = bh % a.H;
+  const int v0 = blockIdx.y * kBV;
+  const int Dk = a.Dk, nc = a.T / kC;
+  const float* qp = a.q + b * a.sq.b + h * a.sq.h;
+  const float* kp = a.k + b * a.sq.b + h * a.sq.h;
+  const float* vp = a.v + b * a.sv.b + h * a.sv.h + v0;
+  TO* op = static_cast<TO*>(a.o) + b * a.sv.b + h * a.sv.h + v0;
+  const float* rec0 = a.rec + static_cast<int64_t>(bh) * nc * R_FLOATS;
+  const int64_t sbase = static_cast<int64_t>(bh) * Dk * a.Dv;
+
+  // operands of chunk c: W, T beta, v, k, coefficients (group 1); q, Aqk (group 2)
+  auto load_first = [&](int c) {
+    const float* rec = rec0 + static_cast<int64_t>(c) * R_FLOATS;
+    const int64_t t0 = static_cast<int64_t>(c) * kC;
+    copy_rows(s.W, ldk, rec + R_W, kMaxDk, kC, Dk, tid);
+    copy_rows(s.Tb, ldc, rec + R_TB, kC, kC, kC, tid);
+    copy_rows(s.V, ldv, vp + t0 * a.sv.t, a.sv.t, kC, kBV, tid);
+    copy_rows(s.K[c & 1], ldk, kp + t0 * a.sq.t, a.sq.t, kC, Dk, tid);
+    copy_rows(s.coef[c & 1], 0, rec + R_COEF, 0, 1, R_COEF_FLOATS, tid);
+    cp_async_commit();
+  };
+  auto load_second = [&](int c) {
+    const float* rec = rec0 + static_cast<int64_t>(c) * R_FLOATS;
+    const int64_t t0 = static_cast<int64_t>(c) * kC;
+    copy_rows(s.Q, ldk, qp + t0 * a.sq.t, a.sq.t, kC, Dk, tid);
+    copy_rows(s.Aqk, ldc, rec + R_AQK, kC, kC, kC, tid);
+    cp_async_commit();
+  };
+
+  if (nc > 0) {
+    load_first(0);
+    load_second(0);
+  }
+  for (int idx = tid; idx < Dk * kBV; idx += kThreads) {
+    const int d = idx / kBV, j = idx % kBV;
+    s.S[d * ldv + j] = a.S0 ? a.S0[sbase + static_cast<int64_t>(d) * a.Dv + v0 + j] : 0.f;
+  }
+
+  // thread tile of the token-row products: row pi, columns pj .. pj + 3
+  static_assert(kC * (kBV / 4) == kThreads, "one row and column group per thread");
+  const int pi = tid / (kBV / 4), pj = (tid % (kBV / 4)) * 4;
+  for (int c = 0; c < nc; ++c) {
+    cp_async_wait_all();
+    __syncthreads();
+    const float* cf = s.coef[c & 1];
+    const float* Kc = s.K[c & 1];
+
+    // ---- U = (T beta) v and v_new = U - W S --------------------------------
+    {
+      float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int j = 0; j <= pi; ++j) {
+        const float t = s.Tb[pi * ldc + j];
+        const float4 vv = *reinterpret_cast<const float4*>(&s.V[j * ldv + pj]);
+        u.x = fmaf(t, vv.x, u.x); u.y = fmaf(t, vv.y, u.y);
+        u.z = fmaf(t, vv.z, u.z); u.w = fmaf(t, vv.w, u.w);
+      }
+      float4 ws = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+      for (int d = 0; d < Dk; d += 4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(&s.W[pi * ldk + d]);
+        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 sv = *reinterpret_cast<const float4*>(&s.S[(d + e) * ldv + pj]);
+          ws.x = fmaf(wv[e], sv.x, ws.x); ws.y = fmaf(wv[e], sv.y, ws.y);
+          ws.z = fmaf(wv[e], sv.z, ws.z); ws.w = fmaf(wv[e], sv.w, ws.w);
+        }
+      }
+      *reinterpret_cast<float4*>(&s.Vn[pi * ldv + pj]) =
+          make_float4(u.x - ws.x, u.y - ws.y, u.z - ws.z, u.w - ws.w);
+    }
+    __syncthreads();
+    if (c + 1 < nc) load_first(c + 1);   // W, T beta, v are dead; k and coef are double-buffered
+
+    // ---- o = scale ((q S) e^g + Aqk v_new) ----------------------------------
+    {
+      float4 qs = make_float4(0.f, 0.f, 0.f, 0.f), in = qs;
+#pragma unroll 2
+      for (int d = 0; d < Dk; d += 4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(&s.Q[pi * ldk + d]);
+        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 sv = *reinterpret_cast<const float4*>(&s.S[(d + e) * ldv + pj]);
+          qs.x = fmaf(qv[e], sv.x, qs.x); qs.y = fmaf(qv[e], sv.y, qs.y);
+          qs.z = fmaf(qv[e], sv.z, qs.z); qs.w = fmaf(qv[e], sv.w, qs.w);
+        }
+      }
+#pragma unroll 4
+      for (int j = 0; j <= pi; ++j) {
+        const float aq = s.Aqk[pi * ldc + j];
+        const float4 vn = *reinterpret_cast<const float4*>(&s.Vn[j * ldv + pj]);
+        in.x = fmaf(aq, vn.x, in.x); in.y = fmaf(aq, vn.y, in.y);
+        in.z = fmaf(aq, vn.z, in.z); in.w = fmaf(aq, vn.w, in.w);
+      }
+      const float e = cf[R_EG - R_COEF + pi];
+      TO* orow = op + (static_cast<int64_t>(c) * kC + pi) * a.sv.t + pj;
+      orow[0] = from_f32<TO>(a.scale * (qs.x * e + in.x));
+      orow[1] = from_f32<TO>(a.scale * (qs.y * e + in.y));
+      orow[2] = from_f32<TO>(a.scale * (qs.z * e + in.z));
+      orow[3] = from_f32<TO>(a.scale * (qs.w * e + in.w));
+    }
+    __syncthreads();
+    if (c + 1 < nc) load_second(c + 1);   // q and Aqk are dead
+
+    // ---- S = e^{g_last} S + k^T (v_new e^{g_last - g}): rows d0, d0 + 64 ----
+    {
+      const float egl = cf[R_EGL - R_COEF];
+      const float* gam = cf + (R_GAM - R_COEF);
+      const int d0 = tid / (kBV / 4), jv = (tid % (kBV / 4)) * 4;
+      float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+#pragma unroll 4
+      for (int i = 0; i < kC; ++i) {
+        const float gm = gam[i];
+        const float4 vn = *reinterpret_cast<const float4*>(&s.Vn[i * ldv + jv]);
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          const float kg = Kc[i * ldk + d0 + 64 * m] * gm;
+          acc[m].x = fmaf(kg, vn.x, acc[m].x); acc[m].y = fmaf(kg, vn.y, acc[m].y);
+          acc[m].z = fmaf(kg, vn.z, acc[m].z); acc[m].w = fmaf(kg, vn.w, acc[m].w);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const int d = d0 + 64 * m;
+        if (d < Dk) {
+          float4* sp = reinterpret_cast<float4*>(&s.S[d * ldv + jv]);
+          const float4 o = *sp;
+          *sp = make_float4(fmaf(egl, o.x, acc[m].x), fmaf(egl, o.y, acc[m].y),
+                            fmaf(egl, o.z, acc[m].z), fmaf(egl, o.w, acc[m].w));
+        }
+      }
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (a.S_final) {
+    for (int idx = tid; idx < Dk * kBV; idx += kThreads) {
+      const int d = idx / kBV, j = idx % kBV;
+      a.S_final[sbase + static_cast<int64_t>(d) * a.Dv + v0 + j] = s.S[d * ldv + j];
+    }
+  }
+}
+
+template <typename TB>
+cudaError_t launch_prep(const PrepArgs& a, int blocks, cudaStream_t st) {
+  auto kern = simt_prep_kernel<TB>;
+  const int smem = static_cast<int>(sizeof(PrepSmem));
+  cudaError_t e = set_smem_once(kern, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<blocks, kThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename TO>
+cudaError_t launch_chain(const ChainArgs& a, int pairs, cudaStream_t st) {
+  auto kern = simt_chain_kernel<TO>;
+  const int smem = static_cast<int>(sizeof(ChainSmem));
+  cudaError_t e = set_smem_once(kern, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<dim3(pairs, a.Dv / kBV), kThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace simt2
+
+size_t gdn_fwd_simt_split_bytes(const ptof_gdn_params& p) {
+  constexpr size_t kCap = size_t(256) << 20;   // beyond this the single-kernel path runs
+  if (p.in_dtype != PTOF_F32 || p.C != kChunk || p.Dk < 4 || p.Dk > simt2::kMaxDk ||
+      p.Dk % 4 || p.Dv < simt2::kBV || p.Dv % simt2::kBV || p.T % kChunk)
+    return 0;
+  const size_t bytes = static_cast<size_t>(p.B) * p.H * (p.T / kChunk) * simt2::R_FLOATS * 4;
+  return bytes <= kCap ? bytes : 0;
+}
+
+cudaError_t launch_gdn_fwd_simt_split(const ptof_gdn_params& p, const void* q, const void* k,
+                                      const void* v, const void* beta, const float* g,
+                                      const float* S0, void* o, float* S_final, void* scratch,
+                                      cudaStream_t stream) {
+  const int nc = p.T / kChunk, pairs = p.B * p.H;
+  if (nc == 0) return cudaSuccess;
+  simt2::PrepArgs pa;
+  pa.q = static_cast<const float*>(q);
+  pa.k = static_cast<const float*>(k);
+  pa.beta = beta;
+  pa.g = g;
+  pa.rec = static_cast<float*>(scratch);
+  pa.H = p.H; pa.T = p.T; pa.Dk = p.Dk; pa.gate_mode = p.gate_mode;
+  pa.sq = make_strides4(p.layout, p.H, p.T, p.Dk);
+  pa.sg = make_strides3(p.layout, p.H, p.T);
+  cudaError_t e;
+  switch (p.beta_dtype) {
+    case PTOF_F32: e = simt2::launch_prep<float>(pa, pairs * nc, stream); break;
+    case PTOF_F16: e = simt2::launch_prep<__half>(pa, pairs * nc, stream); break;
+    default: e = simt2::launch_prep<__nv_bfloat16>(pa, pairs * nc, stream); break;
+  }
+  if (e != cudaSuccess) return e;
+  simt2::ChainArgs ca;
+  ca.q = pa.q; ca.k = pa.k; ca.v = static_cast<const float*>(v);
+  ca.rec = pa.rec; ca.S0 = S0; ca.o = o; ca.S_final = S_final;
+  ca.H = p.H; ca.T = p.T; ca.Dk = p.Dk; ca.Dv = p.Dv; ca.scale = p.scale;
+  ca.sq = pa.sq;
+  ca.sv = make_strides4(p.layout, p.H, p.T, p.Dv);
+  switch (p.out_dtype) {
+    case PTOF_F32: return simt2::launch_chain<float>(ca, pairs, stream);
+    case PTOF_F16: return simt2::launch_chain<__half>(ca, pairs, stream);
+    default: return simt2::launch_chain<__nv_bfloat16>(ca, pairs, stream);
+  }
+}
+
+}  // namespace ptof

@@ -59,6 +59,14 @@ def test_fp32_initial_state_and_dk_ne_dv():
     _run(1, 2, 256, 128, 64, torch.float32, 1e-4, s0=0.02, mu=3.0)
 
 
+@pytest.mark.parametrize("Dk,Dv", [(32, 48), (128, 16), (30, 40), (64, 20)])
+def test_fp32_two_phase_and_single_kernel_shapes(Dk, Dv):
+    """fp32 with Dk a multiple of 4 and Dv of 16 runs the two-phase kernels (per-chunk
+    prep for all chunks, then the chain per 16 value columns); other shapes the
+    single-kernel path. Both against the oracle at 1e-4, with an initial state."""
+    _run(2, 3, 192, Dk, Dv, torch.float32, 1e-4, s0=0.02)
+
+
 @pytest.mark.parametrize("D", [64, 128])
 def test_bf16_small(D):
     _run(2, 2, 256, D, D, torch.bfloat16, 1e-2)
