@@ -256,14 +256,23 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// [rows][cols] fp32 (cols a multiple of 4) from global rows of pitch `gp` floats into
-// shared rows of pitch `sp`, 16 bytes per copy
-__device__ __forceinline__ void copy_rows(float* dst, int sp, const float* src, int64_t gp,
-                                          int rows, int cols, int tid) {
-  const int c4 = cols / 4;
-  for (int idx = tid; idx < rows * c4; idx += kThreads) {
+// [ROWS][4 C4] fp32 from global rows of pitch `gp` floats into shared rows of pitch
+// SP, 16 bytes per copy (compile-time shape: the index split is shifts and masks)
+template <int ROWS, int C4, int SP>
+__device__ __forceinline__ void copy_rows(float* dst, const float* src, int64_t gp, int tid) {
+#pragma unroll 4
+  for (int idx = tid; idx < ROWS * C4; idx += kThreads) {
+    const int r = idx / C4, cc = (idx % C4) * 4;
+    cp_async16(dst + r * SP + cc, src + r * gp + cc);
+  }
+}
+// the same with a run-time row width (Dk other than 128)
+template <int ROWS, int SP>
+__device__ __forceinline__ void copy_rows_n(float* dst, const float* src, int64_t gp, int c4,
+                                            int tid) {
+  for (int idx = tid; idx < ROWS * c4; idx += kThreads) {
     const int r = idx / c4, cc = (idx % c4) * 4;
-    cp_async16(dst + r * sp + cc, src + r * gp + cc);
+    cp_async16(dst + r * SP + cc, src + r * gp + cc);
   }
 }
 
@@ -285,21 +294,26 @@ __global__ void __launch_bounds__(kThreads) simt_chain_kernel(ChainArgs a) {
   const int64_t sbase = static_cast<int64_t>(bh) * Dk * a.Dv;
 
   // operands of chunk c: W, T beta, v, k, coefficients (group 1); q, Aqk (group 2)
+  // rows of Dk floats (W, k, q)
+  auto copy_dk = [&](float* dst, const float* src, int64_t gp) {
+    if (Dk == kMaxDk) copy_rows<kC, kMaxDk / 4, ldk>(dst, src, gp, tid);
+    else copy_rows_n<kC, ldk>(dst, src, gp, Dk / 4, tid);
+  };
   auto load_first = [&](int c) {
     const float* rec = rec0 + static_cast<int64_t>(c) * R_FLOATS;
     const int64_t t0 = static_cast<int64_t>(c) * kC;
-    copy_rows(s.W, ldk, rec + R_W, kMaxDk, kC, Dk, tid);
-    copy_rows(s.Tb, ldc, rec + R_TB, kC, kC, kC, tid);
-    copy_rows(s.V, ldv, vp + t0 * a.sv.t, a.sv.t, kC, kBV, tid);
-    copy_rows(s.K[c & 1], ldk, kp + t0 * a.sq.t, a.sq.t, kC, Dk, tid);
-    copy_rows(s.coef[c & 1], 0, rec + R_COEF, 0, 1, R_COEF_FLOATS, tid);
+    copy_dk(s.W, rec + R_W, kMaxDk);
+    copy_rows<kC, kC / 4, ldc>(s.Tb, rec + R_TB, kC, tid);
+    copy_rows<kC, kBV / 4, ldv>(s.V, vp + t0 * a.sv.t, a.sv.t, tid);
+    copy_dk(s.K[c & 1], kp + t0 * a.sq.t, a.sq.t);
+    copy_rows<1, R_COEF_FLOATS / 4, 0>(s.coef[c & 1], rec + R_COEF, 0, tid);
     cp_async_commit();
   };
   auto load_second = [&](int c) {
     const float* rec = rec0 + static_cast<int64_t>(c) * R_FLOATS;
     const int64_t t0 = static_cast<int64_t>(c) * kC;
-    copy_rows(s.Q, ldk, qp + t0 * a.sq.t, a.sq.t, kC, Dk, tid);
-    copy_rows(s.Aqk, ldc, rec + R_AQK, kC, kC, kC, tid);
+    copy_dk(s.Q, qp + t0 * a.sq.t, a.sq.t);
+    copy_rows<kC, kC / 4, ldc>(s.Aqk, rec + R_AQK, kC, tid);
     cp_async_commit();
   };
 
