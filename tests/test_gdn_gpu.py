@@ -120,3 +120,26 @@ def test_tc_matches_fp32_simt():
     e_o = ((o_tc.float() - o_32).norm() / o_32.norm()).item()
     e_s = ((S_tc - S_32).norm() / S_32.norm()).item()
     assert e_o < 1e-2 and e_s < 1e-2, (e_o, e_s)
+
+
+def test_fp32_two_phase_deterministic_and_graph_replay():
+    """The two-phase fp32 path (prep kernel, then chain kernel, workspace records in
+    between) gives bit-identical results on repeated calls and inside a CUDA graph."""
+    from pto_fuser import GDNChunkForward, make_gdn_inputs
+    inp = make_gdn_inputs(1, 4, 512, 128, dtype=torch.float32, device="cuda", seed=11,
+                          s0_std=0.02)
+    a = (inp["q"], inp["k"], inp["v"], inp["beta"], inp["g"], inp["S0"])
+    r = GDNChunkForward(1, 4, 512, 128, 128, in_dtype=torch.float32)
+    o1, S1 = (t.clone() for t in r(*a))
+    o2, S2 = r(*a)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(S1, S2)
+    o_buf, S_buf = torch.empty_like(o1), torch.empty_like(S1)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        r(*a, o=o_buf, final_state=S_buf)
+    graph.replay()
+    torch.cuda.synchronize()
+    r.check_status()
+    assert torch.equal(o_buf, o1) and torch.equal(S_buf, S1)
+    r.close()
