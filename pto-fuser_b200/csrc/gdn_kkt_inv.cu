@@ -197,44 +197,39 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gdn_kkt_inv_kernel(const
         if (k + 1 < cnt) fetch(k + 1);
       }
       named_bar_sync(kAllBar, 128);   // gcum / beta of chunk k
-      // ---- KK^T row i = 16 w + l (M = 64 accumulator: lanes 32w .. 32w + 15) ----
+      // ---- KK^T row i = 16 w + (l & 15) (M = 64 accumulator: lanes 32w .. 32w + 15);
+      //      lanes 0-15 take columns 0-31 of their row, lanes 16-31 columns 32-63 ----
       wait(&bars[K_TFULL0 + bb], static_cast<uint32_t>((k >> 1) & 1), 10);
       tc_fence_after();
-      const int i = 16 * w + l;
+      const int i = 16 * w + (l & 15), jb = 32 * (l >> 4);
       const uint32_t tacc = tmem + bb * kC + ((32u * w) << 16);
       const bool fast = *fastp != 0;
-      const float gi = gcum[min(i, kC - 1)], bi = bsm[min(i, kC - 1)], rb = rowfb[min(i, kC - 1)];
-      // two 32-column halves (register budget of four CTAs per SM)
-#pragma unroll
-      for (int h0 = 0; h0 < kC; h0 += 32) {
+      const float gi = gcum[i], bi = bsm[i], rb = rowfb[i];
+      {
         float v[32];
-        tmem_ld16(tacc + h0, *reinterpret_cast<float(*)[16]>(v));
-        tmem_ld16(tacc + h0 + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+        tmem_ld16_split<32>(tacc, *reinterpret_cast<float(*)[16]>(v));
+        tmem_ld16_split<32>(tacc + 16, *reinterpret_cast<float(*)[16]>(v + 16));
         tmem_wait_ld();
-        if (h0 + 32 == kC) {
-          tc_fence_before();
-          __syncwarp();
-          if (l == 0) mbar_arrive(&bars[K_TFREE0 + bb]);
-        }
-        if (l < 16) {
+        tc_fence_before();
+        __syncwarp();
+        if (l == 0) mbar_arrive(&bars[K_TFREE0 + bb]);
 #pragma unroll
-          for (int j0 = 0; j0 < 32; j0 += 8) {
-            uint32_t pk[4];
+        for (int j0 = 0; j0 < 32; j0 += 8) {
+          uint32_t pk[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float a2[2];
+          for (int u = 0; u < 4; ++u) {
+            float a2[2];
 #pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int j = h0 + j0 + 2 * u + e;
-                const float cf = fast ? rb * colf[j] : bi * kkt_coef(gi, gcum[j]);
-                a2[e] = (j < i) ? v[j0 + 2 * u + e] * cf : 0.f;
-              }
-              pk[u] = pack_f16(a2[0], a2[1]);
+            for (int e = 0; e < 2; ++e) {
+              const int j = jb + j0 + 2 * u + e;
+              const float cf = fast ? rb * colf[j] : bi * kkt_coef(gi, gcum[j]);
+              a2[e] = (j < i) ? v[j0 + 2 * u + e] * cf : 0.f;
             }
-            const int jj = h0 + j0;
-            *reinterpret_cast<uint4*>(at + i * 128 + (((jj >> 3) ^ (i & 7)) << 4)) =
-                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            pk[u] = pack_f16(a2[0], a2[1]);
           }
+          const int jj = jb + j0;
+          *reinterpret_cast<uint4*>(at + i * 128 + (((jj >> 3) ^ (i & 7)) << 4)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
       named_bar_sync(kAllBar, 128);   // A complete
