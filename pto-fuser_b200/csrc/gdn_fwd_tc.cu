@@ -423,10 +423,23 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
         tmem_ld16(t_o + c0, x);
         tmem_wait_ld();
         if (v >= 0) {
+          if constexpr (Roles<DK>::OUT_GROUP) {
+            // the output group has registers to spare: vector loads of the multipliers
+            float sc[16];
 #pragma unroll
-          for (int m = 0; m < 16; ++m) {
-            *op = from_f32<TO>(x[m] * osc[c0 + m]);
-            op += P.os_t;
+            for (int m = 0; m < 16; m += 4)
+              *reinterpret_cast<float4*>(sc + m) = *reinterpret_cast<const float4*>(osc + c0 + m);
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+              *op = from_f32<TO>(x[m] * sc[m]);
+              op += P.os_t;
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+              *op = from_f32<TO>(x[m] * osc[c0 + m]);
+              op += P.os_t;
+            }
           }
         }
       }
@@ -734,10 +747,25 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
         tmem_ld16(t_kq + j0, v);
         tmem_wait_ld();
         if (fast) {
+          if constexpr (DK == 64) {
+            // D = 64: vector loads of the column factors (measured faster there; the
+            // D = 128 kernel measured slower with them and keeps the scalar loads)
+            float cl[16];
 #pragma unroll
-          for (int m = 0; m < 16; ++m) {
-            const float cf = is_k ? rowm * ms[L::M_COLF / 4 + j0 + m] : rowm;
-            v[m] = (j0 + m < lim) ? v[m] * cf : 0.f;
+            for (int m = 0; m < 16; m += 4)
+              *reinterpret_cast<float4*>(cl + m) =
+                  *reinterpret_cast<const float4*>(ms + L::M_COLF / 4 + j0 + m);
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+              const float cf = is_k ? rowm * cl[m] : rowm;
+              v[m] = (j0 + m < lim) ? v[m] * cf : 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 16; ++m) {
+              const float cf = is_k ? rowm * ms[L::M_COLF / 4 + j0 + m] : rowm;
+              v[m] = (j0 + m < lim) ? v[m] * cf : 0.f;
+            }
           }
         } else {
           // exact per-element coefficients: K rows beta_i * kkt_coef, Q rows qk_coef
@@ -865,13 +893,27 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
                 tv[2 * m + 1] = f.y * gi;
               }
             }
-            const float* bk = ms + L::M_BK / 4 + j0;
-            const float* bv = ms + L::M_BV / 4 + j0;
             uint32_t a[8], bb[8];
+            if constexpr (DK == 64) {   // vector loads at D = 64 only (as for the column factors)
+              float bk[16], bv[16];
 #pragma unroll
-            for (int m = 0; m < 8; ++m) {
-              a[m] = pack2<F16>(tv[2 * m] * bk[2 * m], tv[2 * m + 1] * bk[2 * m + 1]);
-              bb[m] = pack2<F16>(tv[2 * m] * bv[2 * m], tv[2 * m + 1] * bv[2 * m + 1]);
+              for (int m = 0; m < 16; m += 4) {
+                *reinterpret_cast<float4*>(bk + m) = *reinterpret_cast<const float4*>(ms + L::M_BK / 4 + j0 + m);
+                *reinterpret_cast<float4*>(bv + m) = *reinterpret_cast<const float4*>(ms + L::M_BV / 4 + j0 + m);
+              }
+#pragma unroll
+              for (int m = 0; m < 8; ++m) {
+                a[m] = pack2<F16>(tv[2 * m] * bk[2 * m], tv[2 * m + 1] * bk[2 * m + 1]);
+                bb[m] = pack2<F16>(tv[2 * m] * bv[2 * m], tv[2 * m + 1] * bv[2 * m + 1]);
+              }
+            } else {
+              const float* bk = ms + L::M_BK / 4 + j0;
+              const float* bv = ms + L::M_BV / 4 + j0;
+#pragma unroll
+              for (int m = 0; m < 8; ++m) {
+                a[m] = pack2<F16>(tv[2 * m] * bk[2 * m], tv[2 * m + 1] * bk[2 * m + 1]);
+                bb[m] = pack2<F16>(tv[2 * m] * bv[2 * m], tv[2 * m + 1] * bv[2 * m + 1]);
+              }
             }
             st_chunk(s_tp, i, j0 / 8, make_uint4(a[0], a[1], a[2], a[3]));
             st_chunk(s_tp, i, j0 / 8 + 1, make_uint4(a[4], a[5], a[6], a[7]));
