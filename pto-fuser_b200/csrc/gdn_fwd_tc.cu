@@ -829,18 +829,33 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
         tc_fence_after();
         if (qp == 0) trace_mark<TRACE>(P, cp, TR_PREP_WU);
         unsigned char* wt = sm + L::OFF_WT;
-        const int d = (DK == 128) ? 32 * q + l : (l < 16 ? 16 * q + l : -1);
+        if constexpr (DK == 128) {
+          const int d = 32 * q + l;
 #pragma unroll 1
-        for (int j0 = 0; j0 < kC; j0 += 16) {
-          float a0[16];
-          tmem_ld16(t_rw + j0, a0);
-          tmem_wait_ld();
-          if (d >= 0) {
+          for (int j0 = 0; j0 < kC; j0 += 16) {
+            float a0[16];
+            tmem_ld16(t_rw + j0, a0);
+            tmem_wait_ld();
             uint32_t pk[8];
 #pragma unroll
             for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
             st_chunk(wt, d, j0 / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
             st_chunk(wt, d, j0 / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
+          }
+        } else {
+          // M = 64 accumulator: lanes 0-15 read columns 0-31 of row 16q + l, lanes
+          // 16-31 columns 32-63 of row 16q + l - 16 (16x32bx2 loads)
+          const int d = 16 * q + (l & 15), jb = 32 * (l >> 4);
+#pragma unroll 1
+          for (int j0 = 0; j0 < 32; j0 += 16) {
+            float a0[16];
+            tmem_ld16_split<32>(t_rw + j0, a0);
+            tmem_wait_ld();
+            uint32_t pk[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) pk[m] = pack2<F16>(a0[2 * m], a0[2 * m + 1]);
+            st_chunk(wt, d, (jb + j0) / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+            st_chunk(wt, d, (jb + j0) / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
           }
         }
         tc_fence_before();
@@ -1056,25 +1071,27 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
         }
         tmem_wait_st();
       } else {
+        // M = 64 accumulator (lanes 32q .. 32q + 15): lanes 0-15 convert columns 0-31 of
+        // row 16q + l, lanes 16-31 columns 32-63 of row 16q + l - 16 (16x32bx2 loads)
+        const int vr = 16 * q + (l & 15), cb = 32 * (l >> 4);
 #pragma unroll 1
-        for (int c0 = 0; c0 < kC; c0 += 16) {
+        for (int c0 = 0; c0 < 32; c0 += 16) {
           float x[16];
-          tmem_ld16(t_vn + c0, x);
+          tmem_ld16_split<32>(t_vn + c0, x);
           tmem_wait_ld();
-          if (v >= 0) {
-            uint32_t a[8];
+          const int cc = cb + c0;
+          uint32_t a[8];
 #pragma unroll
-            for (int m = 0; m < 8; ++m) a[m] = pack2<F16>(x[2 * m], x[2 * m + 1]);
-            st_chunk(s_vnt, v, c0 / 8, make_uint4(a[0], a[1], a[2], a[3]));
-            st_chunk(s_vnt, v, c0 / 8 + 1, make_uint4(a[4], a[5], a[6], a[7]));
-            if (!fastc) {
-              uint32_t gq[8];
+          for (int m = 0; m < 8; ++m) a[m] = pack2<F16>(x[2 * m], x[2 * m + 1]);
+          st_chunk(s_vnt, vr, cc / 8, make_uint4(a[0], a[1], a[2], a[3]));
+          st_chunk(s_vnt, vr, cc / 8 + 1, make_uint4(a[4], a[5], a[6], a[7]));
+          if (!fastc) {
+            uint32_t gq[8];
 #pragma unroll
-              for (int m = 0; m < 8; ++m)
-                gq[m] = pack2<F16>(x[2 * m] * gam[c0 + 2 * m], x[2 * m + 1] * gam[c0 + 2 * m + 1]);
-              st_chunk(s_vng, v, c0 / 8, make_uint4(gq[0], gq[1], gq[2], gq[3]));
-              st_chunk(s_vng, v, c0 / 8 + 1, make_uint4(gq[4], gq[5], gq[6], gq[7]));
-            }
+            for (int m = 0; m < 8; ++m)
+              gq[m] = pack2<F16>(x[2 * m] * gam[cc + 2 * m], x[2 * m + 1] * gam[cc + 2 * m + 1]);
+            st_chunk(s_vng, vr, cc / 8, make_uint4(gq[0], gq[1], gq[2], gq[3]));
+            st_chunk(s_vng, vr, cc / 8 + 1, make_uint4(gq[4], gq[5], gq[6], gq[7]));
           }
         }
         fence_async_smem();
