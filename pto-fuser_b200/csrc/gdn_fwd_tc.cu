@@ -976,6 +976,46 @@ __global__ void __launch_bounds__(Roles<DK>::THREADS, 1) gdn_fwd_tc_kernel(const
     // KDA: `md` (per key dimension d) scales the state first: the per-dimension decay
     // of the chunk just completed, so S_{c+1} = e^{g_tot} (S_c + (K e^-g)^T V_new)
     auto state_pass = [&](bool from_global, float mult, float* final_out, const float* md) {
+      if constexpr (!L::SA_TMEM && DK == 64) {
+        // M = 64 master (lanes 32q .. 32q + 15): lanes 0-15 take key columns 0-31 of
+        // row 16q + l, lanes 16-31 columns 32-63 of row 16q + l - 16 (16x32bx2 shape)
+        const int vr = 16 * q + (l & 15), db = 32 * (l >> 4);
+        float x[32];
+        if (from_global) {
+#pragma unroll
+          for (int m = 0; m < 32; ++m)
+            x[m] = P.S0 ? P.S0[sbase + static_cast<int64_t>(db + m) * DV + vr] : 0.f;
+        } else {
+          tmem_ld16_split<32>(t_sm, *reinterpret_cast<float(*)[16]>(x));
+          tmem_ld16_split<32>(t_sm + 16, *reinterpret_cast<float(*)[16]>(x + 16));
+          tmem_wait_ld();
+        }
+        if constexpr (KDA) {
+          if (md != nullptr) {
+#pragma unroll
+            for (int m = 0; m < 32; ++m) x[m] *= md[db + m];
+          }
+        }
+        if (final_out) {
+#pragma unroll
+          for (int m = 0; m < 32; ++m) final_out[sbase + static_cast<int64_t>(db + m) * DV + vr] = x[m];
+          return;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) pk[m] = pack2<F16>(x[2 * m], x[2 * m + 1]);
+        st_chunk(s_sa, vr, db / 8, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+        st_chunk(s_sa, vr, db / 8 + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
+        st_chunk(s_sa, vr, db / 8 + 2, make_uint4(pk[8], pk[9], pk[10], pk[11]));
+        st_chunk(s_sa, vr, db / 8 + 3, make_uint4(pk[12], pk[13], pk[14], pk[15]));
+        float y0[16], y1[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) { y0[m] = x[m] * mult; y1[m] = x[16 + m] * mult; }
+        tmem_st16f_split<32>(t_sm, y0);
+        tmem_st16f_split<32>(t_sm + 16, y1);
+        tmem_wait_st();
+        return;
+      }
 #pragma unroll 1
       for (int d0 = 0; d0 < DK; d0 += 32) {
         float x[32];

@@ -320,6 +320,22 @@ __device__ __forceinline__ void tmem_st16f(uint32_t taddr, const float (&v)[16])
   tmem_st16(taddr, r);
 }
 
+// 16x32bx2 store, the counterpart of tmem_ld16_split (same lane / column mapping)
+template <int HALF>
+__device__ __forceinline__ void tmem_st16f_split(uint32_t taddr, const float (&v)[16]) {
+  uint32_t r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], %1, "
+      "{%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17};"
+      :
+      : "r"(taddr), "n"(HALF), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+        "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
+        "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 // --------------------------------------------------------------------------
 // Descriptors
 // --------------------------------------------------------------------------
