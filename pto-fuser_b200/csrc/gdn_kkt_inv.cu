@@ -8,8 +8,8 @@
 // Persistent CTAs, three per SM, each walking chunks m = blockIdx.x + k * gridDim.x:
 //   warp 4      one thread: TMA producer of K tiles (2-stage ring) and UMMA issuer of
 //               KK^T (M = N = 64, fp32 accumulators in two TMEM buffers)
-//   warps 0-3   gate cumsum and coefficients (warp 0, g and beta prefetched one chunk
-//               ahead), KK^T epilogue from TMEM -> fp16 A tile: beta_i e^{g_i - g_0}
+//   warps 0-3   gate cumsum and coefficients (warp 1 during the inverse of the previous
+//               chunk, g and beta prefetched one chunk ahead; two record buffers), KK^T epilogue from TMEM -> fp16 A tile: beta_i e^{g_i - g_0}
 //               e^{g_0 - g_j} for monotone chunks with total decay < 80, else the exact
 //               per-element safe_exp,
 //               (I + A)^-1 in place on warp-level MMAs, T -> fp32 staging tile ->
@@ -39,8 +39,10 @@ struct KLayout {
   static constexpr int OFF_A = kNS * STAGE;          // fp16 A -> T tile, 8 KB
   // fp32 gcum[64], beta[64], rowfb[64] = beta_i e^{g_i - g_0}, colf[64] = e^{g_0 - g_j},
   // then the chunk's fast-path flag
+  // (two buffers: the next chunk's are written during the inverse of the current one)
+  static constexpr int G_BYTES = 1024 + 16;
   static constexpr int OFF_G = OFF_A + kC * 128;
-  static constexpr int OFF_BAR = OFF_G + 1024 + 16;
+  static constexpr int OFF_BAR = OFF_G + 2 * G_BYTES;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
   static constexpr int TCOLS = 2 * kC;               // two fp32 64x64 accumulators
 };
@@ -140,12 +142,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gdn_kkt_inv_kernel(const
     // ============================ compute warps 0-3 ============================
     const int w = warp, l = lane;
     unsigned char* at = sm + L::OFF_A;
-    float* gcum = reinterpret_cast<float*>(sm + L::OFF_G);
-    float* bsm = gcum + kC;
-    float* rowfb = gcum + 2 * kC;
-    float* colf = gcum + 3 * kC;
-    int* fastp = reinterpret_cast<int*>(gcum + 4 * kC);
-    // warp 0: g and beta of a chunk, two tokens per lane (prefetched one chunk ahead)
+    // gate records of chunk k in buffer k & 1: gcum[64], beta[64], rowfb[64], colf[64], fast
+    auto gbuf = [&](int64_t k) { return reinterpret_cast<float*>(sm + L::OFF_G + (k & 1) * L::G_BYTES); };
+    // warp 1: g and beta of a chunk, two tokens per lane (prefetched one chunk ahead)
     float pg0 = 0.f, pg1 = 0.f, pb0 = 0.f, pb1 = 0.f;
     auto fetch = [&](int64_t k) {
       const int64_t m = chunk_of(k);
@@ -160,43 +159,54 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gdn_kkt_inv_kernel(const
       pb0 = ld_beta_any(P.beta, P.beta_dtype, i0);
       pb1 = ld_beta_any(P.beta, P.beta_dtype, i0 + P.gs_t);
     };
-    if (w == 0 && cnt > 0) fetch(0);
+    // the gate records of chunk k from the prefetched registers, then the prefetch of
+    // chunk k + 1 (whole warp 1)
+    auto gate = [&](int64_t k) {
+      float* gr = gbuf(k);
+      float g0 = pg0, g1 = pg1;
+      const float b0 = pb0, b1 = pb1;
+      bool mono = true;   // the chunk-local cumsum never increases
+      if (P.gate_mode == PTOF_GATE_RAW) {
+        mono = (g0 <= 0.f) && (g1 <= 0.f);
+        g1 += g0;
+        float run = g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, run, o);
+          if (l >= o) run += y;
+        }
+        g0 += run - g1;
+        g1 = run;
+      } else if (P.gate_mode == PTOF_GATE_CUMSUM) {
+        const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
+        mono = (g1 <= g0) && (l == 0 || g0 <= prev);
+      }
+      // exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j): overflow-free when the cumsum is
+      // monotone and the chunk's total decay is below 80; otherwise the exact form
+      const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
+      const float gl = __shfl_sync(0xffffffffu, g1, 31);
+      const bool fast = __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
+      reinterpret_cast<float2*>(gr)[l] = make_float2(g0, g1);
+      reinterpret_cast<float2*>(gr + kC)[l] = make_float2(b0, b1);
+      reinterpret_cast<float2*>(gr + 2 * kC)[l] =
+          make_float2(b0 * __expf(g0 - gfirst), b1 * __expf(g1 - gfirst));
+      reinterpret_cast<float2*>(gr + 3 * kC)[l] = make_float2(__expf(gfirst - g0), __expf(gfirst - g1));
+      if (l == 0) *reinterpret_cast<int*>(gr + 4 * kC) = fast ? 1 : 0;
+      if (k + 1 < cnt) fetch(k + 1);
+    };
+    if (w == 1 && cnt > 0) {
+      fetch(0);
+      gate(0);
+    }
+    named_bar_sync(kAllBar, 128);   // gate records of chunk 0
     for (int64_t k = 0; k < cnt; ++k) {
       const int bb = static_cast<int>(k & 1);
       const int64_t m = chunk_of(k);
-      if (w == 0) {
-        float g0 = pg0, g1 = pg1;
-        const float b0 = pb0, b1 = pb1;
-        bool mono = true;   // the chunk-local cumsum never increases
-        if (P.gate_mode == PTOF_GATE_RAW) {
-          mono = (g0 <= 0.f) && (g1 <= 0.f);
-          g1 += g0;
-          float run = g1;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, run, o);
-            if (l >= o) run += y;
-          }
-          g0 += run - g1;
-          g1 = run;
-        } else if (P.gate_mode == PTOF_GATE_CUMSUM) {
-          const float prev = __shfl_up_sync(0xffffffffu, g1, 1);
-          mono = (g1 <= g0) && (l == 0 || g0 <= prev);
-        }
-        // exp(g_i - g_j) = exp(g_i - g_0) exp(g_0 - g_j): overflow-free when the cumsum is
-        // monotone and the chunk's total decay is below 80; otherwise the exact form
-        const float gfirst = __shfl_sync(0xffffffffu, g0, 0);
-        const float gl = __shfl_sync(0xffffffffu, g1, 31);
-        const bool fast = __all_sync(0xffffffffu, mono) && (gfirst - gl < 80.f);
-        reinterpret_cast<float2*>(gcum)[l] = make_float2(g0, g1);
-        reinterpret_cast<float2*>(bsm)[l] = make_float2(b0, b1);
-        reinterpret_cast<float2*>(rowfb)[l] =
-            make_float2(b0 * __expf(g0 - gfirst), b1 * __expf(g1 - gfirst));
-        reinterpret_cast<float2*>(colf)[l] = make_float2(__expf(gfirst - g0), __expf(gfirst - g1));
-        if (l == 0) *fastp = fast ? 1 : 0;
-        if (k + 1 < cnt) fetch(k + 1);
-      }
-      named_bar_sync(kAllBar, 128);   // gcum / beta of chunk k
+      const float* gcum = gbuf(k);
+      const float* bsm = gcum + kC;
+      const float* rowfb = gcum + 2 * kC;
+      const float* colf = gcum + 3 * kC;
+      const int* fastp = reinterpret_cast<const int*>(gcum + 4 * kC);
       // ---- KK^T row i = 16 w + (l & 15) (M = 64 accumulator: lanes 32w .. 32w + 15);
       //      lanes 0-15 take columns 0-31 of their row, lanes 16-31 columns 32-63 ----
       wait(&bars[K_TFULL0 + bb], static_cast<uint32_t>((k >> 1) & 1), 10);
@@ -233,7 +243,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gdn_kkt_inv_kernel(const
         }
       }
       named_bar_sync(kAllBar, 128);   // A complete
-      tri_inv64_inplace(at, w, l, 2, kAllBar);
+      // warp 1 is idle during the inverse's 16 -> 32 level: it writes the next chunk's
+      // gate records into the other buffer (visible to all four warps after the level)
+      tri_inv64_inplace_idle(at, w, l, 2, kAllBar, [&] {
+        if (w == 1 && k + 1 < cnt) gate(k + 1);
+      });
       // ---- T (fp16 tile) -> fp32 rows of T in global memory: float4 f = tid + 128 it is
       //      row f / 16, columns 4 (f % 16) .. (each row 256 contiguous bytes) ----
       float4* tg = reinterpret_cast<float4*>(P.Tout + m * (kC * kC));
@@ -245,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gdn_kkt_inv_kernel(const
         const float2 lo = unpack_f16(u.x), hi = unpack_f16(u.y);
         tg[f] = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
-      named_bar_sync(kAllBar, 128);   // A tile and gcum free again
+      named_bar_sync(kAllBar, 128);   // A tile free again
     }
   }
   __syncthreads();

@@ -129,8 +129,12 @@ __device__ __forceinline__ void inv16_diag(const unsigned char* a_tile, unsigned
 // blocks must hold zeros), by four whole warps w = 0..3 of one CTA. Named barriers:
 // pair_bar and pair_bar + 1 (64 threads: warps 0-1, 2-3) and all_bar (128 threads).
 // On return every warp's stores of T are visible to the four warps.
-__device__ __forceinline__ void tri_inv64_inplace(unsigned char* tile, int w, int l, int pair_bar,
-                                                  int all_bar) {
+// `idle()` is called by the warps that the 16 -> 32 level leaves idle (w = 1 and 3)
+// before the barrier that ends that level; shared-memory writes it makes are visible to
+// the four warps on return.
+template <typename F>
+__device__ __forceinline__ void tri_inv64_inplace_idle(unsigned char* tile, int w, int l, int pair_bar,
+                                                       int all_bar, F&& idle) {
   // level 0 (warp w): T_bb = (I + N)^-1 of the diagonal block N = A_bb
   inv16_diag(tile, tile, 16 * w, l);
   // level 1 (warps 0, 2): T21 = -(T22 A21) T11 for the block pairs (0,1), (2,3)
@@ -150,6 +154,8 @@ __device__ __forceinline__ void tri_inv64_inplace(unsigned char* tile, int w, in
     mma_f16_16816(o1, za, bf[2], bf[3]);
     st_c(tile, r1, c1, l, o0, -1.f);
     st_c(tile, r1, c1 + 8, l, o1, -1.f);
+  } else {
+    idle();
   }
   // level 2: T[32:64, 0:32] = -(T_BB A_BA) T_AA; warp (rb, ch) owns rows
   // 32 + 16 rb .. +15 and columns 16 ch .. +15
@@ -186,6 +192,11 @@ __device__ __forceinline__ void tri_inv64_inplace(unsigned char* tile, int w, in
     st_c(tile, R, 16 * chh + 8, l, o1, -1.f);
   }
   named_bar_sync(all_bar, 128);
+}
+
+__device__ __forceinline__ void tri_inv64_inplace(unsigned char* tile, int w, int l, int pair_bar,
+                                                  int all_bar) {
+  tri_inv64_inplace_idle(tile, w, l, pair_bar, all_bar, [] {});
 }
 
 }  // namespace ptof
